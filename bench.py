@@ -1,0 +1,495 @@
+#!/usr/bin/env python
+"""Decode-step benchmark of the B200 KV-cache hot path.
+
+One step = for each of the 36 Qwen3-4B layers: append one new K/V token per
+sequence into the paged pool (kv_append) and run GQA-4 paged decode attention
+over the whole context (paged_decode).  Batch 256 per GPU, context lengths
+uniform in [512, 4096], block size 256, block pool sized to ~70% of HBM with a
+random block assignment, K/V ~ 0.5*N(0,1), Q ~ N(0,1) (synthetic data).
+
+N > 1 (torchrun): tensor parallelism over KV heads with weak scaling -- every
+rank holds Hkv/N KV heads (and 4x as many query heads) for a global batch of
+256*N sequences, so each rank streams the same bytes as one GPU at N=1; there is
+no collective inside the hot path (attention is head-local).  The timed region
+is bracketed by barrier + synchronize and the max over ranks is reported.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+"""
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decode tokens/sec and paged-attn HBM GB/s (% of 8 TB/s), Qwen3-4B, 1/2/4/8 B200"
+LAYERS, HQ, HKV, D, BS = 36, 32, 8, 128, 256
+BATCH_PER_GPU = 256
+CTX_LO, CTX_HI = 512, 4096
+POOL_FRAC = 0.70
+NOMINAL_HBM_GBS = 8000.0
+FALLBACK_HBM_GBS = 6650.0
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def measured_hbm_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+class Clocks:
+    """nvidia-smi sampling of SM clocks and throttle reasons during a region."""
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.proc = None
+        props = torch.cuda.get_device_properties(device)
+        bus = getattr(props, "pci_bus_id", None)
+        dom = getattr(props, "pci_domain_id", None)
+        dev = getattr(props, "pci_device_id", None)
+        self.sel = (f"{dom:08X}:{bus:02X}:{dev:02X}.0" if None not in (bus, dom, dev)
+                    else str(device.index or 0))
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", self.sel, f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        self.samples = []
+        if self.proc is None:
+            return False
+        time.sleep(0.2)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            out = ""
+        for line in out.strip().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 8:
+                self.samples.append(parts)
+        return False
+
+    def summary(self):
+        if not getattr(self, "samples", None):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm = [float(s[0]) for s in self.samples if s[0].replace(".", "").isdigit()]
+        mx = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for s in self.samples for n, v in zip(names, s[4:8])
+                          if v.lower() == "active"})
+        under = sorted(sm)[len(sm) // 2:] if sm else []
+        return {"sm_mhz": statistics.median(under) if under else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(self.samples)}
+
+
+# ----------------------------------------------------------------------------
+# workload
+# ----------------------------------------------------------------------------
+
+def make_metadata(n_gpus, seed=2, batch_per_gpu=BATCH_PER_GPU):
+    """Global batch metadata, identical on every rank (same generator)."""
+    gen = torch.Generator().manual_seed(seed)
+    B = batch_per_gpu * n_gpus
+    lens = torch.randint(CTX_LO, CTX_HI + 1, (B,), generator=gen, dtype=torch.int64)
+    pages = (lens + BS - 1) // BS
+    return B, lens.to(torch.int32), pages, gen
+
+
+def build_gpu_workload(args, rank, n, device):
+    hkv, hq = HKV // n, HQ // n
+    B, lens, pages, gen = make_metadata(n, batch_per_gpu=args.batch)
+    W = int(pages.max())
+    need = int(pages.sum())
+    block_bytes = 2 * args.layers * BS * hkv * D * 2
+    free, total = torch.cuda.mem_get_info(device)
+    if args.pool_blocks:
+        NB = args.pool_blocks
+    else:
+        NB = int(POOL_FRAC * total) // block_bytes
+        NB = min(NB, int((free - (6 << 30)) // block_bytes))
+    if NB < need:
+        raise SystemExit(f"pool of {NB} blocks cannot hold the {need} blocks of the batch")
+    perm = torch.randperm(NB, generator=gen)[:need].to(torch.int32)
+    tables = torch.full((B, W), -1, dtype=torch.int32)
+    cur = 0
+    for b in range(B):
+        p = int(pages[b])
+        tables[b, :p] = perm[cur:cur + p]
+        cur += p
+    last = (lens - 1).to(torch.int64)
+    slots = (tables[torch.arange(B), last // BS].to(torch.int64) * BS + last % BS).to(torch.int32)
+
+    log(f"[rank {rank}] pool {NB} blocks x {block_bytes / 2**20:.1f} MiB = "
+        f"{NB * block_bytes / 2**30:.1f} GiB ({NB * block_bytes / total:.0%} of HBM), "
+        f"batch {B}, Hkv {hkv}, layers {args.layers}")
+    kv = torch.empty(2, args.layers, NB, BS, hkv, D, dtype=torch.bfloat16, device=device)
+    g = torch.Generator(device=device).manual_seed(1234 + rank)
+    for i in range(2):
+        for l in range(args.layers):
+            kv[i, l].normal_(0.0, 0.5, generator=g)
+    q = torch.randn(args.layers, B, hq, D, device=device, generator=g).to(torch.bfloat16)
+    knew = (torch.randn(args.layers, B, hkv, D, device=device, generator=g) * 0.5).bfloat16()
+    vnew = (torch.randn(args.layers, B, hkv, D, device=device, generator=g) * 0.5).bfloat16()
+    out = torch.empty(args.layers, B, hq, D, dtype=torch.bfloat16, device=device)
+    return dict(B=B, hq=hq, hkv=hkv, NB=NB, W=W, lens_cpu=lens, tables_cpu=tables,
+                slots_cpu=slots, lens=lens.to(device), tables=tables.to(device),
+                slots=slots.to(device), kv=kv, q=q, knew=knew, vnew=vnew, out=out,
+                block_bytes=block_bytes)
+
+
+def decode_bytes(wl):
+    """Algorithmic HBM bytes of one paged_decode launch (one layer)."""
+    ctx = int(wl["lens_cpu"].to(torch.int64).sum())
+    pages = int(((wl["lens_cpu"].to(torch.int64) + BS - 1) // BS).sum())
+    kv = ctx * wl["hkv"] * D * 2 * 2
+    qo = wl["B"] * wl["hq"] * D * 2 * 2
+    meta = wl["B"] * 4 + pages * 4
+    return kv + qo + meta
+
+
+def append_bytes(wl):
+    """Algorithmic HBM bytes of one kv_append launch: read + write new K and V."""
+    return wl["B"] * wl["hkv"] * D * 2 * 2 * 2 + wl["B"] * 4
+
+
+# ----------------------------------------------------------------------------
+# our implementation
+# ----------------------------------------------------------------------------
+
+def run_ours(args):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    n = args.gpus
+    if world != n:
+        raise SystemExit(f"--gpus {n} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    dist = None
+    if n > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=device)
+    pkg = importlib.import_module("slo-aware-llm-serving-engine_b200")
+    pkg._lib.lib()
+
+    wl = build_gpu_workload(args, rank, n, device)
+    L, B = args.layers, wl["B"]
+    scale = D ** -0.5
+    kv = wl["kv"]
+
+    def step():
+        for l in range(L):
+            pkg.store_kvcache(wl["knew"][l], wl["vnew"][l], kv[0, l], kv[1, l], wl["slots"])
+            pkg.flash_attn_with_kvcache(wl["q"][l].unsqueeze(1), kv[0, l], kv[1, l],
+                                        cache_seqlens=wl["lens"], block_table=wl["tables"],
+                                        softmax_scale=scale, out=wl["out"][l].unsqueeze(1))
+
+    def decode_only():
+        for l in range(L):
+            pkg.flash_attn_with_kvcache(wl["q"][l].unsqueeze(1), kv[0, l], kv[1, l],
+                                        cache_seqlens=wl["lens"], block_table=wl["tables"],
+                                        softmax_scale=scale, out=wl["out"][l].unsqueeze(1))
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    step()                                   # eager pass: allocates the workspace
+    torch.cuda.synchronize()
+    if pkg.read_device_errors():
+        raise SystemExit("device error word set during warm-up")
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    dgraph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(dgraph):
+        decode_only()
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+
+    # ---- timed region: K decode steps ----
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = Clocks(device)
+    with clocks:
+        barrier()
+        torch.cuda.synchronize()
+        start.record()
+        for _ in range(args.steps):
+            graph.replay()
+        end.record()
+        torch.cuda.synchronize()
+        barrier()
+    ms = start.elapsed_time(end) / args.steps
+
+    # ---- kernel timing for the roofline: decode launches alone ----
+    reps = max(2, args.steps // 2)
+    dgraph.replay()
+    torch.cuda.synchronize()
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record()
+    for _ in range(reps):
+        dgraph.replay()
+    e2.record()
+    torch.cuda.synchronize()
+    dec_ms = s2.elapsed_time(e2) / (reps * L)
+    errs = pkg.read_device_errors()
+
+    # ---- end to end through the public API with host buffers ----
+    e2e = run_e2e(args, pkg, wl, device, barrier) if not args.no_e2e else None
+
+    t = torch.tensor([ms, dec_ms, e2e["ms"] if e2e else 0.0], device=device)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, dec_ms, e2e_ms = t.tolist()
+
+    if rank == 0:
+        peak, peak_kind = measured_hbm_peak()
+        dbytes = decode_bytes(wl)
+        abytes = append_bytes(wl)
+        step_bytes = L * (dbytes + abytes)
+        achieved = dbytes / (dec_ms * 1e-3) / 1e9
+        step_gbs = step_bytes / (ms * 1e-3) / 1e9
+        tok_s = B / (ms * 1e-3)
+        traffic = None
+        try:
+            with open(os.path.join(ROOT, "profiles", "paged_decode_traffic.json")) as f:
+                tr = json.load(f)
+            traffic = tr.get("dram_bytes_per_launch")
+        except Exception:
+            pass
+        line = {
+            "metric": METRIC, "value": round(tok_s, 1), "unit": "tok/s", "n_gpus": n,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: K/V ~ 0.5*N(0,1), Q ~ N(0,1), context ~ U[512,4096], random "
+                    "block assignment (seeded)",
+            "config": {
+                "workload": "BASELINE config 2: pure decode step, 36 layers of kv_append + "
+                            "GQA-4 paged decode, Qwen3-4B KV geometry",
+                "batch_per_gpu": args.batch, "global_batch": B, "layers": L,
+                "kv_heads_per_gpu": wl["hkv"], "q_heads_per_gpu": wl["hq"], "head_dim": D,
+                "block_size": BS, "context": f"U[{CTX_LO},{CTX_HI}]", "pool_blocks": wl["NB"],
+                "pool_gib": round(wl["NB"] * wl["block_bytes"] / 2 ** 30, 1),
+                "parallelism": f"tp{n} over KV heads (weak: global batch {args.batch}*N)",
+                "l2": "inputs larger than L2: %.2f GB of K/V read per layer" % (dbytes / 1e9),
+                "graph": "one CUDA graph per step (append + decode for every layer)"},
+            "hbm": {"step_gbs": round(step_gbs, 1),
+                    "frac_of_8tbs": round(step_gbs / NOMINAL_HBM_GBS, 4),
+                    "frac_of_measured": round(step_gbs / peak, 4),
+                    "step_bytes": step_bytes},
+            "roofline": {"kernel": "paged_decode (main + merge launch, one layer)",
+                         "bound": "hbm", "achieved": round(achieved, 1),
+                         "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "peak_kind": peak_kind, "frac_of_8tbs": round(achieved / NOMINAL_HBM_GBS, 4),
+                         "algorithmic_bytes": dbytes, "launch_ms": round(dec_ms, 5),
+                         "traffic": traffic},
+            "gpu_launches": args.steps * L * 3,
+            "clocks": clocks.summary(),
+            "device_errors": errs,
+        }
+        if e2e:
+            line["e2e"] = {"value": round(B / (e2e_ms * 1e-3), 1), "unit": "tok/s",
+                           "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"],
+                           "ms_per_step": round(e2e_ms, 3),
+                           "path": "Attention.forward + Context per layer (store_kvcache + "
+                                   "flash_attn_with_kvcache), pinned host buffers"}
+        if n == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(args, sample_seconds=args.cpu_seconds)
+        print(json.dumps(line), flush=True)
+    del graph, dgraph
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_e2e(args, pkg, wl, device, barrier):
+    """The same decode step driven through the public Attention/Context API from
+    pinned host buffers: per step the metadata and every layer's q/k/v go
+    host->device and every layer's attention output comes back device->host."""
+    L, B = args.layers, wl["B"]
+    attn = []
+    for l in range(L):
+        a = pkg.Attention(wl["hq"], D, D ** -0.5, wl["hkv"])
+        a.k_cache, a.v_cache = wl["kv"][0, l], wl["kv"][1, l]
+        attn.append(a)
+    h_q = wl["q"].cpu().pin_memory()
+    h_k = wl["knew"].cpu().pin_memory()
+    h_v = wl["vnew"].cpu().pin_memory()
+    h_out = torch.empty(wl["out"].shape, dtype=torch.bfloat16).pin_memory()
+    h_slots = wl["slots_cpu"].pin_memory()
+    h_lens = wl["lens_cpu"].pin_memory()
+    h_tables = wl["tables_cpu"].pin_memory()
+    h2d = (h_slots.numel() + h_lens.numel() + h_tables.numel()) * 4 + L * (
+        h_q[0].numel() + h_k[0].numel() + h_v[0].numel()) * 2
+    d2h = L * h_out[0].numel() * 2
+
+    def one_step():
+        slots = h_slots.to(device, non_blocking=True)
+        lens = h_lens.to(device, non_blocking=True)
+        tables = h_tables.to(device, non_blocking=True)
+        pkg.set_context(False, slot_mapping=slots, context_lens=lens, block_tables=tables)
+        for l in range(L):
+            q = h_q[l].to(device, non_blocking=True)
+            k = h_k[l].to(device, non_blocking=True)
+            v = h_v[l].to(device, non_blocking=True)
+            o = attn[l](q, k, v)
+            h_out[l].copy_(o.view(B, wl["hq"], D), non_blocking=True)
+        pkg.reset_context()
+
+    for _ in range(max(1, args.warmup)):
+        one_step()
+    torch.cuda.synchronize()
+    steps = max(2, args.steps // 2)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    s.record()
+    for _ in range(steps):
+        one_step()
+    e.record()
+    torch.cuda.synchronize()
+    barrier()
+    return {"ms": s.elapsed_time(e) / steps, "h2d": h2d, "d2h": d2h}
+
+
+# ----------------------------------------------------------------------------
+# CPU baseline: the oracle (restatement of the reference's torch path)
+# ----------------------------------------------------------------------------
+
+def _cpu_sample(batch=BATCH_PER_GPU, seed=2):
+    from oracle import kv_oracle as O  # test infrastructure: the timed CPU baseline only
+    B, lens, pages, gen = make_metadata(1, seed=seed, batch_per_gpu=batch)
+    need = int(pages.sum())
+    W = int(pages.max())
+    tables = torch.full((B, W), -1, dtype=torch.int32)
+    perm = torch.randperm(need, generator=gen).to(torch.int32)
+    cur = 0
+    for b in range(B):
+        p = int(pages[b])
+        tables[b, :p] = perm[cur:cur + p]
+        cur += p
+    kc = (torch.randn(need, BS, HKV, D, generator=gen) * 0.5).bfloat16()
+    vc = (torch.randn(need, BS, HKV, D, generator=gen) * 0.5).bfloat16()
+    q = torch.randn(B, HQ, D, generator=gen).bfloat16()
+    k = (torch.randn(B, HKV, D, generator=gen) * 0.5).bfloat16()
+    v = (torch.randn(B, HKV, D, generator=gen) * 0.5).bfloat16()
+    last = (lens - 1).to(torch.int64)
+    slots = (tables[torch.arange(B), last // BS].to(torch.int64) * BS + last % BS).to(torch.int32)
+
+    def layer():
+        O.store_kvcache(k, v, kc, vc, slots)
+        O.decode(q.unsqueeze(1), kc, vc, lens, tables, D ** -0.5)
+    return B, layer
+
+
+def cpu_baseline(args, sample_seconds=10.0):
+    torch.set_num_threads(os.cpu_count() or 1)
+    B, layer = _cpu_sample(batch=args.cpu_batch)
+    layer()                                      # warm-up
+    times = []
+    t_end = time.perf_counter() + sample_seconds
+    while time.perf_counter() < t_end or not times:
+        t0 = time.perf_counter()
+        layer()
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    return {"value": round(B / (LAYERS * t), 3), "unit": "tok/s",
+            "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{len(times)} x one layer (append + decode) of a {B}-sequence batch with "
+                      f"context U[{CTX_LO},{CTX_HI}], fp32 oracle arithmetic on bf16 K/V; "
+                      f"tok/s = batch / (36 x median layer time {t * 1e3:.1f} ms)"}
+
+
+def run_reference(args):
+    """--impl reference: the reference's torch path for the hot path, as restated
+    by the oracle, on the host cores (the reference has no CPU kernel of its own
+    to build).  Rank 0 only; other ranks exit without work."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    torch.set_num_threads(os.cpu_count() or 1)
+    B, layer = _cpu_sample(batch=args.cpu_batch)
+    for _ in range(args.warmup):
+        layer()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        layer()
+    t = (time.perf_counter() - t0) / args.steps
+    value = B / (LAYERS * t)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "tok/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(t * LAYERS * 1e3, 2), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded), as the GPU arm",
+        "config": {"workload": "BASELINE config 2 decode step (append + decode per layer), "
+                               "one layer timed per step and scaled to 36 layers",
+                   "batch": B, "layers": LAYERS, "context": f"U[{CTX_LO},{CTX_HI}]",
+                   "block_size": BS},
+        "cpu_baseline": {"value": round(value, 3), "unit": "tok/s",
+                         "cores": torch.get_num_threads(), "kind": "port",
+                         "sample": f"one layer of a {B}-sequence batch per step"},
+        "e2e": {"value": round(value, 3), "unit": "tok/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--batch", type=int, default=BATCH_PER_GPU, help="sequences per GPU")
+    ap.add_argument("--layers", type=int, default=LAYERS,
+                    help="layers per step (36 for the bench; fewer only for profiling)")
+    ap.add_argument("--pool-blocks", type=int, default=0,
+                    help="pool size in blocks (default: ~70%% of HBM); profiling only")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--cpu-batch", type=int, default=BATCH_PER_GPU)
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        log("note: warm-up raised to 3 steps")
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,149 @@
+/*
+ * slokv.h - C ABI of the B200 (sm_100a) KV-cache hot path.
+ *
+ * Every entry point takes plain device pointers, element strides and a
+ * cudaStream_t passed as `void*`; nothing here knows about torch.  All calls are
+ * asynchronous on `stream`, allocate nothing, never synchronise, and are safe to
+ * capture in a CUDA graph (fixed-address workspace supplied by the caller).
+ *
+ * Return value: SLOKV_OK (0) or a negative SLOKV_ERR_* status for arguments the
+ * host side rejects before any launch.  Invalid *device-resident* metadata
+ * (a slot or block id outside the pool, a context length longer than the block
+ * table) never traps: the kernel skips the offending row, and ORs a
+ * SLOKV_DEVERR_* bit into the caller's `dev_error` word (may be NULL).
+ *
+ * KV pool layout (same as the reference engine): one tensor per layer and per
+ * K/V, shape [num_blocks, block_size, num_kv_heads, head_dim], with the inner
+ * [block_size, num_kv_heads, head_dim] contiguous.  A "slot" is
+ * block_id * block_size + offset.
+ */
+#ifndef SLOKV_H
+#define SLOKV_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes (host-side argument checks) ---------------------------- */
+#define SLOKV_OK                 0
+#define SLOKV_ERR_INVALID_ARG   -1  /* null pointer, negative size, bad geometry  */
+#define SLOKV_ERR_ALIGNMENT     -2  /* pointer/stride not aligned as required     */
+#define SLOKV_ERR_UNSUPPORTED   -3  /* dtype / head_dim / group size not built    */
+#define SLOKV_ERR_CUDA          -4  /* a CUDA runtime call failed                 */
+#define SLOKV_ERR_WORKSPACE     -5  /* workspace missing or too small             */
+
+/* ---- device error word bits ---------------------------------------------- */
+#define SLOKV_DEVERR_SLOT_RANGE   0x1u  /* slot_mapping entry < -1 or >= num_slots  */
+#define SLOKV_DEVERR_BLOCK_RANGE  0x2u  /* block_tables entry outside [0, num_blocks) */
+#define SLOKV_DEVERR_CONTEXT_LEN  0x4u  /* context length > table width * block_size */
+#define SLOKV_DEVERR_TIMEOUT      0x8u  /* a bounded wait on an mbarrier gave up      */
+
+/* ---- element types --------------------------------------------------------- */
+#define SLOKV_DTYPE_BF16      0
+#define SLOKV_DTYPE_F16       1
+#define SLOKV_DTYPE_F32       2
+#define SLOKV_DTYPE_FP8_E4M3  3
+
+/* Human-readable text for a status code. */
+const char *slokv_status_string(int status);
+
+/* ABI version: bumped whenever a signature below changes. */
+int slokv_abi_version(void);
+
+/*
+ * Paged KV append.
+ * Replaces the Triton `store_kvcache_kernel` / `store_kvcache`
+ * (nanovllm/layers/attention.py:10-40).
+ *
+ * For every token i < num_tokens with slot = slot_mapping[i] != -1, copies the
+ * `row_elems` contiguous elements (num_kv_heads * head_dim) of key row i to
+ * k_cache[slot * row_elems ...] and of value row i to v_cache[...].  Rows of
+ * key/value may have any stride (value is a strided view of the fused QKV
+ * output in the reference); the cache rows are contiguous.  Bit copy for any
+ * element type (elem_bytes 1, 2 or 4).  Uses 16-byte vector loads/stores when
+ * every pointer and stride allows it, narrower vectors otherwise.
+ */
+int slokv_kv_append(const void *key, int64_t key_row_stride,
+                    const void *value, int64_t value_row_stride,
+                    void *k_cache, void *v_cache,
+                    const int32_t *slot_mapping, int32_t num_tokens,
+                    int32_t row_elems, int32_t elem_bytes, int64_t num_slots,
+                    uint32_t *dev_error, void *stream);
+
+/*
+ * Workspace needed by slokv_paged_decode for a given geometry, in bytes.
+ * The decode kernel is persistent (one CTA per SM); the workspace holds the
+ * split-K partial states of the context segments that straddle two warps'
+ * ranges, so its size does not depend on the batch or on the context lengths.
+ * device: CUDA ordinal whose SM count sizes the grid (-1 = current device).
+ */
+size_t slokv_paged_decode_workspace_bytes(int32_t device, int32_t num_q_heads,
+                                          int32_t num_kv_heads, int32_t head_dim);
+
+/*
+ * Paged decode attention (one query token per sequence, GQA).
+ * Replaces `flash_attn_with_kvcache(q.unsqueeze(1), k_cache, v_cache,
+ * cache_seqlens=context_lens, block_table=block_tables, softmax_scale, causal=True)`
+ * (nanovllm/layers/attention.py:75-78, nanovllm/layers/mixed_attention.py:117-121).
+ *
+ *   out[b, hq, :] = softmax(scale * q[b, hq] . K[b, 0:L_b, hq / G]^T) . V[...]
+ *
+ * with K/V gathered through block_tables[b, pos / block_size], L_b =
+ * context_lens[b] (already including the token appended this step) and
+ * G = num_q_heads / num_kv_heads.  Rows with L_b <= 0 produce zeros.
+ * Table entries past ceil(L_b / block_size) are never read.
+ *
+ * q/out: element (b, h, d) at base + b*stride_b + h*stride_h + d.
+ * k_cache/v_cache: [num_blocks, block_size, num_kv_heads, head_dim] with the
+ * given block stride (elements).
+ * dtype: SLOKV_DTYPE_BF16 or SLOKV_DTYPE_F16 for q/out/cache.
+ * workspace: >= slokv_paged_decode_workspace_bytes(...) bytes, 256-byte aligned.
+ */
+int slokv_paged_decode(void *out, int64_t out_stride_b, int64_t out_stride_h,
+                       const void *q, int64_t q_stride_b, int64_t q_stride_h,
+                       const void *k_cache, const void *v_cache,
+                       int64_t k_block_stride, int64_t v_block_stride,
+                       int32_t num_blocks, int32_t block_size,
+                       int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                       const int32_t *block_tables, int64_t block_table_stride,
+                       int32_t max_blocks_per_seq,
+                       const int32_t *context_lens, int32_t batch,
+                       float softmax_scale, int32_t dtype,
+                       void *workspace, size_t workspace_bytes,
+                       uint32_t *dev_error, void *stream);
+
+/*
+ * Block-pool page copy.
+ * Device counterpart of the page copy `pool[:, :, page].copy_(saved[:, :, j])`
+ * (diagnostics/online_token_replay/tensors.py:34-43) and of copy-on-write /
+ * swap of whole blocks for prefix sharing and preemption.
+ *
+ * Copies `num_pages` pages.  A page is `page_bytes` contiguous bytes (one block
+ * of one layer of K or V: block_size * num_kv_heads * head_dim * elem_bytes).
+ * The pool is addressed as [num_planes][num_pages_total] pages, where a
+ * "plane" is one (K|V, layer) pair: page p of plane j lives at
+ * base + j * plane_stride_bytes + p * page_stride_bytes.
+ * Page i copies src page src_ids[i] to dst page dst_ids[i], in every plane.
+ * src_ids / dst_ids may be NULL, meaning the identity i (used to gather pages
+ * into, or scatter them out of, a compact buffer).  A pair with a negative id
+ * is skipped; a pair with an id >= the side's capacity (pages per plane) is
+ * skipped and sets SLOKV_DEVERR_BLOCK_RANGE.  Pointers, strides and page_bytes
+ * must be 16-byte aligned.
+ */
+int slokv_kv_block_copy(const void *src, int64_t src_plane_stride_bytes,
+                        int64_t src_page_stride_bytes, const int32_t *src_ids,
+                        int32_t src_capacity,
+                        void *dst, int64_t dst_plane_stride_bytes,
+                        int64_t dst_page_stride_bytes, const int32_t *dst_ids,
+                        int32_t dst_capacity,
+                        int32_t num_pages, int32_t num_planes, int64_t page_bytes,
+                        uint32_t *dev_error, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SLOKV_H */

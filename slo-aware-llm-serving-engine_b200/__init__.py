@@ -1,0 +1,26 @@
+"""B200-native (sm_100a) KV-cache hot path for the SLO-aware serving engine.
+
+Drop-in replacements for the reference engine's paged KV append
+(`store_kvcache`), paged decode / varlen attention (the two flash-attn entry
+points), the `Attention` module with its `Context` metadata, the mixed
+prefill/decode forward, and block-pool page copies.  All compute runs in the
+hand-written kernels of libslokv.so (C ABI: include/slokv.h); nothing here falls
+back to a CPU or library implementation.
+
+The package directory name contains dashes, so import it with
+`importlib.import_module("slo-aware-llm-serving-engine_b200")`.
+"""
+from . import _lib
+from ._lib import SlokvError, read_device_errors
+from .kvcache import (decode_workspace, flash_attn_varlen_func, flash_attn_with_kvcache,
+                      kv_block_copy, kv_block_gather, kv_block_scatter, store_kvcache)
+from .layers.attention import Attention
+from .layers.mixed_attention import MixedAttentionContext, forward_mixed
+from .utils.context import Context, get_context, reset_context, set_context
+
+__all__ = [
+    "Attention", "Context", "MixedAttentionContext", "SlokvError", "decode_workspace",
+    "flash_attn_varlen_func", "flash_attn_with_kvcache", "forward_mixed", "get_context",
+    "kv_block_copy", "kv_block_gather", "kv_block_scatter", "read_device_errors",
+    "reset_context", "set_context", "store_kvcache",
+]

@@ -1,0 +1,626 @@
+// Paged GQA decode attention for sm_100a.
+//
+// Replaces flash_attn_with_kvcache as called by the reference engine
+// (nanovllm/layers/attention.py:75-78 and nanovllm/layers/mixed_attention.py:117-121):
+// one query token per sequence, K/V gathered from the paged pool through
+// block_tables, cache_seqlens already counting the token appended this step.
+//
+// Design (B200-first, HBM-bound):
+//  * Persistent grid: one CTA per SM, 4 autonomous warps per CTA.  The work is
+//    the list of 32-token tiles of every (sequence, kv-head) segment, ordered
+//    (b, kv_head, tile).  Warp slot s of S processes the contiguous range
+//    [s*T/S, (s+1)*T/S) of the T tiles, so every warp streams the same number of
+//    bytes whatever the mix of context lengths (balanced split-K, a.k.a.
+//    flash-decoding with stream-K partitioning).
+//  * Each warp owns a 3-stage ring of 16 KB stages in shared memory.  Lane 0
+//    issues TMA tensor loads (4-D map over [block, token, kv_head, dim], 128-byte
+//    swizzle, evict-first L2 policy) of the K and V tile two stages ahead and
+//    the warp waits on the stage's mbarrier (bounded by a time limit).
+//  * QK^T and PV run on the warp-level tensor-core MMA (m16n8k16, fp32
+//    accumulate): the G query heads that share a KV head are the M rows, so the
+//    K/V tile is read from shared memory once for all of them.  The online
+//    softmax is kept in registers per row and reduced with quad shuffles.
+//  * A segment that lies inside one warp's range is finalised in place; a
+//    segment that straddles warp ranges leaves (m, l, acc) partials in the
+//    workspace, which a small merge kernel combines.  At most two partials per
+//    warp exist, so the workspace does not depend on batch or context length.
+#include "common.cuh"
+
+#include <cudaTypedefs.h>
+
+#include <mutex>
+#include <type_traits>
+
+namespace slokv {
+namespace decode {
+
+constexpr int kD = 128;                         // head_dim
+constexpr int kTile = 32;                       // tokens per pipeline stage
+constexpr int kWarps = 4;                       // autonomous warps per CTA
+constexpr int kStages = 3;                      // ring depth per warp
+constexpr int kHalfBytes = kTile * 128;         // 32 rows x 64 dims x 2 B
+constexpr int kStageBytes = 4 * kHalfBytes;     // K lo/hi + V lo/hi halves
+constexpr int kRingBytes = kWarps * kStages * kStageBytes;
+constexpr int kRowFloats = kD + 4;              // partial row: m, l, pad, pad, acc[kD]
+constexpr int kAccOff = 4;                      // acc starts 16-byte aligned
+constexpr int kMaxBatch = 8192;
+
+struct Params {
+  void *out;
+  int64_t out_sb, out_sh;
+  const void *q;
+  int64_t q_sb, q_sh;
+  const int32_t *block_tables;
+  int64_t bt_stride;
+  int32_t max_blocks;
+  const int32_t *context_lens;
+  int32_t batch;
+  int32_t num_blocks, block_size, hkv, group;
+  float scale_log2;
+  float *partials;  // [nslots][2][group][kRowFloats]
+  uint32_t *err;
+  int32_t nslots;
+};
+
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Number of tiles of sequence b (its segment length per kv head).
+__device__ __forceinline__ int32_t seq_tiles(const Params &p, int b, uint32_t *err_bits) {
+  int32_t len = __ldg(p.context_lens + b);
+  if (len <= 0) return 0;
+  const int32_t cap = p.max_blocks * p.block_size;
+  if (len > cap) {
+    *err_bits |= SLOKV_DEVERR_CONTEXT_LEN;
+    len = cap;
+  }
+  return (len + kTile - 1) / kTile;
+}
+
+__device__ __forceinline__ int32_t seq_len_clamped(const Params &p, int b) {
+  int32_t len = __ldg(p.context_lens + b);
+  const int32_t cap = p.max_blocks * p.block_size;
+  return len > cap ? cap : len;
+}
+
+// Exclusive prefix over sequences of (tiles_b * hkv) into prefix[0..batch].
+// Called by all threads of the CTA.
+__device__ void build_prefix(const Params &p, int32_t *prefix, uint32_t *err_bits) {
+  __shared__ int32_t warp_sums[32];
+  const int tid = threadIdx.x, nthr = blockDim.x;
+  const int per = (p.batch + nthr - 1) / nthr;
+  const int lo = min(tid * per, p.batch), hi = min(lo + per, p.batch);
+  int32_t local = 0;
+  for (int b = lo; b < hi; ++b) local += seq_tiles(p, b, err_bits) * p.hkv;
+  // inclusive scan of `local` across the CTA
+  const int lane = tid & 31, warp = tid >> 5;
+  int32_t v = local;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    int32_t t = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += t;
+  }
+  if (lane == 31) warp_sums[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = nthr >> 5;
+    int32_t w = lane < nw ? warp_sums[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      int32_t t = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += t;
+    }
+    if (lane < nw) warp_sums[lane] = w;
+  }
+  __syncthreads();
+  int32_t run = v - local + (warp > 0 ? warp_sums[warp - 1] : 0);
+  for (int b = lo; b < hi; ++b) {
+    prefix[b] = run;
+    uint32_t dummy = 0;
+    run += seq_tiles(p, b, &dummy) * p.hkv;
+  }
+  if (tid == nthr - 1) prefix[p.batch] = run;
+  __syncthreads();
+}
+
+struct TileRef {
+  int32_t b, h, j, nt, seg_start;
+};
+
+// Locate global tile t: largest b with prefix[b] <= t.
+__device__ __forceinline__ TileRef locate(const Params &p, const int32_t *prefix, int64_t t) {
+  int lo = 0, hi = p.batch - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (prefix[mid] <= t) lo = mid; else hi = mid - 1;
+  }
+  TileRef r;
+  r.b = lo;
+  r.nt = (prefix[lo + 1] - prefix[lo]) / p.hkv;
+  const int32_t rel = static_cast<int32_t>(t - prefix[lo]);
+  r.h = rel / r.nt;
+  r.j = rel - r.h * r.nt;
+  r.seg_start = prefix[lo] + r.h * r.nt;
+  return r;
+}
+
+__device__ __forceinline__ int64_t range_start(int64_t s, int64_t total, int64_t nslots) {
+  return (s * total) / nslots;
+}
+
+// Issue the TMA loads of global tile t into `stage` of this warp's ring.
+__device__ __forceinline__ void issue_tile(const Params &p, const int32_t *prefix,
+                                           const CUtensorMap *kmap, const CUtensorMap *vmap,
+                                           uint32_t ring, uint32_t bars, int stage, int64_t t,
+                                           uint64_t policy) {
+  const TileRef r = locate(p, prefix, t);
+  const int tiles_per_block = p.block_size / kTile;
+  const int page = r.j / tiles_per_block;
+  const int off = (r.j - page * tiles_per_block) * kTile;
+  const int32_t blk = __ldg(p.block_tables + static_cast<int64_t>(r.b) * p.bt_stride + page);
+  if (blk < 0 || blk >= p.num_blocks) record_error(p.err, SLOKV_DEVERR_BLOCK_RANGE);
+  // Out-of-range block ids load as zeros (TMA bounds fill); never a fault.
+  const uint32_t bar = bars + stage * 8;
+  const uint32_t dst = ring + stage * kStageBytes;
+  fence_proxy_async_smem();
+  mbar_arrive_expect_tx(bar, kStageBytes);
+  tma_load_4d(dst + 0 * kHalfBytes, kmap, bar, 0, r.h, off, blk, policy);
+  tma_load_4d(dst + 1 * kHalfBytes, kmap, bar, 64, r.h, off, blk, policy);
+  tma_load_4d(dst + 2 * kHalfBytes, vmap, bar, 0, r.h, off, blk, policy);
+  tma_load_4d(dst + 3 * kHalfBytes, vmap, bar, 64, r.h, off, blk, policy);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kWarps * 32, 1)
+    paged_decode_kernel(const __grid_constant__ CUtensorMap kmap,
+                        const __grid_constant__ CUtensorMap vmap, const Params p) {
+  using M = Mma<T>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  uint8_t *base_ptr = smem_raw + (base - smem_u32(smem_raw));
+  const uint32_t bars_all = base + kRingBytes;
+  int32_t *prefix = reinterpret_cast<int32_t *>(base_ptr + kRingBytes + kWarps * kStages * 8);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, c = lane & 3;
+
+  if (threadIdx.x == 0) {
+    prefetch_tensormap(&kmap);
+    prefetch_tensormap(&vmap);
+  }
+  if (lane == 0) {
+    for (int i = 0; i < kStages; ++i) mbar_init(bars_all + (warp * kStages + i) * 8, 1);
+    fence_barrier_init();
+  }
+  uint32_t err_bits = 0;
+  build_prefix(p, prefix, &err_bits);  // contains __syncthreads
+  if (err_bits && threadIdx.x == 0) record_error(p.err, err_bits);
+
+  const int64_t total = prefix[p.batch];
+  const int64_t s = static_cast<int64_t>(blockIdx.x) * kWarps + warp;
+  const int64_t a = range_start(s, total, p.nslots);
+  const int64_t e = range_start(s + 1, total, p.nslots);
+  if (a >= e) return;
+
+  const uint32_t ring = base + warp * kStages * kStageBytes;
+  const uint32_t bars = bars_all + warp * kStages * 8;
+  const uint64_t policy = l2_evict_first_policy();
+  const int G = p.group;
+
+  if (lane == 0) {
+    for (int i = 0; i < kStages && a + i < e; ++i)
+      issue_tile(p, prefix, &kmap, &vmap, ring, bars, i, a + i, policy);
+  }
+  __syncwarp();
+
+  int64_t t = a;
+  while (t < e) {
+    const TileRef r = locate(p, prefix, t);
+    const int64_t seg_end = static_cast<int64_t>(r.seg_start) + r.nt;
+    const int64_t piece_end = seg_end < e ? seg_end : e;
+    const int32_t len = seq_len_clamped(p, r.b);
+
+    // Q fragments (A operand) for the G heads of kv head r.h; rows >= G are 0.
+    uint32_t qa[8][4];
+    {
+      const T *qb = static_cast<const T *>(p.q) + static_cast<int64_t>(r.b) * p.q_sb +
+                    static_cast<int64_t>(r.h * G) * p.q_sh;
+      const bool r0 = g < G, r1 = g + 8 < G;
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        const int d0 = ks * 16 + 2 * c;
+        qa[ks][0] = r0 ? *reinterpret_cast<const uint32_t *>(qb + g * p.q_sh + d0) : 0u;
+        qa[ks][1] = r1 ? *reinterpret_cast<const uint32_t *>(qb + (g + 8) * p.q_sh + d0) : 0u;
+        qa[ks][2] = r0 ? *reinterpret_cast<const uint32_t *>(qb + g * p.q_sh + d0 + 8) : 0u;
+        qa[ks][3] = r1 ? *reinterpret_cast<const uint32_t *>(qb + (g + 8) * p.q_sh + d0 + 8) : 0u;
+      }
+    }
+    float o[16][4];
+#pragma unroll
+    for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+
+    for (int64_t tt = t; tt < piece_end; ++tt) {
+      const int64_t idx = tt - a;
+      const int stage = static_cast<int>(idx % kStages);
+      const uint32_t parity = static_cast<uint32_t>((idx / kStages) & 1);
+      if (!mbar_wait(bars + stage * 8, parity)) {
+        if (lane == 0) record_error(p.err, SLOKV_DEVERR_TIMEOUT);
+        return;
+      }
+      const int j = static_cast<int>(tt - r.seg_start);
+      const int valid = min(kTile, len - j * kTile);
+      const uint32_t kb = ring + stage * kStageBytes;
+      const uint32_t vb = kb + 2 * kHalfBytes;
+      if (valid < kTile) {
+        // Rows past the context hold stale pool bytes (possibly NaN); zero the
+        // V rows so that P=0 really contributes nothing.
+        uint8_t *vrow = base_ptr + (vb - base);
+        for (int i = lane; i < (kTile - valid) * 16; i += 32) {
+          const int row = valid + (i >> 4), part = i & 15;
+          const int half = part >> 3, chunk = part & 7;
+          *reinterpret_cast<int4 *>(vrow + half * kHalfBytes + row * 128 + chunk * 16) =
+              make_int4(0, 0, 0, 0);
+        }
+        __syncwarp();
+      }
+
+      // ---- S = Q K^T  (16 rows x 32 tokens) ----
+      float sc[4][4];
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt) {
+          const int row = nt * 8 + (lane & 7);
+          const int chunk = kk * 4 + (lane >> 3);
+          const uint32_t addr = kb + (chunk >> 3) * kHalfBytes + swz128(row, chunk & 7);
+          uint32_t b0, b1, b2, b3;
+          ldmatrix_x4(b0, b1, b2, b3, addr);
+          M::run(sc[nt], qa[2 * kk], b0, b1);
+          M::run(sc[nt], qa[2 * kk + 1], b2, b3);
+        }
+      }
+
+      // ---- online softmax (log2 domain) ----
+      float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) {
+#pragma unroll
+        for (int e2 = 0; e2 < 2; ++e2) {
+          const int tok = nt * 8 + 2 * c + e2;
+          const bool ok = tok < valid;
+          sc[nt][e2] = ok ? sc[nt][e2] * p.scale_log2 : -INFINITY;
+          sc[nt][2 + e2] = ok ? sc[nt][2 + e2] * p.scale_log2 : -INFINITY;
+          mx0 = fmaxf(mx0, sc[nt][e2]);
+          mx1 = fmaxf(mx1, sc[nt][2 + e2]);
+        }
+      }
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+      const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+      const float mu0 = mn0 == -INFINITY ? 0.f : mn0;
+      const float mu1 = mn1 == -INFINITY ? 0.f : mn1;
+      const float al0 = fast_exp2(m0 - mu0), al1 = fast_exp2(m1 - mu1);
+      m0 = mn0;
+      m1 = mn1;
+      float rs0 = 0.f, rs1 = 0.f;
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) {
+        sc[nt][0] = fast_exp2(sc[nt][0] - mu0);
+        sc[nt][1] = fast_exp2(sc[nt][1] - mu0);
+        sc[nt][2] = fast_exp2(sc[nt][2] - mu1);
+        sc[nt][3] = fast_exp2(sc[nt][3] - mu1);
+        rs0 += sc[nt][0] + sc[nt][1];
+        rs1 += sc[nt][2] + sc[nt][3];
+      }
+      l0 = l0 * al0 + rs0;
+      l1 = l1 * al1 + rs1;
+#pragma unroll
+      for (int n = 0; n < 16; ++n) {
+        o[n][0] *= al0;
+        o[n][1] *= al0;
+        o[n][2] *= al1;
+        o[n][3] *= al1;
+      }
+      uint32_t pa[2][4];
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        pa[i][0] = M::pack(sc[2 * i][0], sc[2 * i][1]);
+        pa[i][1] = M::pack(sc[2 * i][2], sc[2 * i][3]);
+        pa[i][2] = M::pack(sc[2 * i + 1][0], sc[2 * i + 1][1]);
+        pa[i][3] = M::pack(sc[2 * i + 1][2], sc[2 * i + 1][3]);
+      }
+
+      // ---- O += P V ----
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+#pragma unroll
+        for (int np = 0; np < 8; ++np) {
+          const int row = i * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+          const int chunk = np * 2 + (lane >> 4);
+          const uint32_t addr = vb + (chunk >> 3) * kHalfBytes + swz128(row, chunk & 7);
+          uint32_t b0, b1, b2, b3;
+          ldmatrix_x4_trans(b0, b1, b2, b3, addr);
+          M::run(o[2 * np], pa[i], b0, b1);
+          M::run(o[2 * np + 1], pa[i], b2, b3);
+        }
+      }
+      __syncwarp();
+      if (lane == 0 && tt + kStages < e)
+        issue_tile(p, prefix, &kmap, &vmap, ring, bars, stage, tt + kStages, policy);
+    }
+
+    // ---- finish the piece ----
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+    const bool whole = (t == r.seg_start) && (piece_end == seg_end);
+    if (whole) {
+      const float inv0 = l0 > 0.f ? 1.f / l0 : 0.f;
+      const float inv1 = l1 > 0.f ? 1.f / l1 : 0.f;
+      T *ob = static_cast<T *>(p.out) + static_cast<int64_t>(r.b) * p.out_sb +
+              static_cast<int64_t>(r.h * G) * p.out_sh;
+#pragma unroll
+      for (int n = 0; n < 16; ++n) {
+        const int d = n * 8 + 2 * c;
+        if (g < G)
+          *reinterpret_cast<uint32_t *>(ob + g * p.out_sh + d) =
+              M::pack(o[n][0] * inv0, o[n][1] * inv0);
+        if (g + 8 < G)
+          *reinterpret_cast<uint32_t *>(ob + (g + 8) * p.out_sh + d) =
+              M::pack(o[n][2] * inv1, o[n][3] * inv1);
+      }
+    } else {
+      const int slot_idx = (t == a && t > r.seg_start) ? 0 : 1;
+      float *pb = p.partials + ((s * 2 + slot_idx) * G) * static_cast<int64_t>(kRowFloats);
+      const float mu0 = m0 == -INFINITY ? 0.f : m0;
+      const float mu1 = m1 == -INFINITY ? 0.f : m1;
+      if (g < G) {
+        float *row = pb + g * kRowFloats;
+        if (c == 0) {
+          row[0] = mu0;
+          row[1] = l0;
+        }
+#pragma unroll
+        for (int n = 0; n < 16; ++n)
+          *reinterpret_cast<float2 *>(row + kAccOff + n * 8 + 2 * c) = make_float2(o[n][0], o[n][1]);
+      }
+      if (g + 8 < G) {
+        float *row = pb + (g + 8) * kRowFloats;
+        if (c == 0) {
+          row[0] = mu1;
+          row[1] = l1;
+        }
+#pragma unroll
+        for (int n = 0; n < 16; ++n)
+          *reinterpret_cast<float2 *>(row + kAccOff + n * 8 + 2 * c) = make_float2(o[n][2], o[n][3]);
+      }
+    }
+    t = piece_end;
+  }
+}
+
+// Slot that owns global tile t (max s with range_start(s) <= t).
+__device__ __forceinline__ int64_t owner_slot(int64_t t, int64_t total, int64_t nslots) {
+  int64_t s = (t * nslots) / total;
+  if (s >= nslots) s = nslots - 1;
+  while (s + 1 < nslots && range_start(s + 1, total, nslots) <= t) ++s;
+  while (s > 0 && range_start(s, total, nslots) > t) --s;
+  return s;
+}
+
+// Combine the partials of every segment that straddles warp ranges, and write
+// zeros for empty sequences.  One CTA per sequence; one warp per (kv head, row)
+// item at a time; lane l owns dims [4l, 4l+4).
+template <typename T>
+__global__ void __launch_bounds__(128) paged_decode_merge_kernel(const Params p) {
+  extern __shared__ int32_t prefix[];
+  uint32_t err_bits = 0;
+  build_prefix(p, prefix, &err_bits);
+  const int b = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = p.group;
+  const int64_t total = prefix[p.batch];
+  const int32_t nt = (prefix[b + 1] - prefix[b]) / p.hkv;
+  for (int item = warp; item < p.hkv * G; item += 4) {
+    const int h = item / G, row = item - h * G;
+    T *ob = static_cast<T *>(p.out) + static_cast<int64_t>(b) * p.out_sb +
+            static_cast<int64_t>(h * G + row) * p.out_sh + lane * 4;
+    if (nt == 0) {
+      const float z[4] = {0.f, 0.f, 0.f, 0.f};
+      *reinterpret_cast<uint2 *>(ob) =
+          make_uint2(Mma<T>::pack(z[0], z[1]), Mma<T>::pack(z[2], z[3]));
+      continue;
+    }
+    const int64_t seg0 = static_cast<int64_t>(prefix[b]) + static_cast<int64_t>(h) * nt;
+    const int64_t s_lo = owner_slot(seg0, total, p.nslots);
+    const int64_t s_hi = owner_slot(seg0 + nt - 1, total, p.nslots);
+    if (s_lo == s_hi) continue;  // finalised by the main kernel
+    float mmax = -INFINITY;
+    for (int64_t s = s_lo; s <= s_hi; ++s) {
+      if (s > s_lo && range_start(s + 1, total, p.nslots) == range_start(s, total, p.nslots))
+        continue;
+      const int idx = s == s_lo ? 1 : 0;
+      const float *pr = p.partials + ((s * 2 + idx) * G + row) * static_cast<int64_t>(kRowFloats);
+      mmax = fmaxf(mmax, pr[0]);
+    }
+    float acc[4] = {0.f, 0.f, 0.f, 0.f}, lsum = 0.f;
+    for (int64_t s = s_lo; s <= s_hi; ++s) {
+      if (s > s_lo && range_start(s + 1, total, p.nslots) == range_start(s, total, p.nslots))
+        continue;
+      const int idx = s == s_lo ? 1 : 0;
+      const float *pr = p.partials + ((s * 2 + idx) * G + row) * static_cast<int64_t>(kRowFloats);
+      const float w = fast_exp2(pr[0] - mmax);
+      lsum += w * pr[1];
+      const float4 v = *reinterpret_cast<const float4 *>(pr + kAccOff + lane * 4);
+      acc[0] += w * v.x;
+      acc[1] += w * v.y;
+      acc[2] += w * v.z;
+      acc[3] += w * v.w;
+    }
+    const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+    *reinterpret_cast<uint2 *>(ob) = make_uint2(Mma<T>::pack(acc[0] * inv, acc[1] * inv),
+                                                Mma<T>::pack(acc[2] * inv, acc[3] * inv));
+  }
+}
+
+// ---- host side -------------------------------------------------------------
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+int device_sms(int dev) {
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+    return -1;
+  return n;
+}
+
+bool encode_cache_map(CUtensorMap *map, const void *base, CUtensorMapDataType dt, int elem_bytes,
+                      int64_t block_stride, int num_blocks, int block_size, int hkv) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(kD), static_cast<cuuint64_t>(hkv),
+                        static_cast<cuuint64_t>(block_size), static_cast<cuuint64_t>(num_blocks)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(kD) * elem_bytes,
+                           static_cast<cuuint64_t>(kD) * hkv * elem_bytes,
+                           static_cast<cuuint64_t>(block_stride) * elem_bytes};
+  cuuint32_t box[4] = {static_cast<cuuint32_t>(128 / elem_bytes), 1, kTile, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(map, dt, 4, const_cast<void *>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+size_t workspace_bytes_for(int sms, int group) {
+  return static_cast<size_t>(sms) * kWarps * 2 * group * kRowFloats * sizeof(float);
+}
+
+template <typename T>
+int launch(const Params &p0, const CUtensorMap &km, const CUtensorMap &vm, int sms,
+           cudaStream_t stream) {
+  const size_t smem = 1024 + kRingBytes + kWarps * kStages * 8 +
+                      static_cast<size_t>(p0.batch + 1) * sizeof(int32_t);
+  static std::once_flag once[2];
+  static bool ok[2] = {false, false};
+  const int which = std::is_same<T, __half>::value ? 1 : 0;
+  std::call_once(once[which], [&] {
+    ok[which] = cudaFuncSetAttribute(paged_decode_kernel<T>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     1024 + kRingBytes + kWarps * kStages * 8 +
+                                         (kMaxBatch + 1) * sizeof(int32_t)) == cudaSuccess;
+  });
+  if (!ok[which]) return SLOKV_ERR_CUDA;
+  paged_decode_kernel<T><<<sms, kWarps * 32, smem, stream>>>(km, vm, p0);
+  if (cudaGetLastError() != cudaSuccess) return SLOKV_ERR_CUDA;
+  paged_decode_merge_kernel<T>
+      <<<p0.batch, 128, static_cast<size_t>(p0.batch + 1) * sizeof(int32_t), stream>>>(p0);
+  return cudaGetLastError() == cudaSuccess ? SLOKV_OK : SLOKV_ERR_CUDA;
+}
+
+}  // namespace decode
+}  // namespace slokv
+
+extern "C" size_t slokv_paged_decode_workspace_bytes(int32_t device, int32_t num_q_heads,
+                                                     int32_t num_kv_heads, int32_t head_dim) {
+  using namespace slokv::decode;
+  if (num_kv_heads <= 0 || num_q_heads <= 0 || num_q_heads % num_kv_heads) return 0;
+  if (head_dim != kD) return 0;
+  int dev = device;
+  if (dev < 0 && cudaGetDevice(&dev) != cudaSuccess) return 0;
+  const int sms = device_sms(dev);
+  if (sms <= 0) return 0;
+  return workspace_bytes_for(sms, num_q_heads / num_kv_heads);
+}
+
+extern "C" int slokv_paged_decode(void *out, int64_t out_stride_b, int64_t out_stride_h,
+                                  const void *q, int64_t q_stride_b, int64_t q_stride_h,
+                                  const void *k_cache, const void *v_cache,
+                                  int64_t k_block_stride, int64_t v_block_stride,
+                                  int32_t num_blocks, int32_t block_size, int32_t num_q_heads,
+                                  int32_t num_kv_heads, int32_t head_dim,
+                                  const int32_t *block_tables, int64_t block_table_stride,
+                                  int32_t max_blocks_per_seq, const int32_t *context_lens,
+                                  int32_t batch, float softmax_scale, int32_t dtype,
+                                  void *workspace, size_t workspace_bytes, uint32_t *dev_error,
+                                  void *stream) {
+  using namespace slokv;
+  using namespace slokv::decode;
+  if (batch < 0 || num_blocks <= 0 || block_size <= 0 || num_kv_heads <= 0 || num_q_heads <= 0)
+    return SLOKV_ERR_INVALID_ARG;
+  if (batch == 0) return SLOKV_OK;
+  if (batch > kMaxBatch) return SLOKV_ERR_UNSUPPORTED;
+  if (head_dim != kD) return SLOKV_ERR_UNSUPPORTED;
+  if (dtype != SLOKV_DTYPE_BF16 && dtype != SLOKV_DTYPE_F16) return SLOKV_ERR_UNSUPPORTED;
+  if (num_q_heads % num_kv_heads) return SLOKV_ERR_INVALID_ARG;
+  const int group = num_q_heads / num_kv_heads;
+  if (group > 16) return SLOKV_ERR_UNSUPPORTED;
+  if (block_size % kTile) return SLOKV_ERR_UNSUPPORTED;
+  if (!out || !q || !k_cache || !v_cache || !block_tables || !context_lens || max_blocks_per_seq <= 0)
+    return SLOKV_ERR_INVALID_ARG;
+  // 16-byte rule of TMA for base and strides; 4-byte pairs for q/out.
+  if ((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) & 15u)
+    return SLOKV_ERR_ALIGNMENT;
+  if (((k_block_stride * 2) | (v_block_stride * 2)) & 15) return SLOKV_ERR_ALIGNMENT;
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(out)) & 3u)
+    return SLOKV_ERR_ALIGNMENT;
+  if ((q_stride_b | q_stride_h | out_stride_b | out_stride_h) & 1) return SLOKV_ERR_ALIGNMENT;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return SLOKV_ERR_CUDA;
+  const int sms = device_sms(dev);
+  if (sms <= 0) return SLOKV_ERR_CUDA;
+  const size_t need = workspace_bytes_for(sms, group);
+  if (!workspace || workspace_bytes < need) return SLOKV_ERR_WORKSPACE;
+  if (reinterpret_cast<uintptr_t>(workspace) & 15u) return SLOKV_ERR_ALIGNMENT;
+
+  const CUtensorMapDataType dt =
+      dtype == SLOKV_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap km, vm;
+  if (!encode_cache_map(&km, k_cache, dt, 2, k_block_stride, num_blocks, block_size, num_kv_heads) ||
+      !encode_cache_map(&vm, v_cache, dt, 2, v_block_stride, num_blocks, block_size, num_kv_heads))
+    return SLOKV_ERR_CUDA;
+
+  Params p;
+  p.out = out;
+  p.out_sb = out_stride_b;
+  p.out_sh = out_stride_h;
+  p.q = q;
+  p.q_sb = q_stride_b;
+  p.q_sh = q_stride_h;
+  p.block_tables = block_tables;
+  p.bt_stride = block_table_stride;
+  p.max_blocks = max_blocks_per_seq;
+  p.context_lens = context_lens;
+  p.batch = batch;
+  p.num_blocks = num_blocks;
+  p.block_size = block_size;
+  p.hkv = num_kv_heads;
+  p.group = group;
+  p.scale_log2 = softmax_scale * 1.4426950408889634f;
+  p.partials = static_cast<float *>(workspace);
+  p.err = dev_error;
+  p.nslots = sms * kWarps;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return dtype == SLOKV_DTYPE_BF16 ? launch<__nv_bfloat16>(p, km, vm, sms, st)
+                                   : launch<__half>(p, km, vm, sms, st);
+}

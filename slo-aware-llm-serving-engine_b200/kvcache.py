@@ -1,0 +1,192 @@
+"""Host-side mirror of the reference engine's KV-cache hot path.
+
+Each function keeps the name, argument meaning and error behaviour of the
+reference symbol it replaces, and calls the sm_100a kernels through the C ABI
+(include/slokv.h) on the current CUDA stream.  Everything is asynchronous, does
+no host synchronisation and allocates nothing per call (workspaces are
+per-device and fixed), so it can be captured in a CUDA graph once it has been
+called eagerly at the largest geometry.
+
+  store_kvcache            nanovllm/layers/attention.py:33-40
+  flash_attn_with_kvcache  call sites nanovllm/layers/attention.py:76-78,
+                           nanovllm/layers/mixed_attention.py:117-121
+  kv_block_copy / gather / scatter
+                           page copy of diagnostics/online_token_replay/tensors.py:34-43
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from ._lib import SlokvError, buffers, check, lib, require_cuda, stream_ptr
+
+
+def _i32_contig(name: str, t: torch.Tensor) -> torch.Tensor:
+    if t.dtype != torch.int32:
+        raise SlokvError(f"{name} must be int32, got {t.dtype}")
+    if not t.is_contiguous():
+        raise SlokvError(f"{name} must be contiguous")
+    return t
+
+
+def store_kvcache(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Tensor,
+                  v_cache: torch.Tensor, slot_mapping: torch.Tensor) -> None:
+    """Scatter key/value rows into the paged pool: cache row slot_mapping[i] <- row i.
+
+    slot == -1 skips the token (padding rows of captured decode graphs).  The
+    assertions are the reference wrapper's own (nanovllm/layers/attention.py:36-39).
+    """
+    N, num_heads, head_dim = key.shape
+    D = num_heads * head_dim
+    assert key.stride(-1) == 1 and value.stride(-1) == 1
+    assert key.stride(1) == head_dim and value.stride(1) == head_dim
+    assert k_cache.stride(1) == D and v_cache.stride(1) == D
+    assert slot_mapping.numel() == N
+    dev = require_cuda(key, value, k_cache, v_cache, slot_mapping)
+    if key.dtype != k_cache.dtype or value.dtype != v_cache.dtype or key.dtype != value.dtype:
+        raise SlokvError("key/value/cache dtypes differ")
+    if value.shape != key.shape:
+        raise SlokvError("key and value shapes differ")
+    # The kernel addresses cache row `slot` at slot * D elements, as the reference does.
+    for name, c in (("k_cache", k_cache), ("v_cache", v_cache)):
+        if c.stride(0) != c.shape[1] * D or c.shape[-2] * c.shape[-1] != D:
+            raise SlokvError(f"{name} must be [num_blocks, block_size, {num_heads}, {head_dim}] "
+                             "with contiguous blocks")
+    _i32_contig("slot_mapping", slot_mapping)
+    num_slots = k_cache.shape[0] * k_cache.shape[1]
+    err = buffers.error_word(dev)
+    check(lib().slokv_kv_append(
+        key.data_ptr(), key.stride(0), value.data_ptr(), value.stride(0),
+        k_cache.data_ptr(), v_cache.data_ptr(), slot_mapping.data_ptr(), N, D,
+        key.element_size(), num_slots, err.data_ptr(), stream_ptr(dev)), "kv_append")
+
+
+def decode_workspace(device: torch.device, num_q_heads: int, num_kv_heads: int,
+                     head_dim: int) -> torch.Tensor:
+    """The fixed per-device split-K workspace used by paged decode."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    nbytes = lib().slokv_paged_decode_workspace_bytes(idx, num_q_heads, num_kv_heads, head_dim)
+    if nbytes == 0:
+        raise SlokvError(f"unsupported decode geometry Hq={num_q_heads} Hkv={num_kv_heads} "
+                         f"D={head_dim}")
+    return buffers.workspace(device, f"decode/{num_q_heads // num_kv_heads}/{head_dim}", nbytes)
+
+
+def flash_attn_with_kvcache(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                            cache_seqlens: torch.Tensor, block_table: torch.Tensor,
+                            softmax_scale: float | None = None, causal: bool = True,
+                            out: torch.Tensor | None = None) -> torch.Tensor:
+    """Paged decode attention with the flash_attn_with_kvcache calling convention.
+
+    q: [B, 1, Hq, D]; k_cache/v_cache: [num_blocks, block_size, Hkv, D];
+    cache_seqlens: [B] int32 (length including the token stored this step);
+    block_table: [B, W] int32.  Returns [B, 1, Hq, D].  `causal` is accepted for
+    signature compatibility (one query at the last position sees every key).
+    """
+    if q.dim() != 4 or q.shape[1] != 1:
+        raise SlokvError("paged decode expects q of shape [batch, 1, heads, head_dim]")
+    B, _, Hq, D = q.shape
+    NB, block_size, Hkv, Dk = k_cache.shape
+    if v_cache.shape != k_cache.shape or Dk != D:
+        raise SlokvError("k_cache/v_cache shape mismatch with q")
+    if q.dtype != k_cache.dtype or v_cache.dtype != k_cache.dtype:
+        raise SlokvError("q and cache dtypes differ")
+    if q.stride(-1) != 1:
+        raise SlokvError("q must have a contiguous last dimension")
+    for name, c in (("k_cache", k_cache), ("v_cache", v_cache)):
+        if c.stride(3) != 1 or c.stride(2) != D or c.stride(1) != Hkv * D:
+            raise SlokvError(f"{name} blocks must be contiguous [block_size, Hkv, D]")
+    dev = require_cuda(q, k_cache, v_cache, cache_seqlens, block_table)
+    _i32_contig("cache_seqlens", cache_seqlens)
+    if block_table.dtype != torch.int32 or block_table.stride(-1) != 1:
+        raise SlokvError("block_table must be int32 with a contiguous last dimension")
+    if block_table.shape[0] < B or cache_seqlens.numel() < B:
+        raise SlokvError("block_table / cache_seqlens have fewer rows than q")
+    scale = float(softmax_scale) if softmax_scale is not None else D ** -0.5
+    if out is None:
+        out = torch.empty(B, 1, Hq, D, dtype=q.dtype, device=q.device)
+    ws = decode_workspace(dev, Hq, Hkv, D)
+    err = buffers.error_word(dev)
+    check(lib().slokv_paged_decode(
+        out.data_ptr(), out.stride(0), out.stride(2),
+        q.data_ptr(), q.stride(0), q.stride(2),
+        k_cache.data_ptr(), v_cache.data_ptr(), k_cache.stride(0), v_cache.stride(0),
+        NB, block_size, Hq, Hkv, D,
+        block_table.data_ptr(), block_table.stride(0), block_table.shape[1],
+        cache_seqlens.data_ptr(), B, scale, _lib.dtype_code(q.dtype),
+        ws.data_ptr(), ws.numel(), err.data_ptr(), stream_ptr(dev)), "paged_decode")
+    return out
+
+
+def _pool_planes(pool: torch.Tensor):
+    """View a [2, L, NB, ...] pool (or any [P0, P1, NB, ...]) as planes x pages."""
+    if pool.dim() < 4:
+        raise SlokvError("pool must be [2, num_layers, num_blocks, ...]")
+    inner = pool[0, 0, 0]
+    if not inner.is_contiguous():
+        raise SlokvError("pool pages must be contiguous")
+    if pool.stride(0) != pool.shape[1] * pool.stride(1):
+        raise SlokvError("pool planes (K|V x layer) must be evenly strided")
+    es = pool.element_size()
+    return (pool.shape[0] * pool.shape[1], pool.stride(1) * es, pool.stride(2) * es,
+            inner.numel() * es, pool.shape[2])
+
+
+def kv_block_copy(pool: torch.Tensor, src_ids: torch.Tensor, dst_ids: torch.Tensor) -> None:
+    """pool[:, :, dst_ids[i]] = pool[:, :, src_ids[i]] for every i (all K/V planes, all layers).
+
+    Entries < 0 are skipped.  Source and destination pages must not overlap.
+    """
+    dev = require_cuda(pool, src_ids, dst_ids)
+    _i32_contig("src_ids", src_ids)
+    _i32_contig("dst_ids", dst_ids)
+    if src_ids.numel() != dst_ids.numel():
+        raise SlokvError("src_ids and dst_ids differ in length")
+    planes, plane_stride, page_stride, page_bytes, cap = _pool_planes(pool)
+    check(lib().slokv_kv_block_copy(
+        pool.data_ptr(), plane_stride, page_stride, src_ids.data_ptr(), cap,
+        pool.data_ptr(), plane_stride, page_stride, dst_ids.data_ptr(), cap,
+        src_ids.numel(), planes, page_bytes, buffers.error_word(dev).data_ptr(),
+        stream_ptr(dev)), "kv_block_copy")
+
+
+def kv_block_gather(pool: torch.Tensor, ids: torch.Tensor, out: torch.Tensor | None = None
+                    ) -> torch.Tensor:
+    """Compact copy of pages `ids`: out[:, :, j] = pool[:, :, ids[j]] (swap-out / snapshot)."""
+    dev = require_cuda(pool, ids)
+    _i32_contig("ids", ids)
+    planes, plane_stride, page_stride, page_bytes, cap = _pool_planes(pool)
+    if out is None:
+        shape = list(pool.shape)
+        shape[2] = ids.numel()
+        out = torch.empty(shape, dtype=pool.dtype, device=pool.device)
+    o_planes, o_plane_stride, o_page_stride, o_page_bytes, o_cap = _pool_planes(out)
+    if o_planes != planes or o_page_bytes != page_bytes or o_cap < ids.numel():
+        raise SlokvError("gather destination geometry differs from the pool")
+    check(lib().slokv_kv_block_copy(
+        pool.data_ptr(), plane_stride, page_stride, ids.data_ptr(), cap,
+        out.data_ptr(), o_plane_stride, o_page_stride, None, o_cap,
+        ids.numel(), planes, page_bytes, buffers.error_word(dev).data_ptr(),
+        stream_ptr(dev)), "kv_block_gather")
+    return out
+
+
+def kv_block_scatter(saved: torch.Tensor, pool: torch.Tensor, ids: torch.Tensor) -> None:
+    """pool[:, :, ids[j]] = saved[:, :, j] (swap-in / restore_kv)."""
+    dev = require_cuda(pool, ids, saved)
+    _i32_contig("ids", ids)
+    planes, plane_stride, page_stride, page_bytes, cap = _pool_planes(pool)
+    s_planes, s_plane_stride, s_page_stride, s_page_bytes, s_cap = _pool_planes(saved)
+    if s_planes != planes or s_page_bytes != page_bytes or s_cap < ids.numel():
+        raise SlokvError("scatter source geometry differs from the pool")
+    check(lib().slokv_kv_block_copy(
+        saved.data_ptr(), s_plane_stride, s_page_stride, None, s_cap,
+        pool.data_ptr(), plane_stride, page_stride, ids.data_ptr(), cap,
+        ids.numel(), planes, page_bytes, buffers.error_word(dev).data_ptr(),
+        stream_ptr(dev)), "kv_block_scatter")
+
+
+def flash_attn_varlen_func(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k,
+                           softmax_scale=None, causal=True, block_table=None, out=None):
+    """Causal varlen (prefill) attention; the sm_100a prefill kernel is not built yet."""
+    raise SlokvError("paged prefill attention is not available in this build")

@@ -1,0 +1,49 @@
+"""Drop-in `Attention` module and `store_kvcache` for the reference engine.
+
+Same constructor, `.k_cache`/`.v_cache` attributes (bound by the model runner to
+kv_cache[0, layer] / kv_cache[1, layer]) and forward(q, k, v) dispatch as the
+reference (nanovllm/layers/attention.py:43-79): store the step's K/V, then run
+prefill varlen attention (paged when the context carries block tables), decode
+attention over the paged cache, or the mixed prefill/decode path.
+"""
+import torch
+from torch import nn
+
+from ..kvcache import flash_attn_varlen_func, flash_attn_with_kvcache, store_kvcache
+from ..utils.context import get_context
+
+__all__ = ["Attention", "store_kvcache"]
+
+
+class Attention(nn.Module):
+
+    def __init__(self, num_heads, head_dim, scale, num_kv_heads):
+        super().__init__()
+        self.num_heads = num_heads
+        self.head_dim = head_dim
+        self.scale = scale
+        self.num_kv_heads = num_kv_heads
+        self.k_cache = self.v_cache = torch.tensor([])
+
+    def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor):
+        context = get_context()
+        k_cache, v_cache = self.k_cache, self.v_cache
+        if context.mixed is not None:
+            from .mixed_attention import forward_mixed
+            return forward_mixed(q, k, v, k_cache, v_cache, context, self.scale, store_kvcache)
+        if k_cache.numel() and v_cache.numel():
+            store_kvcache(k, v, k_cache, v_cache, context.slot_mapping)
+        if context.is_prefill:
+            if context.block_tables is not None:    # prefix cache: keys come from the pool
+                k, v = k_cache, v_cache
+            return flash_attn_varlen_func(q, k, v,
+                                          max_seqlen_q=context.max_seqlen_q,
+                                          cu_seqlens_q=context.cu_seqlens_q,
+                                          max_seqlen_k=context.max_seqlen_k,
+                                          cu_seqlens_k=context.cu_seqlens_k,
+                                          softmax_scale=self.scale, causal=True,
+                                          block_table=context.block_tables)
+        return flash_attn_with_kvcache(q.unsqueeze(1), k_cache, v_cache,
+                                       cache_seqlens=context.context_lens,
+                                       block_table=context.block_tables,
+                                       softmax_scale=self.scale, causal=True)

@@ -1,0 +1,52 @@
+"""Mixed prefill/decode attention over one flat decode-first token layout.
+
+Same `MixedAttentionContext` fields and `forward_mixed` signature as the
+reference (nanovllm/layers/mixed_attention.py:15-57): one store over all T rows
+through `store_fn`, decode attention for rows [:num_decode] and varlen prefill
+for the rest (paged through `prefill_tables` when any row has history, else on
+the contiguous k/v of the chunk).  Both kernels write straight into one [T, Hq,
+D] output, so no concatenation copy is made.
+"""
+from dataclasses import dataclass
+
+import torch
+
+from ..kvcache import flash_attn_varlen_func, flash_attn_with_kvcache
+
+
+@dataclass
+class MixedAttentionContext:
+    num_decode: int
+    num_prefill_tokens: int
+    decode_lens: torch.Tensor | None
+    decode_tables: torch.Tensor | None
+    prefill_cu_q: torch.Tensor | None
+    prefill_cu_k: torch.Tensor | None
+    prefill_tables: torch.Tensor | None
+    max_q: int
+    max_k: int
+    prefill_has_history: bool = True
+
+
+def forward_mixed(q, k, v, k_cache, v_cache, context, scale, store_fn):
+    meta = context.mixed
+    if not k_cache.numel() or not v_cache.numel():
+        raise RuntimeError("mixed forward requires an allocated BF16 KV pool")
+    store_fn(k, v, k_cache, v_cache, context.slot_mapping)
+    d = meta.num_decode
+    n = d + meta.num_prefill_tokens
+    out = torch.empty((n,) + tuple(q.shape[1:]), dtype=q.dtype, device=q.device)
+    if d:
+        flash_attn_with_kvcache(q[:d].unsqueeze(1), k_cache, v_cache,
+                                cache_seqlens=meta.decode_lens, block_table=meta.decode_tables,
+                                softmax_scale=scale, causal=True, out=out[:d].unsqueeze(1))
+    if meta.num_prefill_tokens:
+        history = meta.prefill_has_history
+        flash_attn_varlen_func(q[d:n], k_cache if history else k[d:n],
+                               v_cache if history else v[d:n],
+                               cu_seqlens_q=meta.prefill_cu_q, cu_seqlens_k=meta.prefill_cu_k,
+                               max_seqlen_q=meta.max_q, max_seqlen_k=meta.max_k,
+                               softmax_scale=scale, causal=True,
+                               block_table=meta.prefill_tables if history else None,
+                               out=out[d:n])
+    return out

@@ -1,0 +1,83 @@
+"""C-ABI library: it loads, exports every symbol include/*.h declares, and its
+host-side argument checks reject bad calls before any launch.  CPU only: no call
+here reaches a kernel or the CUDA runtime."""
+import ctypes
+import glob
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    names = set()
+    for header in glob.glob(os.path.join(ROOT, "include", "*.h")):
+        text = open(header).read()
+        text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+        names.update(re.findall(r"\b(slokv_\w+)\s*\(", text))
+    return sorted(names)
+
+
+def test_header_declares_entry_points():
+    names = declared_symbols()
+    for required in ("slokv_kv_append", "slokv_paged_decode", "slokv_kv_block_copy",
+                     "slokv_paged_decode_workspace_bytes"):
+        assert required in names
+
+
+def test_library_exports_every_declared_symbol(pkg):
+    lib = pkg._lib.lib()
+    for name in declared_symbols():
+        assert hasattr(lib, name), f"{name} declared in include/ but not exported"
+    assert set(pkg._lib.SIGNATURES) >= set(declared_symbols())
+
+
+def test_status_strings(pkg):
+    lib = pkg._lib.lib()
+    assert lib.slokv_status_string(0) == b"ok"
+    assert b"unsupported" in lib.slokv_status_string(-3)
+    assert lib.slokv_abi_version() >= 1
+
+
+def test_append_argument_checks(pkg):
+    lib = pkg._lib.lib()
+    # zero tokens is a no-op; negative sizes and bad element widths are rejected
+    assert lib.slokv_kv_append(None, 0, None, 0, None, None, None, 0, 1024, 2, 64, None, None) == 0
+    assert lib.slokv_kv_append(None, 0, None, 0, None, None, None, -1, 1024, 2, 64, None, None) == -1
+    assert lib.slokv_kv_append(None, 0, None, 0, None, None, None, 4, 1024, 3, 64, None, None) == -3
+    assert lib.slokv_kv_append(None, 0, None, 0, None, None, None, 4, 1024, 2, 64, None, None) == -1
+
+
+def _decode(lib, **kw):
+    args = dict(out=None, osb=0, osh=0, q=None, qsb=0, qsh=0, kc=None, vc=None, kbs=0, vbs=0,
+                nb=64, bs=256, hq=32, hkv=8, d=128, bt=None, bts=0, w=16, lens=None, batch=4,
+                scale=0.1, dtype=0, ws=None, wsb=0, err=None, stream=None)
+    args.update(kw)
+    return lib.slokv_paged_decode(*args.values())
+
+
+def test_decode_argument_checks(pkg):
+    lib = pkg._lib.lib()
+    assert _decode(lib, batch=0) == 0                   # empty batch: nothing to do
+    assert _decode(lib, batch=-1) == -1
+    assert _decode(lib, d=64) == -3                     # head_dim 128 only
+    assert _decode(lib, dtype=2) == -3                  # fp32 attention not built
+    assert _decode(lib, hq=30) == -1                    # Hq % Hkv
+    assert _decode(lib, hq=8 * 17) == -3                # group > 16
+    assert _decode(lib, bs=48) == -3                    # block size multiple of 32
+    assert _decode(lib) == -1                           # null pointers
+
+
+def test_block_copy_argument_checks(pkg):
+    lib = pkg._lib.lib()
+    def call(src=None, sps=0, dst=None, dps=0, n=0, cap=8, pb=1024):
+        return lib.slokv_kv_block_copy(src, 0, sps, None, cap, dst, 0, dps, None, cap, n, 4, pb,
+                                       None, None)
+    assert call(n=0) == 0
+    assert call(n=-1) == -1
+    assert call(n=2) == -1
+    assert call(n=2, cap=-1) == -1
+    p = ctypes.c_void_p(16)
+    assert call(src=p, sps=8, dst=p, dps=16, n=2) == -2
