@@ -34,6 +34,8 @@ extern "C" {
 #define SLOKV_ERR_UNSUPPORTED   -3  /* dtype / head_dim / group size not built    */
 #define SLOKV_ERR_CUDA          -4  /* a CUDA runtime call failed                 */
 #define SLOKV_ERR_WORKSPACE     -5  /* workspace missing or too small             */
+#define SLOKV_ERR_SCRATCH_LIMIT -6  /* geometry needs more than the fixed scratch of
+                                       slokv_paged_decode_noalloc                 */
 
 /* ---- device error word bits ---------------------------------------------- */
 #define SLOKV_DEVERR_SLOT_RANGE   0x1u  /* slot_mapping entry < -1 or >= num_slots  */
@@ -114,6 +116,46 @@ int slokv_paged_decode(void *out, int64_t out_stride_b, int64_t out_stride_h,
                        float softmax_scale, int32_t dtype,
                        void *workspace, size_t workspace_bytes,
                        uint32_t *dev_error, void *stream);
+
+/*
+ * Allocation-free paged decode.  No counterpart in the reference engine.
+ *
+ * Same arguments and result as slokv_paged_decode, minus the workspace.  It is
+ * for callers that cannot call cudaMalloc: a host runtime that binds only this
+ * C ABI and owns no device allocator, or an engine whose caching allocator has
+ * already given ~90% of HBM to the KV pool, where a new cudaMalloc would fail
+ * or would synchronise the device in the middle of a step.  The split-K
+ * scratch lives in a file-scope __device__ array of
+ * slokv_paged_decode_noalloc_scratch_bytes() bytes (6 MiB) that every GPU
+ * loading the library keeps until the process exits.  Nothing is allocated,
+ * freed or zeroed per call.
+ *
+ * Limits and rules:
+ *  - a geometry whose partials exceed the scratch (on a 148-SM B200: more than
+ *    8 query heads per KV head) returns SLOKV_ERR_SCRATCH_LIMIT and launches
+ *    nothing;
+ *  - the first call on a device looks up the array's device address
+ *    (cudaGetSymbolAddress) with that device current, so make the first call
+ *    on each device before any stream capture;
+ *  - every call on a device shares the one scratch array, which keeps the last
+ *    call's contents; no part of it needs to start at zero (each partial is
+ *    written before it is read within a call), but calls that overlap on the
+ *    GPU -- on different streams, or graphs replayed concurrently -- race on it.
+ */
+int slokv_paged_decode_noalloc(void *out, int64_t out_stride_b, int64_t out_stride_h,
+                               const void *q, int64_t q_stride_b, int64_t q_stride_h,
+                               const void *k_cache, const void *v_cache,
+                               int64_t k_block_stride, int64_t v_block_stride,
+                               int32_t num_blocks, int32_t block_size,
+                               int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                               const int32_t *block_tables, int64_t block_table_stride,
+                               int32_t max_blocks_per_seq,
+                               const int32_t *context_lens, int32_t batch,
+                               float softmax_scale, int32_t dtype,
+                               uint32_t *dev_error, void *stream);
+
+/* Size in bytes of the fixed device scratch used by slokv_paged_decode_noalloc. */
+size_t slokv_paged_decode_noalloc_scratch_bytes(void);
 
 /*
  * Block-pool page copy.

@@ -22,6 +22,7 @@ ERR_ALIGNMENT = -2
 ERR_UNSUPPORTED = -3
 ERR_CUDA = -4
 ERR_WORKSPACE = -5
+ERR_SCRATCH_LIMIT = -6
 
 DEVERR_SLOT_RANGE = 0x1
 DEVERR_BLOCK_RANGE = 0x2
@@ -54,6 +55,11 @@ SIGNATURES = {
         _c_vp, _c_i32,                    # context_lens, batch
         _c_f32, _c_i32,                   # scale, dtype
         _c_vp, _c_sz, _c_vp, _c_vp]),     # workspace, bytes, dev_error, stream
+    "slokv_paged_decode_noalloc": (ctypes.c_int, [
+        _c_vp, _c_i64, _c_i64, _c_vp, _c_i64, _c_i64, _c_vp, _c_vp, _c_i64, _c_i64,
+        _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_vp, _c_i64, _c_i32, _c_vp, _c_i32,
+        _c_f32, _c_i32, _c_vp, _c_vp]),   # as slokv_paged_decode, without the workspace
+    "slokv_paged_decode_noalloc_scratch_bytes": (_c_sz, []),
     "slokv_kv_block_copy": (ctypes.c_int, [
         _c_vp, _c_i64, _c_i64, _c_vp, _c_i32,     # src, strides, ids, capacity
         _c_vp, _c_i64, _c_i64, _c_vp, _c_i32,     # dst, strides, ids, capacity

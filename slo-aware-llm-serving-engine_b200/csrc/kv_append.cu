@@ -110,6 +110,8 @@ extern "C" const char *slokv_status_string(int status) {
     case SLOKV_ERR_UNSUPPORTED: return "unsupported dtype or geometry";
     case SLOKV_ERR_CUDA: return "CUDA runtime error";
     case SLOKV_ERR_WORKSPACE: return "workspace missing or too small";
+    case SLOKV_ERR_SCRATCH_LIMIT:
+      return "geometry needs more than the fixed scratch of the allocation-free entry point";
     default: return "unknown status";
   }
 }

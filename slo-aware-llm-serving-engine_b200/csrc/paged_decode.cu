@@ -624,3 +624,83 @@ extern "C" int slokv_paged_decode(void *out, int64_t out_stride_b, int64_t out_s
   return dtype == SLOKV_DTYPE_BF16 ? launch<__nv_bfloat16>(p, km, vm, sms, st)
                                    : launch<__half>(p, km, vm, sms, st);
 }
+
+// ---- allocation-free decode entry point -------------------------------------
+//
+// For callers that cannot call cudaMalloc: a host runtime bound to this library
+// through its C ABI alone (no device allocator of its own), or an engine whose
+// caching allocator has already handed ~90% of HBM to the KV pool, so a fresh
+// cudaMalloc would fail or would have to synchronise the device mid-step.  The
+// split-K scratch then lives in this file-scope device array instead of a
+// caller-supplied workspace.  Every GPU that loads the library holds the array
+// until the process exits.
+namespace slokv {
+namespace decode {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(6) << 20;  // 6 MiB per device
+constexpr int kMaxDevices = 64;
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+std::mutex g_noalloc_mu;
+void *g_noalloc_ptr[kMaxDevices] = {};
+
+// Device address of g_noalloc_scratch on `dev` (which must be the current
+// device).  In host code the array's name is only a host-side stand-in, so the
+// address is looked up with cudaGetSymbolAddress once per device and cached.
+int noalloc_scratch(int dev, void **out) {
+  if (dev < 0 || dev >= kMaxDevices) return SLOKV_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void *ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || ptr == nullptr)
+      return SLOKV_ERR_CUDA;
+    g_noalloc_ptr[dev] = ptr;
+  }
+  *out = g_noalloc_ptr[dev];
+  return SLOKV_OK;
+}
+
+}  // namespace
+}  // namespace decode
+}  // namespace slokv
+
+extern "C" size_t slokv_paged_decode_noalloc_scratch_bytes(void) {
+  return slokv::decode::kNoAllocScratchBytes;
+}
+
+extern "C" int slokv_paged_decode_noalloc(void *out, int64_t out_stride_b, int64_t out_stride_h,
+                                          const void *q, int64_t q_stride_b, int64_t q_stride_h,
+                                          const void *k_cache, const void *v_cache,
+                                          int64_t k_block_stride, int64_t v_block_stride,
+                                          int32_t num_blocks, int32_t block_size,
+                                          int32_t num_q_heads, int32_t num_kv_heads,
+                                          int32_t head_dim, const int32_t *block_tables,
+                                          int64_t block_table_stride, int32_t max_blocks_per_seq,
+                                          const int32_t *context_lens, int32_t batch,
+                                          float softmax_scale, int32_t dtype,
+                                          uint32_t *dev_error, void *stream) {
+  using namespace slokv;
+  using namespace slokv::decode;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return SLOKV_ERR_CUDA;
+  // The scratch holds the per-warp split-K partials; reject geometries whose
+  // partials would not fit before touching anything.
+  if (num_kv_heads > 0 && num_q_heads > 0 && num_q_heads % num_kv_heads == 0 &&
+      head_dim == kD) {
+    const int sms = device_sms(dev);
+    if (sms <= 0) return SLOKV_ERR_CUDA;
+    if (workspace_bytes_for(sms, num_q_heads / num_kv_heads) > kNoAllocScratchBytes)
+      return SLOKV_ERR_SCRATCH_LIMIT;
+  }
+  void *scratch = nullptr;
+  const int rc = noalloc_scratch(dev, &scratch);
+  if (rc != SLOKV_OK) return rc;
+  return slokv_paged_decode(out, out_stride_b, out_stride_h, q, q_stride_b, q_stride_h, k_cache,
+                            v_cache, k_block_stride, v_block_stride, num_blocks, block_size,
+                            num_q_heads, num_kv_heads, head_dim, block_tables,
+                            block_table_stride, max_blocks_per_seq, context_lens, batch,
+                            softmax_scale, dtype, scratch, kNoAllocScratchBytes, dev_error,
+                            stream);
+}
