@@ -114,21 +114,23 @@ class Clocks:
 # workload
 # ----------------------------------------------------------------------------
 
-def make_metadata(n_gpus, seed=2, batch_per_gpu=BATCH_PER_GPU):
+def make_metadata(n_gpus, seed=2, batch_per_gpu=BATCH_PER_GPU, lo=CTX_LO, hi=CTX_HI):
     """Global batch metadata, identical on every rank (same generator)."""
     gen = torch.Generator().manual_seed(seed)
     B = batch_per_gpu * n_gpus
-    lens = torch.randint(CTX_LO, CTX_HI + 1, (B,), generator=gen, dtype=torch.int64)
+    lens = torch.randint(lo, hi + 1, (B,), generator=gen, dtype=torch.int64)
     pages = (lens + BS - 1) // BS
     return B, lens.to(torch.int32), pages, gen
 
 
 def build_gpu_workload(args, rank, n, device):
     hkv, hq = HKV // n, HQ // n
-    B, lens, pages, gen = make_metadata(n, batch_per_gpu=args.batch)
+    fp8 = args.kv == "fp8"
+    B, lens, pages, gen = make_metadata(n, batch_per_gpu=args.batch, lo=args.ctx_lo,
+                                        hi=args.ctx_hi)
     W = int(pages.max())
     need = int(pages.sum())
-    block_bytes = 2 * args.layers * BS * hkv * D * 2
+    block_bytes = 2 * args.layers * (BS * hkv * D * (1 if fp8 else 2) + (hkv * 4 if fp8 else 0))
     free, total = torch.cuda.mem_get_info(device)
     if args.pool_blocks:
         NB = args.pool_blocks
@@ -150,33 +152,53 @@ def build_gpu_workload(args, rank, n, device):
     log(f"[rank {rank}] pool {NB} blocks x {block_bytes / 2**20:.1f} MiB = "
         f"{NB * block_bytes / 2**30:.1f} GiB ({NB * block_bytes / total:.0%} of HBM), "
         f"batch {B}, Hkv {hkv}, layers {args.layers}")
-    kv = torch.empty(2, args.layers, NB, BS, hkv, D, dtype=torch.bfloat16, device=device)
     g = torch.Generator(device=device).manual_seed(1234 + rank)
-    for i in range(2):
-        for l in range(args.layers):
-            kv[i, l].normal_(0.0, 0.5, generator=g)
+    scales = None
+    if fp8:
+        # finite E4M3 codes (magnitude codes 0..125, random sign) and per-block
+        # scales as if amax 112 had been seen, so appends rarely re-encode
+        kv = torch.empty(2, args.layers, NB, BS, hkv, D, dtype=torch.uint8, device=device)
+        for i in range(2):
+            for l in range(args.layers):
+                kv[i, l].random_(0, 126, generator=g)
+                kv[i, l].bitwise_or_(torch.randint(0, 2, kv[i, l].shape, dtype=torch.uint8,
+                                                   device=device, generator=g) << 7)
+        scales = torch.full((2, args.layers, NB, hkv), 0.25, dtype=torch.float32, device=device)
+    else:
+        kv = torch.empty(2, args.layers, NB, BS, hkv, D, dtype=torch.bfloat16, device=device)
+        for i in range(2):
+            for l in range(args.layers):
+                kv[i, l].normal_(0.0, 0.5, generator=g)
     q = torch.randn(args.layers, B, hq, D, device=device, generator=g).to(torch.bfloat16)
-    knew = (torch.randn(args.layers, B, hkv, D, device=device, generator=g) * 0.5).bfloat16()
-    vnew = (torch.randn(args.layers, B, hkv, D, device=device, generator=g) * 0.5).bfloat16()
+    knew = torch.randn(args.layers, B, hkv, D, device=device, generator=g) * 0.5
+    vnew = torch.randn(args.layers, B, hkv, D, device=device, generator=g) * 0.5
+    if fp8:  # 1% outliers x20
+        knew = torch.where(torch.rand(knew.shape, device=device, generator=g) < 0.01, knew * 20, knew)
+        vnew = torch.where(torch.rand(vnew.shape, device=device, generator=g) < 0.01, vnew * 20, vnew)
+    knew, vnew = knew.bfloat16(), vnew.bfloat16()
     out = torch.empty(args.layers, B, hq, D, dtype=torch.bfloat16, device=device)
     return dict(B=B, hq=hq, hkv=hkv, NB=NB, W=W, lens_cpu=lens, tables_cpu=tables,
                 slots_cpu=slots, lens=lens.to(device), tables=tables.to(device),
                 slots=slots.to(device), kv=kv, q=q, knew=knew, vnew=vnew, out=out,
-                block_bytes=block_bytes)
+                block_bytes=block_bytes, fp8=fp8, scales=scales)
 
 
 def decode_bytes(wl):
     """Algorithmic HBM bytes of one paged_decode launch (one layer)."""
     ctx = int(wl["lens_cpu"].to(torch.int64).sum())
     pages = int(((wl["lens_cpu"].to(torch.int64) + BS - 1) // BS).sum())
-    kv = ctx * wl["hkv"] * D * 2 * 2
+    kv = ctx * wl["hkv"] * D * (1 if wl["fp8"] else 2) * 2
+    scales = pages * wl["hkv"] * 4 * 2 if wl["fp8"] else 0
     qo = wl["B"] * wl["hq"] * D * 2 * 2
     meta = wl["B"] * 4 + pages * 4
-    return kv + qo + meta
+    return kv + scales + qo + meta
 
 
 def append_bytes(wl):
-    """Algorithmic HBM bytes of one kv_append launch: read + write new K and V."""
+    """Algorithmic HBM bytes of one kv_append launch: read new K and V, write them
+    (bf16) or their codes and scales (FP8)."""
+    if wl["fp8"]:
+        return wl["B"] * wl["hkv"] * D * (2 + 1) * 2 + wl["B"] * wl["hkv"] * 4 * 2 * 2 + wl["B"] * 4
     return wl["B"] * wl["hkv"] * D * 2 * 2 * 2 + wl["B"] * 4
 
 
@@ -208,18 +230,31 @@ def run_ours(args):
     scale = D ** -0.5
     kv = wl["kv"]
 
-    def step():
-        for l in range(L):
-            pkg.store_kvcache(wl["knew"][l], wl["vnew"][l], kv[0, l], kv[1, l], wl["slots"])
+    sc = wl["scales"]
+
+    def decode_layer(l):
+        if wl["fp8"]:
+            pkg.flash_attn_with_kvcache_fp8(wl["q"][l].unsqueeze(1), kv[0, l], kv[1, l],
+                                            sc[0, l], sc[1, l], cache_seqlens=wl["lens"],
+                                            block_table=wl["tables"], softmax_scale=scale,
+                                            out=wl["out"][l].unsqueeze(1))
+        else:
             pkg.flash_attn_with_kvcache(wl["q"][l].unsqueeze(1), kv[0, l], kv[1, l],
                                         cache_seqlens=wl["lens"], block_table=wl["tables"],
                                         softmax_scale=scale, out=wl["out"][l].unsqueeze(1))
 
+    def step():
+        for l in range(L):
+            if wl["fp8"]:
+                pkg.store_kvcache_fp8(wl["knew"][l], wl["vnew"][l], kv[0, l], kv[1, l],
+                                      sc[0, l], sc[1, l], wl["slots"])
+            else:
+                pkg.store_kvcache(wl["knew"][l], wl["vnew"][l], kv[0, l], kv[1, l], wl["slots"])
+            decode_layer(l)
+
     def decode_only():
         for l in range(L):
-            pkg.flash_attn_with_kvcache(wl["q"][l].unsqueeze(1), kv[0, l], kv[1, l],
-                                        cache_seqlens=wl["lens"], block_table=wl["tables"],
-                                        softmax_scale=scale, out=wl["out"][l].unsqueeze(1))
+            decode_layer(l)
 
     def barrier():
         if dist is not None:
@@ -286,21 +321,27 @@ def run_ours(args):
         try:
             with open(os.path.join(ROOT, "profiles", "paged_decode_traffic.json")) as f:
                 tr = json.load(f)
-            traffic = tr.get("dram_bytes_per_launch")
+            if not wl["fp8"]:
+                traffic = tr.get("dram_bytes_per_launch")
         except Exception:
             pass
         line = {
             "metric": METRIC, "value": round(tok_s, 1), "unit": "tok/s", "n_gpus": n,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic: K/V ~ 0.5*N(0,1), Q ~ N(0,1), context ~ U[512,4096], random "
-                    "block assignment (seeded)",
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "fp8_e4m3 KV, f16 MMA, bf16 q/out" if wl["fp8"] else "bf16",
+            "data": f"synthetic: K/V ~ 0.5*N(0,1), Q ~ N(0,1), context ~ U[{args.ctx_lo},"
+                    f"{args.ctx_hi}], random block assignment (seeded)",
             "config": {
-                "workload": "BASELINE config 2: pure decode step, 36 layers of kv_append + "
-                            "GQA-4 paged decode, Qwen3-4B KV geometry",
+                "workload": ("BASELINE config 4: FP8-E4M3 KV decode step, 36 layers of "
+                             "quantising append + fused-dequant GQA-4 paged decode"
+                             if wl["fp8"] else
+                             "BASELINE config 2: pure decode step, 36 layers of kv_append + "
+                             "GQA-4 paged decode, Qwen3-4B KV geometry"),
                 "batch_per_gpu": args.batch, "global_batch": B, "layers": L,
                 "kv_heads_per_gpu": wl["hkv"], "q_heads_per_gpu": wl["hq"], "head_dim": D,
-                "block_size": BS, "context": f"U[{CTX_LO},{CTX_HI}]", "pool_blocks": wl["NB"],
+                "block_size": BS, "context": f"U[{args.ctx_lo},{args.ctx_hi}]",
+                "pool_blocks": wl["NB"],
                 "pool_gib": round(wl["NB"] * wl["block_bytes"] / 2 ** 30, 1),
                 "parallelism": f"tp{n} over KV heads (weak: global batch {args.batch}*N)",
                 "l2": "inputs larger than L2: %.2f GB of K/V read per layer" % (dbytes / 1e9),
@@ -325,7 +366,7 @@ def run_ours(args):
                            "ms_per_step": round(e2e_ms, 3),
                            "path": "Attention.forward + Context per layer (store_kvcache + "
                                    "flash_attn_with_kvcache), pinned host buffers"}
-        if n == 1 and not args.no_cpu_baseline:
+        if n == 1 and not args.no_cpu_baseline and not wl["fp8"]:
             line["cpu_baseline"] = cpu_baseline(args, sample_seconds=args.cpu_seconds)
         print(json.dumps(line), flush=True)
     del graph, dgraph
@@ -343,6 +384,8 @@ def run_e2e(args, pkg, wl, device, barrier):
     for l in range(L):
         a = pkg.Attention(wl["hq"], D, D ** -0.5, wl["hkv"])
         a.k_cache, a.v_cache = wl["kv"][0, l], wl["kv"][1, l]
+        if wl["fp8"]:
+            a.k_scale, a.v_scale = wl["scales"][0, l], wl["scales"][1, l]
         attn.append(a)
     h_q = wl["q"].cpu().pin_memory()
     h_k = wl["knew"].cpu().pin_memory()
@@ -472,7 +515,11 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--batch", type=int, default=BATCH_PER_GPU, help="sequences per GPU")
+    ap.add_argument("--kv", choices=["bf16", "fp8"], default="bf16",
+                    help="cache format: bf16 (config 2, the headline) or fp8 (config 4)")
+    ap.add_argument("--batch", type=int, default=None, help="sequences per GPU")
+    ap.add_argument("--ctx-lo", type=int, default=None)
+    ap.add_argument("--ctx-hi", type=int, default=None)
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="layers per step (36 for the bench; fewer only for profiling)")
     ap.add_argument("--pool-blocks", type=int, default=0,
@@ -482,6 +529,13 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--cpu-batch", type=int, default=BATCH_PER_GPU)
     args = ap.parse_args()
+    fp8_defaults = args.kv == "fp8"
+    if args.batch is None:
+        args.batch = 128 if fp8_defaults else BATCH_PER_GPU
+    if args.ctx_lo is None:
+        args.ctx_lo = 1024 if fp8_defaults else CTX_LO
+    if args.ctx_hi is None:
+        args.ctx_hi = 8192 if fp8_defaults else CTX_HI
     if args.warmup < 3 and args.impl == "ours":
         log("note: warm-up raised to 3 steps")
         args.warmup = 3

@@ -42,6 +42,7 @@ extern "C" {
 #define SLOKV_DEVERR_BLOCK_RANGE  0x2u  /* block_tables entry outside [0, num_blocks) */
 #define SLOKV_DEVERR_CONTEXT_LEN  0x4u  /* context length > table width * block_size */
 #define SLOKV_DEVERR_TIMEOUT      0x8u  /* a bounded wait on an mbarrier gave up      */
+#define SLOKV_DEVERR_NONFINITE    0x10u /* FP8 encode met NaN/Inf (stored as code 0x7F) */
 
 /* ---- element types --------------------------------------------------------- */
 #define SLOKV_DTYPE_BF16      0
@@ -116,6 +117,95 @@ int slokv_paged_decode(void *out, int64_t out_stride_b, int64_t out_stride_h,
                        float softmax_scale, int32_t dtype,
                        void *workspace, size_t workspace_bytes,
                        uint32_t *dev_error, void *stream);
+
+/*
+ * Causal varlen attention for prefill chunks, prefix-cached prefill and the
+ * prefill rows of a mixed batch.
+ * Replaces flash_attn_varlen_func(q, k|k_cache, v|v_cache, cu_seqlens_q,
+ * cu_seqlens_k, max_seqlen_q, max_seqlen_k, softmax_scale, causal=True,
+ * block_table) (nanovllm/layers/attention.py:69-74,
+ * nanovllm/layers/mixed_attention.py:123-133).
+ *
+ * Row r has q_len = cu_q[r+1]-cu_q[r] queries and k_len = cu_k[r+1]-cu_k[r]
+ * keys; query i sees keys 0 .. k_len-q_len+i (bottom-right aligned).  Keys come
+ * from the paged pool through block_tables[r, key / block_size] when
+ * block_tables is non-null (k/v are the [num_blocks, block_size, Hkv, 128]
+ * caches, block strides in elements), else from rows cu_k[r] .. of contiguous
+ * k/v ([kv_rows, Hkv, 128] with row strides kv_stride_t / v_stride_t).
+ * q/out: [q_rows, Hq, 128] with the given token / head strides.  bf16 or f16.
+ * tcgen05.mma with TMEM accumulators; block_size must be a multiple of 128.
+ */
+int slokv_paged_prefill(void *out, int64_t out_stride_t, int64_t out_stride_h,
+                        const void *q, int64_t q_stride_t, int64_t q_stride_h, int64_t q_rows,
+                        const void *k, const void *v, int64_t kv_stride_t, int64_t v_stride_t,
+                        int64_t kv_rows, int64_t k_block_stride, int64_t v_block_stride,
+                        const int32_t *cu_seqlens_q, const int32_t *cu_seqlens_k,
+                        int32_t num_rows, int32_t max_seqlen_q,
+                        const int32_t *block_tables, int64_t block_table_stride,
+                        int32_t max_blocks_per_seq, int32_t num_blocks, int32_t block_size,
+                        int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                        float softmax_scale, int32_t dtype, uint32_t *dev_error, void *stream);
+
+/*
+ * FP8-E4M3 KV cache.
+ *
+ * Pool: codes uint8 [num_blocks, block_size, num_kv_heads, head_dim] (one tensor
+ * for K, one for V, as in the bf16 layout) and fp32 scales [num_blocks,
+ * num_kv_heads] for K and for V.  A scale of 0 means "nothing nonzero stored
+ * yet"; zero a block's scales when the block is (re)assigned to a sequence.
+ * The reference has the E4M3FN codec (benchmarks/v0/probe_quant_support.py:24-56)
+ * but no quantised KV path; this is the per-(block, kv-head) contract of the
+ * north star, written out in oracle/kv_oracle.py (fp8_append):
+ *   s_new = max(s_old, amax(new tokens of the block, this head) / 448);
+ *   if s_new > s_old > 0 the block/head's earlier positions are re-encoded as
+ *   encode(fp32(decode(c) * s_old) / s_new); new tokens get encode(x / s_new)
+ *   (divisor 1 while s_new == 0); RNE everywhere, saturation at 448.
+ * The new tokens of one block must be adjacent in slot_mapping with
+ * consecutive offsets (decode: one token per block; prefill: a run).
+ */
+
+/* Quantising append; counterpart of slokv_kv_append for the FP8 pool
+ * (replaces store_kvcache, nanovllm/layers/attention.py:33-40, when the pool is
+ * FP8).  in_dtype: SLOKV_DTYPE_BF16, _F16 or _F32 for key/value.  head_dim 128. */
+int slokv_kv_append_fp8(const void *key, int64_t key_row_stride,
+                        const void *value, int64_t value_row_stride,
+                        void *k_codes, void *v_codes, float *k_scale, float *v_scale,
+                        const int32_t *slot_mapping, int32_t num_tokens,
+                        int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                        int32_t num_blocks, int32_t in_dtype,
+                        uint32_t *dev_error, void *stream);
+
+/* Workspace of slokv_paged_decode_fp8 (8 warp slots per SM), in bytes. */
+size_t slokv_paged_decode_fp8_workspace_bytes(int32_t device, int32_t num_q_heads,
+                                              int32_t num_kv_heads, int32_t head_dim);
+
+/* Paged decode over the FP8 pool, dequantisation fused into the tile load
+ * (replaces flash_attn_with_kvcache, nanovllm/layers/attention.py:76-78, when
+ * the pool is FP8).  Same arguments as slokv_paged_decode plus the two scale
+ * arrays; q/out are bf16 or f16 (q_dtype).  QK^T runs in f16 on the raw codes
+ * with the K scale applied to the scores; PV runs in f16 with the output kept
+ * in units of the current page's V scale.  q must lie within the f16 range. */
+int slokv_paged_decode_fp8(void *out, int64_t out_stride_b, int64_t out_stride_h,
+                           const void *q, int64_t q_stride_b, int64_t q_stride_h,
+                           const void *k_codes, const void *v_codes,
+                           int64_t k_block_stride, int64_t v_block_stride,
+                           const float *k_scale, const float *v_scale,
+                           int32_t num_blocks, int32_t block_size,
+                           int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                           const int32_t *block_tables, int64_t block_table_stride,
+                           int32_t max_blocks_per_seq,
+                           const int32_t *context_lens, int32_t batch,
+                           float softmax_scale, int32_t q_dtype,
+                           void *workspace, size_t workspace_bytes,
+                           uint32_t *dev_error, void *stream);
+
+/* E4M3FN codec on device arrays (the encoder of
+ * benchmarks/v0/probe_quant_support.py:39-56 and decoder of :24-33):
+ * RNE to the nearest code, ties to even, saturate at 448; NaN/Inf encode as
+ * 0x7F and flag SLOKV_DEVERR_NONFINITE. */
+int slokv_fp8_e4m3_encode(const float *x, uint8_t *codes, int64_t n,
+                          uint32_t *dev_error, void *stream);
+int slokv_fp8_e4m3_decode(const uint8_t *codes, float *x, int64_t n, void *stream);
 
 /*
  * Allocation-free paged decode.  No counterpart in the reference engine.

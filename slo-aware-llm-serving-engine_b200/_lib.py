@@ -28,6 +28,7 @@ DEVERR_SLOT_RANGE = 0x1
 DEVERR_BLOCK_RANGE = 0x2
 DEVERR_CONTEXT_LEN = 0x4
 DEVERR_TIMEOUT = 0x8
+DEVERR_NONFINITE = 0x10
 
 DTYPE_BF16 = 0
 DTYPE_F16 = 1
@@ -55,6 +56,26 @@ SIGNATURES = {
         _c_vp, _c_i32,                    # context_lens, batch
         _c_f32, _c_i32,                   # scale, dtype
         _c_vp, _c_sz, _c_vp, _c_vp]),     # workspace, bytes, dev_error, stream
+    "slokv_paged_prefill": (ctypes.c_int, [
+        _c_vp, _c_i64, _c_i64,                    # out, token / head strides
+        _c_vp, _c_i64, _c_i64, _c_i64,            # q, strides, rows
+        _c_vp, _c_vp, _c_i64, _c_i64, _c_i64,     # k, v, row strides, kv rows
+        _c_i64, _c_i64,                           # block strides
+        _c_vp, _c_vp, _c_i32, _c_i32,             # cu_q, cu_k, rows, max_seqlen_q
+        _c_vp, _c_i64, _c_i32, _c_i32, _c_i32,    # tables, stride, width, num_blocks, bs
+        _c_i32, _c_i32, _c_i32, _c_f32, _c_i32,   # Hq, Hkv, D, scale, dtype
+        _c_vp, _c_vp]),                           # dev_error, stream
+    "slokv_kv_append_fp8": (ctypes.c_int, [
+        _c_vp, _c_i64, _c_vp, _c_i64, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_i32, _c_i32,
+        _c_i32, _c_i32, _c_i32, _c_i32, _c_vp, _c_vp]),
+    "slokv_paged_decode_fp8_workspace_bytes": (_c_sz, [_c_i32, _c_i32, _c_i32, _c_i32]),
+    "slokv_paged_decode_fp8": (ctypes.c_int, [
+        _c_vp, _c_i64, _c_i64, _c_vp, _c_i64, _c_i64, _c_vp, _c_vp, _c_i64, _c_i64,
+        _c_vp, _c_vp,                     # k_scale, v_scale
+        _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_vp, _c_i64, _c_i32, _c_vp, _c_i32,
+        _c_f32, _c_i32, _c_vp, _c_sz, _c_vp, _c_vp]),
+    "slokv_fp8_e4m3_encode": (ctypes.c_int, [_c_vp, _c_vp, _c_i64, _c_vp, _c_vp]),
+    "slokv_fp8_e4m3_decode": (ctypes.c_int, [_c_vp, _c_vp, _c_i64, _c_vp]),
     "slokv_paged_decode_noalloc": (ctypes.c_int, [
         _c_vp, _c_i64, _c_i64, _c_vp, _c_i64, _c_i64, _c_vp, _c_vp, _c_i64, _c_i64,
         _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_vp, _c_i64, _c_i32, _c_vp, _c_i32,

@@ -24,8 +24,10 @@ SOURCES = [
     "kv_append.cu",
     "paged_decode.cu",
     "kv_block_copy.cu",
+    "kv_append_fp8.cu",
+    "paged_prefill.cu",
 ]
-HEADERS = ["common.cuh"]
+HEADERS = ["common.cuh", "fp8_e4m3.cuh", "tcgen05.cuh"]
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = [

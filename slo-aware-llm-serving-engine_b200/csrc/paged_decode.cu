@@ -25,6 +25,7 @@
 //    workspace, which a small merge kernel combines.  At most two partials per
 //    warp exist, so the workspace does not depend on batch or context length.
 #include "common.cuh"
+#include "fp8_e4m3.cuh"
 
 #include <cudaTypedefs.h>
 
@@ -57,7 +58,10 @@ struct Params {
   int32_t batch;
   int32_t num_blocks, block_size, hkv, group;
   float scale_log2;
+  const float *k_scale;  // FP8 cache only: [num_blocks, hkv] fp32
+  const float *v_scale;
   float *partials;  // [nslots][2][group][kRowFloats]
+  int4 *jobs;       // [nslots]: merge job of the warp slot (x = -1: none)
   uint32_t *err;
   int32_t nslots;
 };
@@ -151,7 +155,17 @@ __device__ __forceinline__ int64_t range_start(int64_t s, int64_t total, int64_t
   return (s * total) / nslots;
 }
 
+// Slot that owns global tile t (max s with range_start(s) <= t).
+__device__ __forceinline__ int64_t owner_slot(int64_t t, int64_t total, int64_t nslots) {
+  int64_t s = (t * nslots) / total;
+  if (s >= nslots) s = nslots - 1;
+  while (s + 1 < nslots && range_start(s + 1, total, nslots) <= t) ++s;
+  while (s > 0 && range_start(s, total, nslots) > t) --s;
+  return s;
+}
+
 // Issue the TMA loads of global tile t into `stage` of this warp's ring.
+template <bool kFp8>
 __device__ __forceinline__ void issue_tile(const Params &p, const int32_t *prefix,
                                            const CUtensorMap *kmap, const CUtensorMap *vmap,
                                            uint32_t ring, uint32_t bars, int stage, int64_t t,
@@ -164,25 +178,93 @@ __device__ __forceinline__ void issue_tile(const Params &p, const int32_t *prefi
   if (blk < 0 || blk >= p.num_blocks) record_error(p.err, SLOKV_DEVERR_BLOCK_RANGE);
   // Out-of-range block ids load as zeros (TMA bounds fill); never a fault.
   const uint32_t bar = bars + stage * 8;
-  const uint32_t dst = ring + stage * kStageBytes;
   fence_proxy_async_smem();
-  mbar_arrive_expect_tx(bar, kStageBytes);
-  tma_load_4d(dst + 0 * kHalfBytes, kmap, bar, 0, r.h, off, blk, policy);
-  tma_load_4d(dst + 1 * kHalfBytes, kmap, bar, 64, r.h, off, blk, policy);
-  tma_load_4d(dst + 2 * kHalfBytes, vmap, bar, 0, r.h, off, blk, policy);
-  tma_load_4d(dst + 3 * kHalfBytes, vmap, bar, 64, r.h, off, blk, policy);
+  if constexpr (kFp8) {
+    const uint32_t dst = ring + stage * (2 * kTile * 128);
+    mbar_arrive_expect_tx(bar, 2 * kTile * 128);
+    tma_load_4d(dst, kmap, bar, 0, r.h, off, blk, policy);
+    tma_load_4d(dst + kTile * 128, vmap, bar, 0, r.h, off, blk, policy);
+  } else {
+    const uint32_t dst = ring + stage * kStageBytes;
+    mbar_arrive_expect_tx(bar, kStageBytes);
+    tma_load_4d(dst + 0 * kHalfBytes, kmap, bar, 0, r.h, off, blk, policy);
+    tma_load_4d(dst + 1 * kHalfBytes, kmap, bar, 64, r.h, off, blk, policy);
+    tma_load_4d(dst + 2 * kHalfBytes, vmap, bar, 0, r.h, off, blk, policy);
+    tma_load_4d(dst + 3 * kHalfBytes, vmap, bar, 64, r.h, off, blk, policy);
+  }
 }
 
-template <typename T>
-__global__ void __launch_bounds__(kWarps * 32, 1)
+// Shared-memory ring geometry of the two cache formats.  Both use 192 KiB of
+// ring: bf16/f16 tiles are 16 KiB (K and V, two 64-dim halves each), FP8 tiles
+// are 8 KiB, so the FP8 variant runs twice as many warps per SM.
+template <bool kFp8>
+struct Ring {
+  static constexpr int kWarpsPerCta = kFp8 ? 8 : 4;
+  static constexpr int kStage = kFp8 ? 2 * kTile * 128 : kStageBytes;
+  static constexpr int kVOff = kFp8 ? kTile * 128 : 2 * kHalfBytes;  // V offset in a stage
+  static constexpr int kBytes = kWarpsPerCta * kStages * kStage;
+};
+static_assert(Ring<true>::kBytes == kRingBytes && Ring<false>::kBytes == kRingBytes, "ring");
+
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr));
+  return v;
+}
+
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t a) {
+  uint32_t d;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(d) : "r"(a));
+  return d;
+}
+
+// Both byte pairs of a 32-bit word of E4M3 codes -> two f16x2 (low byte of a
+// pair -> low half).
+__device__ __forceinline__ void e4m3x4_to_f16x2x2(uint32_t w, uint32_t &lo, uint32_t &hi) {
+  asm("{\n\t.reg .b16 l, h;\n\tmov.b32 {l, h}, %2;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %0, l;\n\tcvt.rn.f16x2.e4m3x2 %1, h;\n\t}"
+      : "=r"(lo), "=r"(hi)
+      : "r"(w));
+}
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+  return d;
+}
+
+__device__ __forceinline__ uint32_t word(const uint4 &w, int i) {
+  return i == 0 ? w.x : i == 1 ? w.y : i == 2 ? w.z : w.w;
+}
+
+// Output dims of accumulator elements (n-tile n, quad c): bf16/f16 n-tile n
+// holds dims [8n, 8n+8), so the pair (c0, c1) is dims 8n+2c, 8n+2c+1.  FP8:
+// the V fragments of n-tile n take dim 16*g + n for B column g, so c0 / c1 are
+// dims 32c + n and 32c + 16 + n.
+template <bool kFp8>
+__device__ __forceinline__ int out_dim0(int n, int c) {
+  return kFp8 ? 32 * c + n : 8 * n + 2 * c;
+}
+template <bool kFp8>
+__device__ __forceinline__ int out_dim1(int n, int c) {
+  return kFp8 ? 32 * c + 16 + n : 8 * n + 2 * c + 1;
+}
+
+template <typename T, bool kFp8>
+__global__ void __launch_bounds__(Ring<kFp8>::kWarpsPerCta * 32, 1)
     paged_decode_kernel(const __grid_constant__ CUtensorMap kmap,
                         const __grid_constant__ CUtensorMap vmap, const Params p) {
-  using M = Mma<T>;
+  using R = Ring<kFp8>;
+  using MQ = Mma<typename std::conditional<kFp8, __half, T>::type>;  // MMA input type
+  using MO = Mma<T>;                                                  // output type
+  constexpr int kW = R::kWarpsPerCta;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
   uint8_t *base_ptr = smem_raw + (base - smem_u32(smem_raw));
   const uint32_t bars_all = base + kRingBytes;
-  int32_t *prefix = reinterpret_cast<int32_t *>(base_ptr + kRingBytes + kWarps * kStages * 8);
+  int32_t *prefix = reinterpret_cast<int32_t *>(base_ptr + kRingBytes + kW * kStages * 8);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
@@ -200,19 +282,39 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
   if (err_bits && threadIdx.x == 0) record_error(p.err, err_bits);
 
   const int64_t total = prefix[p.batch];
-  const int64_t s = static_cast<int64_t>(blockIdx.x) * kWarps + warp;
+  const int G = p.group;
+
+  // Sequences with no context (graph padding rows) produce zeros; nothing else
+  // touches their output rows.
+  for (int b = blockIdx.x; b < p.batch; b += gridDim.x) {
+    if (prefix[b + 1] != prefix[b]) continue;
+    T *ob = static_cast<T *>(p.out) + static_cast<int64_t>(b) * p.out_sb;
+    const int pairs = kD / 2;
+    for (int i = threadIdx.x; i < p.hkv * G * pairs; i += blockDim.x) {
+      const int row = i / pairs, pr = i - row * pairs;
+      *reinterpret_cast<uint32_t *>(ob + row * p.out_sh + 2 * pr) = 0u;
+    }
+  }
+
+  const int64_t s = static_cast<int64_t>(blockIdx.x) * kW + warp;
   const int64_t a = range_start(s, total, p.nslots);
   const int64_t e = range_start(s + 1, total, p.nslots);
-  if (a >= e) return;
+  // The merge job of this warp slot: the segment whose last piece this warp
+  // holds while earlier pieces sit in other slots.  Rewritten on every call.
+  int4 job = make_int4(-1, 0, 0, 0);
+  if (a >= e) {
+    if (lane == 0) p.jobs[s] = job;
+    return;
+  }
 
-  const uint32_t ring = base + warp * kStages * kStageBytes;
+  const uint32_t ring = base + warp * kStages * R::kStage;
   const uint32_t bars = bars_all + warp * kStages * 8;
   const uint64_t policy = l2_evict_first_policy();
-  const int G = p.group;
+  const int tiles_per_block = p.block_size / kTile;
 
   if (lane == 0) {
     for (int i = 0; i < kStages && a + i < e; ++i)
-      issue_tile(p, prefix, &kmap, &vmap, ring, bars, i, a + i, policy);
+      issue_tile<kFp8>(p, prefix, &kmap, &vmap, ring, bars, i, a + i, policy);
   }
   __syncwarp();
 
@@ -229,41 +331,88 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
       const T *qb = static_cast<const T *>(p.q) + static_cast<int64_t>(r.b) * p.q_sb +
                     static_cast<int64_t>(r.h * G) * p.q_sh;
       const bool r0 = g < G, r1 = g + 8 < G;
+      if constexpr (!kFp8) {
 #pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        const int d0 = ks * 16 + 2 * c;
-        qa[ks][0] = r0 ? *reinterpret_cast<const uint32_t *>(qb + g * p.q_sh + d0) : 0u;
-        qa[ks][1] = r1 ? *reinterpret_cast<const uint32_t *>(qb + (g + 8) * p.q_sh + d0) : 0u;
-        qa[ks][2] = r0 ? *reinterpret_cast<const uint32_t *>(qb + g * p.q_sh + d0 + 8) : 0u;
-        qa[ks][3] = r1 ? *reinterpret_cast<const uint32_t *>(qb + (g + 8) * p.q_sh + d0 + 8) : 0u;
+        for (int ks = 0; ks < 8; ++ks) {
+          const int d0 = ks * 16 + 2 * c;
+          qa[ks][0] = r0 ? *reinterpret_cast<const uint32_t *>(qb + g * p.q_sh + d0) : 0u;
+          qa[ks][1] = r1 ? *reinterpret_cast<const uint32_t *>(qb + (g + 8) * p.q_sh + d0) : 0u;
+          qa[ks][2] = r0 ? *reinterpret_cast<const uint32_t *>(qb + g * p.q_sh + d0 + 8) : 0u;
+          qa[ks][3] = r1 ? *reinterpret_cast<const uint32_t *>(qb + (g + 8) * p.q_sh + d0 + 8) : 0u;
+        }
+      } else {
+        // f16 fragments in the dim order of the FP8 K fragments: k-step
+        // 4*gi + tq takes dims 64*gi + 16*c + 4*tq + {0,1} (k = 2c, 2c+1) and
+        // + {2,3} (k = 2c+8, 2c+9).
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+          const int d0 = 64 * (ks >> 2) + 16 * c + 4 * (ks & 3);
+          uint32_t w[4] = {0u, 0u, 0u, 0u};
+          if (r0) {
+            w[0] = *reinterpret_cast<const uint32_t *>(qb + g * p.q_sh + d0);
+            w[1] = *reinterpret_cast<const uint32_t *>(qb + g * p.q_sh + d0 + 2);
+          }
+          if (r1) {
+            w[2] = *reinterpret_cast<const uint32_t *>(qb + (g + 8) * p.q_sh + d0);
+            w[3] = *reinterpret_cast<const uint32_t *>(qb + (g + 8) * p.q_sh + d0 + 2);
+          }
+          const float2 f0 = MO::unpack(w[0]), f1 = MO::unpack(w[1]);
+          const float2 f2 = MO::unpack(w[2]), f3 = MO::unpack(w[3]);
+          qa[ks][0] = MQ::pack(f0.x, f0.y);
+          qa[ks][2] = MQ::pack(f1.x, f1.y);
+          qa[ks][1] = MQ::pack(f2.x, f2.y);
+          qa[ks][3] = MQ::pack(f3.x, f3.y);
+        }
       }
     }
     float o[16][4];
 #pragma unroll
     for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    float vs_cur = 1.f;  // FP8: o is kept in units of this page's V scale
 
     for (int64_t tt = t; tt < piece_end; ++tt) {
       const int64_t idx = tt - a;
       const int stage = static_cast<int>(idx % kStages);
       const uint32_t parity = static_cast<uint32_t>((idx / kStages) & 1);
+      const int j = static_cast<int>(tt - r.seg_start);
+      float ks_tile = 1.f, vs_tile = 1.f;
+      if constexpr (kFp8) {
+        const int page = j / tiles_per_block;
+        const int32_t blk = __ldg(p.block_tables + static_cast<int64_t>(r.b) * p.bt_stride + page);
+        if (blk >= 0 && blk < p.num_blocks) {
+          const int64_t si = static_cast<int64_t>(blk) * p.hkv + r.h;
+          ks_tile = __ldg(p.k_scale + si);
+          vs_tile = __ldg(p.v_scale + si);
+        } else {
+          ks_tile = 0.f;
+          vs_tile = 0.f;
+        }
+        if (!(vs_tile > 0.f)) vs_tile = 1.f;  // an all-zero page: any unit works
+      }
       if (!mbar_wait(bars + stage * 8, parity)) {
         if (lane == 0) record_error(p.err, SLOKV_DEVERR_TIMEOUT);
         return;
       }
-      const int j = static_cast<int>(tt - r.seg_start);
       const int valid = min(kTile, len - j * kTile);
-      const uint32_t kb = ring + stage * kStageBytes;
-      const uint32_t vb = kb + 2 * kHalfBytes;
+      const uint32_t kb = ring + stage * R::kStage;
+      const uint32_t vb = kb + R::kVOff;
       if (valid < kTile) {
         // Rows past the context hold stale pool bytes (possibly NaN); zero the
-        // V rows so that P=0 really contributes nothing.
+        // V rows so that P = 0 really contributes nothing.
         uint8_t *vrow = base_ptr + (vb - base);
-        for (int i = lane; i < (kTile - valid) * 16; i += 32) {
-          const int row = valid + (i >> 4), part = i & 15;
-          const int half = part >> 3, chunk = part & 7;
-          *reinterpret_cast<int4 *>(vrow + half * kHalfBytes + row * 128 + chunk * 16) =
-              make_int4(0, 0, 0, 0);
+        if constexpr (!kFp8) {
+          for (int i = lane; i < (kTile - valid) * 16; i += 32) {
+            const int row = valid + (i >> 4), part = i & 15;
+            const int half = part >> 3, chunk = part & 7;
+            *reinterpret_cast<int4 *>(vrow + half * kHalfBytes + row * 128 + chunk * 16) =
+                make_int4(0, 0, 0, 0);
+          }
+        } else {
+          for (int i = lane; i < (kTile - valid) * 8; i += 32) {
+            const int row = valid + (i >> 3), chunk = i & 7;
+            *reinterpret_cast<int4 *>(vrow + row * 128 + chunk * 16) = make_int4(0, 0, 0, 0);
+          }
         }
         __syncwarp();
       }
@@ -272,21 +421,40 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
       float sc[4][4];
 #pragma unroll
       for (int nt = 0; nt < 4; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+      if constexpr (!kFp8) {
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
+        for (int kk = 0; kk < 4; ++kk) {
+#pragma unroll
+          for (int nt = 0; nt < 4; ++nt) {
+            const int row = nt * 8 + (lane & 7);
+            const int chunk = kk * 4 + (lane >> 3);
+            const uint32_t addr = kb + (chunk >> 3) * kHalfBytes + swz128(row, chunk & 7);
+            uint32_t b0, b1, b2, b3;
+            ldmatrix_x4(b0, b1, b2, b3, addr);
+            MQ::run(sc[nt], qa[2 * kk], b0, b1);
+            MQ::run(sc[nt], qa[2 * kk + 1], b2, b3);
+          }
+        }
+      } else {
+        // Lane (g, c) reads 16-byte chunks c (dims 16c..) and c + 4 (dims
+        // 64 + 16c..) of token row 8*nt + g: word t of a chunk feeds k-step
+        // 4*gi + t (see the Q fragment order above).
 #pragma unroll
         for (int nt = 0; nt < 4; ++nt) {
-          const int row = nt * 8 + (lane & 7);
-          const int chunk = kk * 4 + (lane >> 3);
-          const uint32_t addr = kb + (chunk >> 3) * kHalfBytes + swz128(row, chunk & 7);
-          uint32_t b0, b1, b2, b3;
-          ldmatrix_x4(b0, b1, b2, b3, addr);
-          M::run(sc[nt], qa[2 * kk], b0, b1);
-          M::run(sc[nt], qa[2 * kk + 1], b2, b3);
+          const int row = nt * 8 + g;
+          const uint4 w0 = lds128(kb + swz128(row, c));
+          const uint4 w1 = lds128(kb + swz128(row, c + 4));
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks) {
+            uint32_t b0, b1;
+            e4m3x4_to_f16x2x2(word(ks < 4 ? w0 : w1, ks & 3), b0, b1);
+            MQ::run(sc[nt], qa[ks], b0, b1);
+          }
         }
       }
 
       // ---- online softmax (log2 domain) ----
+      const float sl = kFp8 ? ks_tile * p.scale_log2 : p.scale_log2;
       float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
       for (int nt = 0; nt < 4; ++nt) {
@@ -294,8 +462,8 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
         for (int e2 = 0; e2 < 2; ++e2) {
           const int tok = nt * 8 + 2 * c + e2;
           const bool ok = tok < valid;
-          sc[nt][e2] = ok ? sc[nt][e2] * p.scale_log2 : -INFINITY;
-          sc[nt][2 + e2] = ok ? sc[nt][2 + e2] * p.scale_log2 : -INFINITY;
+          sc[nt][e2] = ok ? sc[nt][e2] * sl : -INFINITY;
+          sc[nt][2 + e2] = ok ? sc[nt][2 + e2] * sl : -INFINITY;
           mx0 = fmaxf(mx0, sc[nt][e2]);
           mx1 = fmaxf(mx1, sc[nt][2 + e2]);
         }
@@ -322,39 +490,75 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
       }
       l0 = l0 * al0 + rs0;
       l1 = l1 * al1 + rs1;
+      float oa0 = al0, oa1 = al1;
+      if constexpr (kFp8) {
+        // Re-express o in units of this tile's V scale (1 when it is unchanged).
+        const float ratio = tt == t ? 1.f : vs_cur / vs_tile;
+        oa0 *= ratio;
+        oa1 *= ratio;
+        vs_cur = vs_tile;
+      }
 #pragma unroll
       for (int n = 0; n < 16; ++n) {
-        o[n][0] *= al0;
-        o[n][1] *= al0;
-        o[n][2] *= al1;
-        o[n][3] *= al1;
+        o[n][0] *= oa0;
+        o[n][1] *= oa0;
+        o[n][2] *= oa1;
+        o[n][3] *= oa1;
       }
       uint32_t pa[2][4];
 #pragma unroll
       for (int i = 0; i < 2; ++i) {
-        pa[i][0] = M::pack(sc[2 * i][0], sc[2 * i][1]);
-        pa[i][1] = M::pack(sc[2 * i][2], sc[2 * i][3]);
-        pa[i][2] = M::pack(sc[2 * i + 1][0], sc[2 * i + 1][1]);
-        pa[i][3] = M::pack(sc[2 * i + 1][2], sc[2 * i + 1][3]);
+        pa[i][0] = MQ::pack(sc[2 * i][0], sc[2 * i][1]);
+        pa[i][1] = MQ::pack(sc[2 * i][2], sc[2 * i][3]);
+        pa[i][2] = MQ::pack(sc[2 * i + 1][0], sc[2 * i + 1][1]);
+        pa[i][3] = MQ::pack(sc[2 * i + 1][2], sc[2 * i + 1][3]);
       }
 
       // ---- O += P V ----
+      if constexpr (!kFp8) {
 #pragma unroll
-      for (int i = 0; i < 2; ++i) {
+        for (int i = 0; i < 2; ++i) {
 #pragma unroll
-        for (int np = 0; np < 8; ++np) {
-          const int row = i * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-          const int chunk = np * 2 + (lane >> 4);
-          const uint32_t addr = vb + (chunk >> 3) * kHalfBytes + swz128(row, chunk & 7);
-          uint32_t b0, b1, b2, b3;
-          ldmatrix_x4_trans(b0, b1, b2, b3, addr);
-          M::run(o[2 * np], pa[i], b0, b1);
-          M::run(o[2 * np + 1], pa[i], b2, b3);
+          for (int np = 0; np < 8; ++np) {
+            const int row = i * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+            const int chunk = np * 2 + (lane >> 4);
+            const uint32_t addr = vb + (chunk >> 3) * kHalfBytes + swz128(row, chunk & 7);
+            uint32_t b0, b1, b2, b3;
+            ldmatrix_x4_trans(b0, b1, b2, b3, addr);
+            MQ::run(o[2 * np], pa[i], b0, b1);
+            MQ::run(o[2 * np + 1], pa[i], b2, b3);
+          }
+        }
+      } else {
+        // B fragment of n-tile n for lane (g, c): V[tokens 2c, 2c+1 | 2c+8,
+        // 2c+9][dim 16g + n].  The lane loads chunk g (dims 16g..16g+15) of those
+        // four token rows -- rows with different swizzle phases, so the loads
+        // are conflict-free -- and prmt pairs the two tokens' codes of a dim
+        // before one cvt makes the f16x2 register.
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          const int r0 = 16 * i + 2 * c;
+          const uint4 a0 = lds128(vb + swz128(r0, g)), a1 = lds128(vb + swz128(r0 + 1, g));
+          const uint4 a8 = lds128(vb + swz128(r0 + 8, g)), a9 = lds128(vb + swz128(r0 + 9, g));
+#pragma unroll
+          for (int wi = 0; wi < 4; ++wi) {
+            const uint32_t lo01 = prmt(word(a0, wi), word(a1, wi), 0x5140u);  // dims 4wi, 4wi+1
+            const uint32_t hi01 = prmt(word(a0, wi), word(a1, wi), 0x7362u);  // dims 4wi+2, +3
+            const uint32_t lo89 = prmt(word(a8, wi), word(a9, wi), 0x5140u);
+            const uint32_t hi89 = prmt(word(a8, wi), word(a9, wi), 0x7362u);
+            uint32_t b[4][2];
+            e4m3x4_to_f16x2x2(lo01, b[0][0], b[1][0]);
+            e4m3x4_to_f16x2x2(hi01, b[2][0], b[3][0]);
+            e4m3x4_to_f16x2x2(lo89, b[0][1], b[1][1]);
+            e4m3x4_to_f16x2x2(hi89, b[2][1], b[3][1]);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) MQ::run(o[4 * wi + e], pa[i], b[e][0], b[e][1]);
+          }
         }
       }
       __syncwarp();
       if (lane == 0 && tt + kStages < e)
-        issue_tile(p, prefix, &kmap, &vmap, ring, bars, stage, tt + kStages, policy);
+        issue_tile<kFp8>(p, prefix, &kmap, &vmap, ring, bars, stage, tt + kStages, policy);
     }
 
     // ---- finish the piece ----
@@ -364,22 +568,39 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
     l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
     const bool whole = (t == r.seg_start) && (piece_end == seg_end);
     if (whole) {
-      const float inv0 = l0 > 0.f ? 1.f / l0 : 0.f;
-      const float inv1 = l1 > 0.f ? 1.f / l1 : 0.f;
+      const float inv0 = l0 > 0.f ? vs_cur / l0 : 0.f;
+      const float inv1 = l1 > 0.f ? vs_cur / l1 : 0.f;
       T *ob = static_cast<T *>(p.out) + static_cast<int64_t>(r.b) * p.out_sb +
               static_cast<int64_t>(r.h * G) * p.out_sh;
 #pragma unroll
       for (int n = 0; n < 16; ++n) {
-        const int d = n * 8 + 2 * c;
-        if (g < G)
-          *reinterpret_cast<uint32_t *>(ob + g * p.out_sh + d) =
-              M::pack(o[n][0] * inv0, o[n][1] * inv0);
-        if (g + 8 < G)
-          *reinterpret_cast<uint32_t *>(ob + (g + 8) * p.out_sh + d) =
-              M::pack(o[n][2] * inv1, o[n][3] * inv1);
+        if constexpr (!kFp8) {
+          const int d = out_dim0<false>(n, c);
+          if (g < G)
+            *reinterpret_cast<uint32_t *>(ob + g * p.out_sh + d) =
+                MO::pack(o[n][0] * inv0, o[n][1] * inv0);
+          if (g + 8 < G)
+            *reinterpret_cast<uint32_t *>(ob + (g + 8) * p.out_sh + d) =
+                MO::pack(o[n][2] * inv1, o[n][3] * inv1);
+        } else {
+          const int d0 = out_dim0<true>(n, c), d1 = out_dim1<true>(n, c);
+          const uint32_t v0 = MO::pack(o[n][0] * inv0, o[n][1] * inv0);
+          const uint32_t v1 = MO::pack(o[n][2] * inv1, o[n][3] * inv1);
+          if (g < G) {
+            reinterpret_cast<uint16_t *>(ob + g * p.out_sh + d0)[0] = static_cast<uint16_t>(v0);
+            reinterpret_cast<uint16_t *>(ob + g * p.out_sh + d1)[0] = static_cast<uint16_t>(v0 >> 16);
+          }
+          if (g + 8 < G) {
+            reinterpret_cast<uint16_t *>(ob + (g + 8) * p.out_sh + d0)[0] = static_cast<uint16_t>(v1);
+            reinterpret_cast<uint16_t *>(ob + (g + 8) * p.out_sh + d1)[0] = static_cast<uint16_t>(v1 >> 16);
+          }
+        }
       }
     } else {
       const int slot_idx = (t == a && t > r.seg_start) ? 0 : 1;
+      if (slot_idx == 0 && piece_end == seg_end)
+        job = make_int4(r.b, r.h, static_cast<int>(owner_slot(r.seg_start, total, p.nslots)),
+                        static_cast<int>(total));
       float *pb = p.partials + ((s * 2 + slot_idx) * G) * static_cast<int64_t>(kRowFloats);
       const float mu0 = m0 == -INFINITY ? 0.f : m0;
       const float mu1 = m1 == -INFINITY ? 0.f : m1;
@@ -390,8 +611,10 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
           row[1] = l0;
         }
 #pragma unroll
-        for (int n = 0; n < 16; ++n)
-          *reinterpret_cast<float2 *>(row + kAccOff + n * 8 + 2 * c) = make_float2(o[n][0], o[n][1]);
+        for (int n = 0; n < 16; ++n) {
+          row[kAccOff + out_dim0<kFp8>(n, c)] = o[n][0] * vs_cur;
+          row[kAccOff + out_dim1<kFp8>(n, c)] = o[n][1] * vs_cur;
+        }
       }
       if (g + 8 < G) {
         float *row = pb + (g + 8) * kRowFloats;
@@ -400,64 +623,45 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
           row[1] = l1;
         }
 #pragma unroll
-        for (int n = 0; n < 16; ++n)
-          *reinterpret_cast<float2 *>(row + kAccOff + n * 8 + 2 * c) = make_float2(o[n][2], o[n][3]);
+        for (int n = 0; n < 16; ++n) {
+          row[kAccOff + out_dim0<kFp8>(n, c)] = o[n][2] * vs_cur;
+          row[kAccOff + out_dim1<kFp8>(n, c)] = o[n][3] * vs_cur;
+        }
       }
     }
     t = piece_end;
   }
+  if (lane == 0) p.jobs[s] = job;
 }
 
-// Slot that owns global tile t (max s with range_start(s) <= t).
-__device__ __forceinline__ int64_t owner_slot(int64_t t, int64_t total, int64_t nslots) {
-  int64_t s = (t * nslots) / total;
-  if (s >= nslots) s = nslots - 1;
-  while (s + 1 < nslots && range_start(s + 1, total, nslots) <= t) ++s;
-  while (s > 0 && range_start(s, total, nslots) > t) --s;
-  return s;
-}
-
-// Combine the partials of every segment that straddles warp ranges, and write
-// zeros for empty sequences.  One CTA per sequence; one warp per (kv head, row)
-// item at a time; lane l owns dims [4l, 4l+4).
+// Combine the partials of every segment that straddles warp ranges.  One warp
+// per warp slot of the main kernel; the slot's job names the segment whose
+// last piece it holds (pieces: slot s_lo's tail partial, then the head partial
+// of every non-empty slot up to this one).  Lane l owns dims [4l, 4l+4).
 template <typename T>
 __global__ void __launch_bounds__(128) paged_decode_merge_kernel(const Params p) {
-  extern __shared__ int32_t prefix[];
-  uint32_t err_bits = 0;
-  build_prefix(p, prefix, &err_bits);
-  const int b = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t s = static_cast<int64_t>(blockIdx.x) * 4 + warp;
+  if (s >= p.nslots) return;
+  const int4 job = p.jobs[s];
+  if (job.x < 0) return;
   const int G = p.group;
-  const int64_t total = prefix[p.batch];
-  const int32_t nt = (prefix[b + 1] - prefix[b]) / p.hkv;
-  for (int item = warp; item < p.hkv * G; item += 4) {
-    const int h = item / G, row = item - h * G;
-    T *ob = static_cast<T *>(p.out) + static_cast<int64_t>(b) * p.out_sb +
-            static_cast<int64_t>(h * G + row) * p.out_sh + lane * 4;
-    if (nt == 0) {
-      const float z[4] = {0.f, 0.f, 0.f, 0.f};
-      *reinterpret_cast<uint2 *>(ob) =
-          make_uint2(Mma<T>::pack(z[0], z[1]), Mma<T>::pack(z[2], z[3]));
-      continue;
-    }
-    const int64_t seg0 = static_cast<int64_t>(prefix[b]) + static_cast<int64_t>(h) * nt;
-    const int64_t s_lo = owner_slot(seg0, total, p.nslots);
-    const int64_t s_hi = owner_slot(seg0 + nt - 1, total, p.nslots);
-    if (s_lo == s_hi) continue;  // finalised by the main kernel
+  const int64_t total = job.w, s_lo = job.z;
+  for (int row = 0; row < G; ++row) {
     float mmax = -INFINITY;
-    for (int64_t s = s_lo; s <= s_hi; ++s) {
-      if (s > s_lo && range_start(s + 1, total, p.nslots) == range_start(s, total, p.nslots))
+    for (int64_t t = s_lo; t <= s; ++t) {
+      if (t > s_lo && range_start(t + 1, total, p.nslots) == range_start(t, total, p.nslots))
         continue;
-      const int idx = s == s_lo ? 1 : 0;
-      const float *pr = p.partials + ((s * 2 + idx) * G + row) * static_cast<int64_t>(kRowFloats);
+      const float *pr = p.partials + ((t * 2 + (t == s_lo ? 1 : 0)) * G + row) *
+                                         static_cast<int64_t>(kRowFloats);
       mmax = fmaxf(mmax, pr[0]);
     }
     float acc[4] = {0.f, 0.f, 0.f, 0.f}, lsum = 0.f;
-    for (int64_t s = s_lo; s <= s_hi; ++s) {
-      if (s > s_lo && range_start(s + 1, total, p.nslots) == range_start(s, total, p.nslots))
+    for (int64_t t = s_lo; t <= s; ++t) {
+      if (t > s_lo && range_start(t + 1, total, p.nslots) == range_start(t, total, p.nslots))
         continue;
-      const int idx = s == s_lo ? 1 : 0;
-      const float *pr = p.partials + ((s * 2 + idx) * G + row) * static_cast<int64_t>(kRowFloats);
+      const float *pr = p.partials + ((t * 2 + (t == s_lo ? 1 : 0)) * G + row) *
+                                         static_cast<int64_t>(kRowFloats);
       const float w = fast_exp2(pr[0] - mmax);
       lsum += w * pr[1];
       const float4 v = *reinterpret_cast<const float4 *>(pr + kAccOff + lane * 4);
@@ -467,6 +671,8 @@ __global__ void __launch_bounds__(128) paged_decode_merge_kernel(const Params p)
       acc[3] += w * v.w;
     }
     const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+    T *ob = static_cast<T *>(p.out) + static_cast<int64_t>(job.x) * p.out_sb +
+            static_cast<int64_t>(job.y * G + row) * p.out_sh + lane * 4;
     *reinterpret_cast<uint2 *>(ob) = make_uint2(Mma<T>::pack(acc[0] * inv, acc[1] * inv),
                                                 Mma<T>::pack(acc[2] * inv, acc[3] * inv));
   }
@@ -506,66 +712,57 @@ bool encode_cache_map(CUtensorMap *map, const void *base, CUtensorMapDataType dt
                            static_cast<cuuint64_t>(block_stride) * elem_bytes};
   cuuint32_t box[4] = {static_cast<cuuint32_t>(128 / elem_bytes), 1, kTile, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
+  // Promote L2 fills only up to the size of one head's row (256 B bf16, 128 B
+  // FP8): a wider fill would drag in a neighbouring head's row that another
+  // warp streams much later (it is evicted first), doubling DRAM reads.
   CUresult r = fn(map, dt, 4, const_cast<void *>(base), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                  elem_bytes == 1 ? CU_TENSOR_MAP_L2_PROMOTION_L2_128B
+                                  : CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 
-size_t workspace_bytes_for(int sms, int group) {
-  return static_cast<size_t>(sms) * kWarps * 2 * group * kRowFloats * sizeof(float);
+size_t partial_bytes_for(int sms, int group, int warps = kWarps) {
+  return static_cast<size_t>(sms) * warps * 2 * group * kRowFloats * sizeof(float);
 }
 
-template <typename T>
+// Workspace of the bf16/f16 decode (4 warp slots per SM).
+size_t workspace_bytes_for(int sms, int group, int warps = kWarps) {
+  return partial_bytes_for(sms, group, warps) + static_cast<size_t>(sms) * warps * sizeof(int4);
+}
+
+template <typename T, bool kFp8>
 int launch(const Params &p0, const CUtensorMap &km, const CUtensorMap &vm, int sms,
            cudaStream_t stream) {
-  const size_t smem = 1024 + kRingBytes + kWarps * kStages * 8 +
+  constexpr int kW = Ring<kFp8>::kWarpsPerCta;
+  const size_t smem = 1024 + kRingBytes + kW * kStages * 8 +
                       static_cast<size_t>(p0.batch + 1) * sizeof(int32_t);
-  static std::once_flag once[2];
-  static bool ok[2] = {false, false};
-  const int which = std::is_same<T, __half>::value ? 1 : 0;
-  std::call_once(once[which], [&] {
-    ok[which] = cudaFuncSetAttribute(paged_decode_kernel<T>,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     1024 + kRingBytes + kWarps * kStages * 8 +
-                                         (kMaxBatch + 1) * sizeof(int32_t)) == cudaSuccess;
+  static std::once_flag once;
+  static bool ok = false;
+  std::call_once(once, [] {
+    ok = cudaFuncSetAttribute(paged_decode_kernel<T, kFp8>,
+                              cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              1024 + kRingBytes + kW * kStages * 8 +
+                                  (kMaxBatch + 1) * sizeof(int32_t)) == cudaSuccess;
   });
-  if (!ok[which]) return SLOKV_ERR_CUDA;
-  paged_decode_kernel<T><<<sms, kWarps * 32, smem, stream>>>(km, vm, p0);
+  if (!ok) return SLOKV_ERR_CUDA;
+  paged_decode_kernel<T, kFp8><<<sms, kW * 32, smem, stream>>>(km, vm, p0);
   if (cudaGetLastError() != cudaSuccess) return SLOKV_ERR_CUDA;
-  paged_decode_merge_kernel<T>
-      <<<p0.batch, 128, static_cast<size_t>(p0.batch + 1) * sizeof(int32_t), stream>>>(p0);
+  paged_decode_merge_kernel<T><<<(p0.nslots + 3) / 4, 128, 0, stream>>>(p0);
   return cudaGetLastError() == cudaSuccess ? SLOKV_OK : SLOKV_ERR_CUDA;
 }
 
-}  // namespace decode
-}  // namespace slokv
-
-extern "C" size_t slokv_paged_decode_workspace_bytes(int32_t device, int32_t num_q_heads,
-                                                     int32_t num_kv_heads, int32_t head_dim) {
-  using namespace slokv::decode;
-  if (num_kv_heads <= 0 || num_q_heads <= 0 || num_q_heads % num_kv_heads) return 0;
-  if (head_dim != kD) return 0;
-  int dev = device;
-  if (dev < 0 && cudaGetDevice(&dev) != cudaSuccess) return 0;
-  const int sms = device_sms(dev);
-  if (sms <= 0) return 0;
-  return workspace_bytes_for(sms, num_q_heads / num_kv_heads);
-}
-
-extern "C" int slokv_paged_decode(void *out, int64_t out_stride_b, int64_t out_stride_h,
-                                  const void *q, int64_t q_stride_b, int64_t q_stride_h,
-                                  const void *k_cache, const void *v_cache,
-                                  int64_t k_block_stride, int64_t v_block_stride,
-                                  int32_t num_blocks, int32_t block_size, int32_t num_q_heads,
-                                  int32_t num_kv_heads, int32_t head_dim,
-                                  const int32_t *block_tables, int64_t block_table_stride,
-                                  int32_t max_blocks_per_seq, const int32_t *context_lens,
-                                  int32_t batch, float softmax_scale, int32_t dtype,
-                                  void *workspace, size_t workspace_bytes, uint32_t *dev_error,
-                                  void *stream) {
-  using namespace slokv;
-  using namespace slokv::decode;
+// Shared argument checks and launch of both cache formats.
+int run_decode(bool fp8, void *out, int64_t out_stride_b, int64_t out_stride_h, const void *q,
+               int64_t q_stride_b, int64_t q_stride_h, const void *k_cache, const void *v_cache,
+               int64_t k_block_stride, int64_t v_block_stride, const float *k_scale,
+               const float *v_scale, int32_t num_blocks, int32_t block_size,
+               int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+               const int32_t *block_tables, int64_t block_table_stride,
+               int32_t max_blocks_per_seq, const int32_t *context_lens, int32_t batch,
+               float softmax_scale, int32_t dtype, void *workspace, size_t workspace_bytes,
+               uint32_t *dev_error, void *stream) {
   if (batch < 0 || num_blocks <= 0 || block_size <= 0 || num_kv_heads <= 0 || num_q_heads <= 0)
     return SLOKV_ERR_INVALID_ARG;
   if (batch == 0) return SLOKV_OK;
@@ -578,10 +775,13 @@ extern "C" int slokv_paged_decode(void *out, int64_t out_stride_b, int64_t out_s
   if (block_size % kTile) return SLOKV_ERR_UNSUPPORTED;
   if (!out || !q || !k_cache || !v_cache || !block_tables || !context_lens || max_blocks_per_seq <= 0)
     return SLOKV_ERR_INVALID_ARG;
+  if (fp8 && (!k_scale || !v_scale)) return SLOKV_ERR_INVALID_ARG;
+  const int cache_bytes = fp8 ? 1 : 2;
   // 16-byte rule of TMA for base and strides; 4-byte pairs for q/out.
   if ((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) & 15u)
     return SLOKV_ERR_ALIGNMENT;
-  if (((k_block_stride * 2) | (v_block_stride * 2)) & 15) return SLOKV_ERR_ALIGNMENT;
+  if (((k_block_stride * cache_bytes) | (v_block_stride * cache_bytes)) & 15)
+    return SLOKV_ERR_ALIGNMENT;
   if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(out)) & 3u)
     return SLOKV_ERR_ALIGNMENT;
   if ((q_stride_b | q_stride_h | out_stride_b | out_stride_h) & 1) return SLOKV_ERR_ALIGNMENT;
@@ -589,15 +789,20 @@ extern "C" int slokv_paged_decode(void *out, int64_t out_stride_b, int64_t out_s
   if (cudaGetDevice(&dev) != cudaSuccess) return SLOKV_ERR_CUDA;
   const int sms = device_sms(dev);
   if (sms <= 0) return SLOKV_ERR_CUDA;
-  const size_t need = workspace_bytes_for(sms, group);
+  const int warps = fp8 ? Ring<true>::kWarpsPerCta : Ring<false>::kWarpsPerCta;
+  const size_t need = workspace_bytes_for(sms, group, warps);
   if (!workspace || workspace_bytes < need) return SLOKV_ERR_WORKSPACE;
   if (reinterpret_cast<uintptr_t>(workspace) & 15u) return SLOKV_ERR_ALIGNMENT;
 
   const CUtensorMapDataType dt =
-      dtype == SLOKV_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+      fp8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+          : (dtype == SLOKV_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                       : CU_TENSOR_MAP_DATA_TYPE_FLOAT16);
   CUtensorMap km, vm;
-  if (!encode_cache_map(&km, k_cache, dt, 2, k_block_stride, num_blocks, block_size, num_kv_heads) ||
-      !encode_cache_map(&vm, v_cache, dt, 2, v_block_stride, num_blocks, block_size, num_kv_heads))
+  if (!encode_cache_map(&km, k_cache, dt, cache_bytes, k_block_stride, num_blocks, block_size,
+                        num_kv_heads) ||
+      !encode_cache_map(&vm, v_cache, dt, cache_bytes, v_block_stride, num_blocks, block_size,
+                        num_kv_heads))
     return SLOKV_ERR_CUDA;
 
   Params p;
@@ -617,12 +822,83 @@ extern "C" int slokv_paged_decode(void *out, int64_t out_stride_b, int64_t out_s
   p.hkv = num_kv_heads;
   p.group = group;
   p.scale_log2 = softmax_scale * 1.4426950408889634f;
+  p.k_scale = k_scale;
+  p.v_scale = v_scale;
   p.partials = static_cast<float *>(workspace);
+  p.jobs = reinterpret_cast<int4 *>(static_cast<char *>(workspace) +
+                                    partial_bytes_for(sms, group, warps));
   p.err = dev_error;
-  p.nslots = sms * kWarps;
+  p.nslots = sms * warps;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  return dtype == SLOKV_DTYPE_BF16 ? launch<__nv_bfloat16>(p, km, vm, sms, st)
-                                   : launch<__half>(p, km, vm, sms, st);
+  if (fp8)
+    return dtype == SLOKV_DTYPE_BF16 ? launch<__nv_bfloat16, true>(p, km, vm, sms, st)
+                                     : launch<__half, true>(p, km, vm, sms, st);
+  return dtype == SLOKV_DTYPE_BF16 ? launch<__nv_bfloat16, false>(p, km, vm, sms, st)
+                                   : launch<__half, false>(p, km, vm, sms, st);
+}
+
+size_t query_workspace(int32_t device, int32_t num_q_heads, int32_t num_kv_heads,
+                       int32_t head_dim, int warps) {
+  if (num_kv_heads <= 0 || num_q_heads <= 0 || num_q_heads % num_kv_heads) return 0;
+  if (head_dim != kD) return 0;
+  int dev = device;
+  if (dev < 0 && cudaGetDevice(&dev) != cudaSuccess) return 0;
+  const int sms = device_sms(dev);
+  if (sms <= 0) return 0;
+  return workspace_bytes_for(sms, num_q_heads / num_kv_heads, warps);
+}
+
+}  // namespace decode
+}  // namespace slokv
+
+extern "C" size_t slokv_paged_decode_workspace_bytes(int32_t device, int32_t num_q_heads,
+                                                     int32_t num_kv_heads, int32_t head_dim) {
+  using namespace slokv::decode;
+  return query_workspace(device, num_q_heads, num_kv_heads, head_dim,
+                         Ring<false>::kWarpsPerCta);
+}
+
+extern "C" size_t slokv_paged_decode_fp8_workspace_bytes(int32_t device, int32_t num_q_heads,
+                                                         int32_t num_kv_heads, int32_t head_dim) {
+  using namespace slokv::decode;
+  return query_workspace(device, num_q_heads, num_kv_heads, head_dim, Ring<true>::kWarpsPerCta);
+}
+
+extern "C" int slokv_paged_decode(void *out, int64_t out_stride_b, int64_t out_stride_h,
+                                  const void *q, int64_t q_stride_b, int64_t q_stride_h,
+                                  const void *k_cache, const void *v_cache,
+                                  int64_t k_block_stride, int64_t v_block_stride,
+                                  int32_t num_blocks, int32_t block_size, int32_t num_q_heads,
+                                  int32_t num_kv_heads, int32_t head_dim,
+                                  const int32_t *block_tables, int64_t block_table_stride,
+                                  int32_t max_blocks_per_seq, const int32_t *context_lens,
+                                  int32_t batch, float softmax_scale, int32_t dtype,
+                                  void *workspace, size_t workspace_bytes, uint32_t *dev_error,
+                                  void *stream) {
+  return slokv::decode::run_decode(
+      false, out, out_stride_b, out_stride_h, q, q_stride_b, q_stride_h, k_cache, v_cache,
+      k_block_stride, v_block_stride, nullptr, nullptr, num_blocks, block_size, num_q_heads,
+      num_kv_heads, head_dim, block_tables, block_table_stride, max_blocks_per_seq,
+      context_lens, batch, softmax_scale, dtype, workspace, workspace_bytes, dev_error, stream);
+}
+
+extern "C" int slokv_paged_decode_fp8(void *out, int64_t out_stride_b, int64_t out_stride_h,
+                                      const void *q, int64_t q_stride_b, int64_t q_stride_h,
+                                      const void *k_codes, const void *v_codes,
+                                      int64_t k_block_stride, int64_t v_block_stride,
+                                      const float *k_scale, const float *v_scale,
+                                      int32_t num_blocks, int32_t block_size,
+                                      int32_t num_q_heads, int32_t num_kv_heads,
+                                      int32_t head_dim, const int32_t *block_tables,
+                                      int64_t block_table_stride, int32_t max_blocks_per_seq,
+                                      const int32_t *context_lens, int32_t batch,
+                                      float softmax_scale, int32_t q_dtype, void *workspace,
+                                      size_t workspace_bytes, uint32_t *dev_error, void *stream) {
+  return slokv::decode::run_decode(
+      true, out, out_stride_b, out_stride_h, q, q_stride_b, q_stride_h, k_codes, v_codes,
+      k_block_stride, v_block_stride, k_scale, v_scale, num_blocks, block_size, num_q_heads,
+      num_kv_heads, head_dim, block_tables, block_table_stride, max_blocks_per_seq,
+      context_lens, batch, softmax_scale, q_dtype, workspace, workspace_bytes, dev_error, stream);
 }
 
 // ---- allocation-free decode entry point -------------------------------------

@@ -1,0 +1,484 @@
+// Causal varlen (prefill / prefix-cache / mixed-batch prefill) attention on the
+// sm_100a tensor cores.
+//
+// Replaces flash_attn_varlen_func as the reference engine calls it
+// (nanovllm/layers/attention.py:69-74, nanovllm/layers/mixed_attention.py:123-133):
+// rows r with q_len = cu_q[r+1]-cu_q[r] queries and k_len = cu_k[r+1]-cu_k[r]
+// keys; query i sees keys 0 .. k_len-q_len+i (bottom-right aligned causal
+// mask); keys come from the paged pool through block_tables (prefix cache) or
+// from contiguous k/v rows (cold prefill).  GQA: query head h uses kv head
+// h / (Hq/Hkv).
+//
+// Design (one CTA = 128 queries of one head of one row, 4 warps):
+//  * TMA loads Q once and K/V tiles of 128 keys (two 64-dim halves each,
+//    128-byte swizzle = the canonical K-major UMMA layout) into double-buffered
+//    K and V rings; no cluster multicast.
+//  * One thread issues tcgen05.mma (kind::f16, M=128, fp32 accumulate in TMEM):
+//    S_j = Q K_j^T into one of two TMEM S buffers -- S_{j+1} is issued before the
+//    softmax of S_j, so the tensor core works while the CUDA cores do exp --
+//    and O += P_j V_j with V as an MN-major operand (two N=64 halves).
+//  * Softmax: thread t owns query row t (TMEM lane t): it loads its 128 scores
+//    with tcgen05.ld, so max/sum need no shuffles; P is written as bf16/f16
+//    into a swizzled shared-memory tile (the A operand of the PV MMA).  O stays
+//    in TMEM and is rescaled there (tcgen05.ld/st) only when a warp's row max
+//    moved.
+//  * V rows past k_len in the last tile are zeroed before PV so stale pool bytes
+//    (possibly NaN) never reach O; masked scores are -inf, not multiplied.
+#include "common.cuh"
+#include "tcgen05.cuh"
+
+#include <cudaTypedefs.h>
+
+#include <mutex>
+#include <type_traits>
+
+namespace slokv {
+namespace prefill {
+
+constexpr int kD = 128;
+constexpr int kBM = 128;                  // queries per CTA
+constexpr int kBN = 128;                  // keys per tile
+constexpr int kHalf = 128 * 128;          // 128 rows x 128 bytes (one 64-dim half)
+constexpr int kTile = 2 * kHalf;          // 32 KiB: 128 x 128 16-bit elements
+constexpr int kOffQ = 0;
+constexpr int kOffK = kTile;              // two stages
+constexpr int kOffV = 3 * kTile;          // two stages
+constexpr int kOffP = 5 * kTile;
+constexpr int kTiles = 6 * kTile;         // 192 KiB
+// barriers after the tiles: Q, K[2], V[2], S[2], PV
+constexpr int kBarQ = 0, kBarK = 1, kBarV = 3, kBarS = 5, kBarPV = 7, kNumBars = 8;
+constexpr int kSmemBytes = 1024 + kTiles + kNumBars * 8 + 16;
+constexpr uint32_t kTmemCols = 512;       // S0 | S1 | O (128 columns each)
+constexpr uint32_t kColS = 0, kColO = 256;
+
+struct Params {
+  void *out;
+  int64_t out_st, out_sh;                 // out[token][head][dim]
+  const int32_t *cu_q, *cu_k;
+  const int32_t *block_tables;            // null: contiguous k/v
+  int64_t bt_stride;
+  int32_t max_blocks;
+  int32_t num_blocks, block_size;
+  int32_t hq, hkv, group;
+  float scale_log2;
+  uint32_t *err;
+};
+
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <typename T>
+struct Pack;
+template <>
+struct Pack<__nv_bfloat16> {
+  __device__ __forceinline__ static uint32_t two(float a, float b) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t *>(&v);
+  }
+};
+template <>
+struct Pack<__half> {
+  __device__ __forceinline__ static uint32_t two(float a, float b) {
+    __half2 v = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t *>(&v);
+  }
+};
+
+// Coordinates of key tile j (keys 128j .. 128j+127 of row r) for the K/V maps.
+struct KvCoord {
+  int32_t c2, c3;
+  bool ok;
+};
+
+__device__ __forceinline__ KvCoord kv_coord(const Params &p, int r, int k0, int j) {
+  KvCoord c;
+  const int key = j * kBN;
+  if (p.block_tables == nullptr) {
+    c.c2 = k0 + key;
+    c.c3 = 0;
+    c.ok = true;
+  } else {
+    const int page = key / p.block_size;
+    c.c2 = key - page * p.block_size;
+    // A page past the table width or an id outside the pool loads as zeros
+    // (TMA bounds fill) and is flagged; the table row is never over-read.
+    c.c3 = page < p.max_blocks
+               ? __ldg(p.block_tables + static_cast<int64_t>(r) * p.bt_stride + page) : -1;
+    c.ok = c.c3 >= 0 && c.c3 < p.num_blocks;
+  }
+  return c;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(128, 1)
+    paged_prefill_kernel(const __grid_constant__ CUtensorMap qmap,
+                         const __grid_constant__ CUtensorMap kmap,
+                         const __grid_constant__ CUtensorMap vmap, const Params p) {
+  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+  constexpr uint32_t kIdescS = tc::idesc_f16(kBf16, false, 128, 128);
+  constexpr uint32_t kIdescPV = tc::idesc_f16(kBf16, true, 128, 64);
+
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int r = blockIdx.z, h = blockIdx.y;
+  const int m = gridDim.x - 1 - blockIdx.x;  // longest (last) query tiles first
+  const int q0 = __ldg(p.cu_q + r), q_len = __ldg(p.cu_q + r + 1) - q0;
+  const int k0 = __ldg(p.cu_k + r), k_len = __ldg(p.cu_k + r + 1) - k0;
+  if (m * kBM >= q_len) return;
+  const int hk = h / p.group;
+  const int qk_off = k_len - q_len;
+  const int last_q = min((m + 1) * kBM, q_len) - 1;
+  const int need = min(k_len, qk_off + last_q + 1);   // keys any query of the tile sees
+  const int nk = need > 0 ? (need + kBN - 1) / kBN : 0;
+  // query row of this thread and the last key it may see (inclusive)
+  const int qi = m * kBM + tid;
+  const bool row_ok = qi < q_len;
+  const int kmax = row_ok ? min(qk_off + qi, k_len - 1) : -1;
+  T *orow = static_cast<T *>(p.out) + static_cast<int64_t>(q0 + qi) * p.out_st +
+            static_cast<int64_t>(h) * p.out_sh;
+
+  if (nk == 0) {  // no query of the tile sees any key: zero output
+    if (row_ok)
+      for (int d = 0; d < kD; d += 8)
+        *reinterpret_cast<uint4 *>(orow + d) = make_uint4(0, 0, 0, 0);
+    return;
+  }
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t *base_ptr = smem_raw + (base - raw);
+  const uint32_t bars = base + kTiles;
+  volatile uint32_t *tmem_slot = reinterpret_cast<volatile uint32_t *>(base_ptr + kTiles + kNumBars * 8);
+  volatile uint32_t *abort_flag = tmem_slot + 1;
+
+  if (tid == 0) {
+    prefetch_tensormap(&qmap);
+    prefetch_tensormap(&kmap);
+    prefetch_tensormap(&vmap);
+    for (int i = 0; i < kNumBars; ++i) mbar_init(bars + i * 8, 1);
+    fence_barrier_init();
+    *abort_flag = 0;
+  }
+  if (warp == 0) {
+    tc::tmem_alloc(smem_u32(const_cast<uint32_t *>(tmem_slot)), kTmemCols);
+    tc::tmem_relinquish();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+  const uint64_t policy = l2_evict_first_policy();
+
+  auto bar = [&](int i) { return bars + i * 8; };
+  auto issue_k = [&](int j) {
+    const KvCoord c = kv_coord(p, r, k0, j);
+    if (!c.ok) record_error(p.err, SLOKV_DEVERR_BLOCK_RANGE);
+    const uint32_t dst = base + kOffK + (j & 1) * kTile;
+    mbar_arrive_expect_tx(bar(kBarK + (j & 1)), kTile);
+    tma_load_4d(dst, &kmap, bar(kBarK + (j & 1)), 0, hk, c.c2, c.c3, policy);
+    tma_load_4d(dst + kHalf, &kmap, bar(kBarK + (j & 1)), 64, hk, c.c2, c.c3, policy);
+  };
+  auto issue_v = [&](int j) {
+    const KvCoord c = kv_coord(p, r, k0, j);
+    const uint32_t dst = base + kOffV + (j & 1) * kTile;
+    mbar_arrive_expect_tx(bar(kBarV + (j & 1)), kTile);
+    tma_load_4d(dst, &vmap, bar(kBarV + (j & 1)), 0, hk, c.c2, c.c3, policy);
+    tma_load_4d(dst + kHalf, &vmap, bar(kBarV + (j & 1)), 64, hk, c.c2, c.c3, policy);
+  };
+  auto wait_or_abort = [&](int i, uint32_t parity) {
+    if (!mbar_wait(bar(i), parity)) {
+      record_error(p.err, SLOKV_DEVERR_TIMEOUT);
+      *abort_flag = 1;
+      return false;
+    }
+    return true;
+  };
+  // S_j = Q K_j^T -> TMEM S buffer j&1 (issued by thread 0)
+  auto issue_s = [&](int j) {
+    if (*abort_flag || !wait_or_abort(kBarK + (j & 1), (j >> 1) & 1)) return;
+    tc::fence_after_sync();
+    const uint32_t qa = base + kOffQ, kb = base + kOffK + (j & 1) * kTile;
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      const uint32_t off = (kk >> 2) * kHalf + (kk & 3) * 32;
+      tc::mma_f16_ss(tmem + kColS + (j & 1) * 128, tc::smem_desc_sw128(qa + off, 16, 1024),
+                     tc::smem_desc_sw128(kb + off, 16, 1024), kIdescS, kk > 0);
+    }
+    tc::commit(bar(kBarS + (j & 1)));
+  };
+
+  if (tid == 0) {
+    fence_proxy_async_smem();
+    mbar_arrive_expect_tx(bar(kBarQ), kTile);
+    tma_load_4d(base + kOffQ, &qmap, bar(kBarQ), 0, h, q0 + m * kBM, 0, policy);
+    tma_load_4d(base + kOffQ + kHalf, &qmap, bar(kBarQ), 64, h, q0 + m * kBM, 0, policy);
+    issue_k(0);
+    issue_v(0);
+    if (nk > 1) {
+      issue_k(1);
+      issue_v(1);
+    }
+    if (wait_or_abort(kBarQ, 0)) issue_s(0);
+  }
+
+  float m_run = -INFINITY, l_run = 0.f;
+  uint32_t sreg[32];
+  for (int j = 0; j < nk; ++j) {
+    __syncthreads();               // every exit decision is taken here, by all threads
+    if (*abort_flag) break;
+    if (tid == 0 && j + 1 < nk) issue_s(j + 1);
+    wait_or_abort(kBarS + (j & 1), (j >> 1) & 1);   // S_j in TMEM
+    tc::fence_after_sync();
+    if (tid == 0 && j + 2 < nk && !*abort_flag) issue_k(j + 2);  // S_j freed K stage j&1
+
+    // ---- pass 1: running max of row qi over keys 128j .. 128j+127 ----
+    const int key0 = j * kBN;
+    const bool full = key0 + kBN - 1 <= kmax;
+    const uint32_t s_addr = tmem + lane_base + kColS + (j & 1) * 128;
+    float mx = -INFINITY;
+#pragma unroll
+    for (int cb = 0; cb < 4; ++cb) {
+      tc::ld32(s_addr + cb * 32, sreg);
+      tc::wait_ld();
+#pragma unroll
+      for (int c = 0; c < 32; ++c) {
+        const int key = key0 + cb * 32 + c;
+        if (full || key <= kmax) mx = fmaxf(mx, __uint_as_float(sreg[c]) * p.scale_log2);
+      }
+    }
+    const float m_new = fmaxf(m_run, mx);
+    const float mu = m_new == -INFINITY ? 0.f : m_new;
+    const float alpha = fast_exp2(m_run - mu);
+    m_run = m_new;
+
+    // PV_{j-1} must be done before P, O and V stage (j-1)&1 are reused.
+    if (j > 0) {
+      wait_or_abort(kBarPV, (j - 1) & 1);
+      tc::fence_after_sync();
+      if (tid == 0 && j + 1 < nk && !*abort_flag) issue_v(j + 1);
+    }
+
+    // ---- pass 2: P = exp2(s - m) -> shared memory (K-major, 128-byte swizzle) ----
+    float rs = 0.f;
+    uint8_t *prow = base_ptr + kOffP + tid * 128;
+#pragma unroll
+    for (int cb = 0; cb < 4; ++cb) {
+      tc::ld32(s_addr + cb * 32, sreg);
+      tc::wait_ld();
+      uint32_t pk[16];
+#pragma unroll
+      for (int c = 0; c < 32; c += 2) {
+        const int key = key0 + cb * 32 + c;
+        const float a = (full || key <= kmax)
+                            ? fast_exp2(__uint_as_float(sreg[c]) * p.scale_log2 - mu) : 0.f;
+        const float b = (full || key + 1 <= kmax)
+                            ? fast_exp2(__uint_as_float(sreg[c + 1]) * p.scale_log2 - mu) : 0.f;
+        rs += a + b;
+        pk[c >> 1] = Pack<T>::two(a, b);
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int chunk = cb * 4 + i;  // 8 keys per 16-byte chunk
+        *reinterpret_cast<uint4 *>(prow + (chunk >> 3) * kHalf + (((chunk & 7) ^ (tid & 7)) << 4)) =
+            make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+      }
+    }
+    l_run = l_run * alpha + rs;
+
+    // rescale O when the running max moved for any row of this warp
+    if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+      const uint32_t o_addr = tmem + lane_base + kColO;
+#pragma unroll
+      for (int cb = 0; cb < 4; ++cb) {
+        tc::ld32(o_addr + cb * 32, sreg);
+        tc::wait_ld();
+#pragma unroll
+        for (int c = 0; c < 32; ++c) sreg[c] = __float_as_uint(__uint_as_float(sreg[c]) * alpha);
+        tc::st32(o_addr + cb * 32, sreg);
+      }
+      tc::wait_st();
+    }
+    // zero V rows past the sequence end in the last tile
+    if (key0 + kBN > k_len && wait_or_abort(kBarV + (j & 1), (j >> 1) & 1)) {
+      const int valid = k_len - key0;
+      uint8_t *vt = base_ptr + kOffV + (j & 1) * kTile;
+      for (int i = tid; i < (kBN - valid) * 16; i += 128) {
+        const int row = valid + (i >> 4), part = i & 15;
+        *reinterpret_cast<uint4 *>(vt + (part >> 3) * kHalf + row * 128 + (part & 7) * 16) =
+            make_uint4(0, 0, 0, 0);
+      }
+    }
+    fence_proxy_async_smem();
+    tc::fence_before_sync();
+    __syncthreads();
+    if (tid == 0 && !*abort_flag) {
+      tc::fence_after_sync();
+      if (wait_or_abort(kBarV + (j & 1), (j >> 1) & 1)) {
+        const uint32_t pa = base + kOffP, vb = base + kOffV + (j & 1) * kTile;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint64_t adesc =
+              tc::smem_desc_sw128(pa + (kk >> 2) * kHalf + (kk & 3) * 32, 16, 1024);
+#pragma unroll
+          for (int nh = 0; nh < 2; ++nh)
+            tc::mma_f16_ss(tmem + kColO + nh * 64, adesc,
+                           tc::smem_desc_sw128(vb + nh * kHalf + kk * 16 * 128, 1024, 1024),
+                           kIdescPV, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        tc::commit(bar(kBarPV));
+      }
+    }
+  }
+
+  // ---- epilogue: O / l -> out ----
+  __syncthreads();
+  const bool ok = !*abort_flag && wait_or_abort(kBarPV, (nk - 1) & 1);
+  tc::fence_after_sync();
+  if (__all_sync(0xffffffffu, ok)) {
+    const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+    const uint32_t o_addr = tmem + lane_base + kColO;
+#pragma unroll
+    for (int cblk = 0; cblk < 4; ++cblk) {
+      tc::ld32(o_addr + cblk * 32, sreg);
+      tc::wait_ld();
+      if (row_ok) {
+#pragma unroll
+        for (int c = 0; c < 32; c += 8) {
+          uint4 w;
+          w.x = Pack<T>::two(__uint_as_float(sreg[c]) * inv, __uint_as_float(sreg[c + 1]) * inv);
+          w.y = Pack<T>::two(__uint_as_float(sreg[c + 2]) * inv, __uint_as_float(sreg[c + 3]) * inv);
+          w.z = Pack<T>::two(__uint_as_float(sreg[c + 4]) * inv, __uint_as_float(sreg[c + 5]) * inv);
+          w.w = Pack<T>::two(__uint_as_float(sreg[c + 6]) * inv, __uint_as_float(sreg[c + 7]) * inv);
+          *reinterpret_cast<uint4 *>(orow + cblk * 32 + c) = w;
+        }
+      }
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) tc::tmem_dealloc(tmem, kTmemCols);
+}
+
+// ---- host side -------------------------------------------------------------
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+// 4-D map {dim 128, head, row, page} with a {64, 1, 128, 1} box, 128-byte swizzle.
+bool encode_map(CUtensorMap *map, const void *base, CUtensorMapDataType dt, uint64_t heads,
+                uint64_t head_stride, uint64_t rows, uint64_t row_stride, uint64_t pages,
+                uint64_t page_stride) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[4] = {kD, heads, rows, pages};
+  cuuint64_t strides[3] = {head_stride * 2, row_stride * 2, page_stride * 2};
+  cuuint32_t box[4] = {64, 1, 128, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  return fn(map, dt, 4, const_cast<void *>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <typename T>
+int launch(const Params &p, const CUtensorMap &qm, const CUtensorMap &km, const CUtensorMap &vm,
+           int rows, int max_q, cudaStream_t stream) {
+  static std::once_flag once;
+  static bool ok = false;
+  std::call_once(once, [] {
+    ok = cudaFuncSetAttribute(paged_prefill_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              kSmemBytes) == cudaSuccess;
+  });
+  if (!ok) return SLOKV_ERR_CUDA;
+  dim3 grid((max_q + kBM - 1) / kBM, p.hq, rows);
+  paged_prefill_kernel<T><<<grid, 128, kSmemBytes, stream>>>(qm, km, vm, p);
+  return cudaGetLastError() == cudaSuccess ? SLOKV_OK : SLOKV_ERR_CUDA;
+}
+
+}  // namespace prefill
+}  // namespace slokv
+
+extern "C" int slokv_paged_prefill(void *out, int64_t out_stride_t, int64_t out_stride_h,
+                                   const void *q, int64_t q_stride_t, int64_t q_stride_h,
+                                   int64_t q_rows, const void *k, const void *v,
+                                   int64_t kv_stride_t, int64_t v_stride_t, int64_t kv_rows,
+                                   int64_t k_block_stride, int64_t v_block_stride,
+                                   const int32_t *cu_seqlens_q, const int32_t *cu_seqlens_k,
+                                   int32_t num_rows, int32_t max_seqlen_q,
+                                   const int32_t *block_tables, int64_t block_table_stride,
+                                   int32_t max_blocks_per_seq, int32_t num_blocks,
+                                   int32_t block_size, int32_t num_q_heads, int32_t num_kv_heads,
+                                   int32_t head_dim, float softmax_scale, int32_t dtype,
+                                   uint32_t *dev_error, void *stream) {
+  using namespace slokv;
+  using namespace slokv::prefill;
+  if (num_rows < 0 || max_seqlen_q < 0 || num_q_heads <= 0 || num_kv_heads <= 0)
+    return SLOKV_ERR_INVALID_ARG;
+  if (num_rows == 0 || max_seqlen_q == 0) return SLOKV_OK;
+  if (head_dim != kD) return SLOKV_ERR_UNSUPPORTED;
+  if (dtype != SLOKV_DTYPE_BF16 && dtype != SLOKV_DTYPE_F16) return SLOKV_ERR_UNSUPPORTED;
+  if (num_q_heads % num_kv_heads) return SLOKV_ERR_INVALID_ARG;
+  if (!out || !q || !k || !v || !cu_seqlens_q || !cu_seqlens_k || q_rows <= 0)
+    return SLOKV_ERR_INVALID_ARG;
+  const bool paged = block_tables != nullptr;
+  if (paged && (block_size <= 0 || block_size % kBN || num_blocks <= 0 || max_blocks_per_seq <= 0))
+    return paged && block_size % kBN ? SLOKV_ERR_UNSUPPORTED : SLOKV_ERR_INVALID_ARG;
+  if (!paged && kv_rows <= 0) return SLOKV_ERR_INVALID_ARG;
+  // TMA: 16-byte aligned bases and strides; 16-byte output stores.
+  const uint64_t bits = reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
+                        reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(out);
+  if (bits & 15u) return SLOKV_ERR_ALIGNMENT;
+  if (((q_stride_t | q_stride_h | out_stride_t | out_stride_h) * 2) & 15) return SLOKV_ERR_ALIGNMENT;
+  if (paged ? (((k_block_stride | v_block_stride) * 2) & 15) : (((kv_stride_t | v_stride_t) * 2) & 15))
+    return SLOKV_ERR_ALIGNMENT;
+
+  const CUtensorMapDataType dt =
+      dtype == SLOKV_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap qm, km, vm;
+  const uint64_t hkv = static_cast<uint64_t>(num_kv_heads);
+  bool ok = encode_map(&qm, q, dt, num_q_heads, q_stride_h, q_rows, q_stride_t, 1,
+                       q_rows * q_stride_t);
+  if (paged) {
+    ok = ok && encode_map(&km, k, dt, hkv, kD, block_size, hkv * kD, num_blocks, k_block_stride) &&
+         encode_map(&vm, v, dt, hkv, kD, block_size, hkv * kD, num_blocks, v_block_stride);
+  } else {
+    ok = ok && encode_map(&km, k, dt, hkv, kD, kv_rows, kv_stride_t, 1, kv_rows * kv_stride_t) &&
+         encode_map(&vm, v, dt, hkv, kD, kv_rows, v_stride_t, 1, kv_rows * v_stride_t);
+  }
+  if (!ok) return SLOKV_ERR_CUDA;
+
+  Params p;
+  p.out = out;
+  p.out_st = out_stride_t;
+  p.out_sh = out_stride_h;
+  p.cu_q = cu_seqlens_q;
+  p.cu_k = cu_seqlens_k;
+  p.block_tables = block_tables;
+  p.bt_stride = block_table_stride;
+  p.max_blocks = max_blocks_per_seq;
+  p.num_blocks = num_blocks;
+  p.block_size = block_size;
+  p.hq = num_q_heads;
+  p.hkv = num_kv_heads;
+  p.group = num_q_heads / num_kv_heads;
+  p.scale_log2 = softmax_scale * 1.4426950408889634f;
+  p.err = dev_error;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return dtype == SLOKV_DTYPE_BF16
+             ? launch<__nv_bfloat16>(p, qm, km, vm, num_rows, max_seqlen_q, st)
+             : launch<__half>(p, qm, km, vm, num_rows, max_seqlen_q, st);
+}

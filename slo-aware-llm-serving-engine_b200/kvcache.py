@@ -12,6 +12,10 @@ called eagerly at the largest geometry.
                            nanovllm/layers/mixed_attention.py:117-121
   kv_block_copy / gather / scatter
                            page copy of diagnostics/online_token_replay/tensors.py:34-43
+  store_kvcache_fp8 / flash_attn_with_kvcache_fp8
+                           the same two calls over an FP8-E4M3 pool with per-(block,
+                           kv-head) scales (the reference's E4M3 codec,
+                           benchmarks/v0/probe_quant_support.py:24-56, applied to KV)
 """
 from __future__ import annotations
 
@@ -118,6 +122,116 @@ def flash_attn_with_kvcache(q: torch.Tensor, k_cache: torch.Tensor, v_cache: tor
     return out
 
 
+# ---------------------------------------------------------------------------
+# FP8-E4M3 KV cache (per-(block, kv-head) fp32 scales; contract in include/slokv.h)
+# ---------------------------------------------------------------------------
+
+FP8_DTYPES = (torch.uint8,) + ((torch.float8_e4m3fn,) if hasattr(torch, "float8_e4m3fn") else ())
+
+
+def is_fp8_cache(cache: torch.Tensor) -> bool:
+    return cache.dtype in FP8_DTYPES
+
+
+def store_kvcache_fp8(key: torch.Tensor, value: torch.Tensor, k_codes: torch.Tensor,
+                      v_codes: torch.Tensor, k_scale: torch.Tensor, v_scale: torch.Tensor,
+                      slot_mapping: torch.Tensor) -> None:
+    """Quantising store into the FP8 pool (store_kvcache's counterpart).
+
+    k_codes/v_codes: [num_blocks, block_size, Hkv, D] uint8 (or float8_e4m3fn);
+    k_scale/v_scale: [num_blocks, Hkv] fp32, zero for freshly assigned blocks.
+    The new tokens of one block must be adjacent in slot_mapping with
+    consecutive offsets (the engine's decode and prefill layouts are).
+    """
+    N, num_heads, head_dim = key.shape
+    assert key.stride(-1) == 1 and value.stride(-1) == 1
+    assert key.stride(1) == head_dim and value.stride(1) == head_dim
+    assert slot_mapping.numel() == N
+    dev = require_cuda(key, value, k_codes, v_codes, k_scale, v_scale, slot_mapping)
+    NB, bs, Hkv, D = k_codes.shape
+    if (Hkv, D) != (num_heads, head_dim) or v_codes.shape != k_codes.shape:
+        raise SlokvError("FP8 pool geometry differs from key/value")
+    for name, c in (("k_codes", k_codes), ("v_codes", v_codes)):
+        if not is_fp8_cache(c) or not c.is_contiguous():
+            raise SlokvError(f"{name} must be a contiguous uint8/float8_e4m3fn pool")
+    for name, sc in (("k_scale", k_scale), ("v_scale", v_scale)):
+        if sc.dtype != torch.float32 or tuple(sc.shape) != (NB, Hkv) or not sc.is_contiguous():
+            raise SlokvError(f"{name} must be contiguous fp32 [num_blocks, num_kv_heads]")
+    _i32_contig("slot_mapping", slot_mapping)
+    err = buffers.error_word(dev)
+    check(lib().slokv_kv_append_fp8(
+        key.data_ptr(), key.stride(0), value.data_ptr(), value.stride(0),
+        k_codes.data_ptr(), v_codes.data_ptr(), k_scale.data_ptr(), v_scale.data_ptr(),
+        slot_mapping.data_ptr(), N, Hkv, D, bs, NB, _lib.dtype_code(key.dtype),
+        err.data_ptr(), stream_ptr(dev)), "kv_append_fp8")
+
+
+def flash_attn_with_kvcache_fp8(q: torch.Tensor, k_codes: torch.Tensor, v_codes: torch.Tensor,
+                                k_scale: torch.Tensor, v_scale: torch.Tensor,
+                                cache_seqlens: torch.Tensor, block_table: torch.Tensor,
+                                softmax_scale: float | None = None, causal: bool = True,
+                                out: torch.Tensor | None = None) -> torch.Tensor:
+    """Paged decode over the FP8 pool, dequantisation fused into the tile load."""
+    if q.dim() != 4 or q.shape[1] != 1:
+        raise SlokvError("paged decode expects q of shape [batch, 1, heads, head_dim]")
+    B, _, Hq, D = q.shape
+    NB, block_size, Hkv, Dk = k_codes.shape
+    if v_codes.shape != k_codes.shape or Dk != D:
+        raise SlokvError("FP8 pool shape mismatch with q")
+    for name, c in (("k_codes", k_codes), ("v_codes", v_codes)):
+        if not is_fp8_cache(c) or c.stride(3) != 1 or c.stride(2) != D or c.stride(1) != Hkv * D:
+            raise SlokvError(f"{name} must be an FP8 pool with contiguous blocks")
+    for name, sc in (("k_scale", k_scale), ("v_scale", v_scale)):
+        if sc.dtype != torch.float32 or tuple(sc.shape) != (NB, Hkv) or not sc.is_contiguous():
+            raise SlokvError(f"{name} must be contiguous fp32 [num_blocks, num_kv_heads]")
+    if q.stride(-1) != 1:
+        raise SlokvError("q must have a contiguous last dimension")
+    dev = require_cuda(q, k_codes, v_codes, k_scale, v_scale, cache_seqlens, block_table)
+    _i32_contig("cache_seqlens", cache_seqlens)
+    if block_table.dtype != torch.int32 or block_table.stride(-1) != 1:
+        raise SlokvError("block_table must be int32 with a contiguous last dimension")
+    scale = float(softmax_scale) if softmax_scale is not None else D ** -0.5
+    if out is None:
+        out = torch.empty(B, 1, Hq, D, dtype=q.dtype, device=q.device)
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    nbytes = lib().slokv_paged_decode_fp8_workspace_bytes(idx, Hq, Hkv, D)
+    if nbytes == 0:
+        raise SlokvError("unsupported FP8 decode geometry")
+    ws = buffers.workspace(dev, f"decode_fp8/{Hq // Hkv}/{D}", nbytes)
+    err = buffers.error_word(dev)
+    check(lib().slokv_paged_decode_fp8(
+        out.data_ptr(), out.stride(0), out.stride(2), q.data_ptr(), q.stride(0), q.stride(2),
+        k_codes.data_ptr(), v_codes.data_ptr(), k_codes.stride(0), v_codes.stride(0),
+        k_scale.data_ptr(), v_scale.data_ptr(), NB, block_size, Hq, Hkv, D,
+        block_table.data_ptr(), block_table.stride(0), block_table.shape[1],
+        cache_seqlens.data_ptr(), B, scale, _lib.dtype_code(q.dtype),
+        ws.data_ptr(), ws.numel(), err.data_ptr(), stream_ptr(dev)), "paged_decode_fp8")
+    return out
+
+
+def e4m3_encode(x: torch.Tensor) -> torch.Tensor:
+    """E4M3FN codes (uint8) of a CUDA fp32 tensor: RNE, ties to even, saturate at 448."""
+    dev = require_cuda(x)
+    if x.dtype != torch.float32 or not x.is_contiguous():
+        raise SlokvError("e4m3_encode expects a contiguous fp32 tensor")
+    codes = torch.empty(x.shape, dtype=torch.uint8, device=x.device)
+    check(lib().slokv_fp8_e4m3_encode(x.data_ptr(), codes.data_ptr(), x.numel(),
+                                      buffers.error_word(dev).data_ptr(), stream_ptr(dev)),
+          "fp8_e4m3_encode")
+    return codes
+
+
+def e4m3_decode(codes: torch.Tensor) -> torch.Tensor:
+    """fp32 values of E4M3FN codes (uint8 CUDA tensor)."""
+    dev = require_cuda(codes)
+    if codes.dtype not in FP8_DTYPES or not codes.is_contiguous():
+        raise SlokvError("e4m3_decode expects a contiguous uint8 tensor")
+    x = torch.empty(codes.shape, dtype=torch.float32, device=codes.device)
+    check(lib().slokv_fp8_e4m3_decode(codes.data_ptr(), x.data_ptr(), codes.numel(),
+                                      stream_ptr(dev)), "fp8_e4m3_decode")
+    return x
+
+
 def _pool_planes(pool: torch.Tensor):
     """View a [2, L, NB, ...] pool (or any [P0, P1, NB, ...]) as planes x pages."""
     if pool.dim() < 4:
@@ -188,5 +302,56 @@ def kv_block_scatter(saved: torch.Tensor, pool: torch.Tensor, ids: torch.Tensor)
 
 def flash_attn_varlen_func(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k,
                            softmax_scale=None, causal=True, block_table=None, out=None):
-    """Causal varlen (prefill) attention; the sm_100a prefill kernel is not built yet."""
-    raise SlokvError("paged prefill attention is not available in this build")
+    """Causal varlen attention with the flash_attn_varlen_func calling convention.
+
+    q: [Tq, Hq, D].  Without block_table, k/v are [Tk, Hkv, D] rows addressed by
+    cu_seqlens_k (v may be a strided view of the fused QKV output); with
+    block_table, k/v are the paged caches [num_blocks, block_size, Hkv, D] and
+    row r's keys are gathered through block_table[r].  Query i of row r sees
+    keys 0 .. k_len - q_len + i (bottom-right aligned).  Returns [Tq, Hq, D].
+    """
+    if not causal:
+        raise SlokvError("only causal varlen attention is implemented (the engine's only use)")
+    if q.dim() != 3:
+        raise SlokvError("q must be [tokens, heads, head_dim]")
+    Tq, Hq, D = q.shape
+    dev = require_cuda(q, k, v, cu_seqlens_q, cu_seqlens_k, block_table)
+    _i32_contig("cu_seqlens_q", cu_seqlens_q)
+    _i32_contig("cu_seqlens_k", cu_seqlens_k)
+    if cu_seqlens_k.numel() != cu_seqlens_q.numel():
+        raise SlokvError("cu_seqlens_q and cu_seqlens_k differ in length")
+    if q.dtype != k.dtype or v.dtype != k.dtype:
+        raise SlokvError("q, k and v dtypes differ")
+    if q.stride(-1) != 1 or k.stride(-1) != 1 or v.stride(-1) != 1:
+        raise SlokvError("q, k and v need a contiguous last dimension")
+    rows = cu_seqlens_q.numel() - 1
+    scale = float(softmax_scale) if softmax_scale is not None else D ** -0.5
+    if out is None:
+        out = torch.empty(Tq, Hq, D, dtype=q.dtype, device=q.device)
+    if block_table is not None:
+        NB, bs, Hkv, Dk = k.shape
+        if v.shape != k.shape or Dk != D:
+            raise SlokvError("k_cache/v_cache shape mismatch with q")
+        for name, c in (("k_cache", k), ("v_cache", v)):
+            if c.stride(2) != D or c.stride(1) != Hkv * D:
+                raise SlokvError(f"{name} blocks must be contiguous [block_size, Hkv, D]")
+        if block_table.dtype != torch.int32 or block_table.stride(-1) != 1:
+            raise SlokvError("block_table must be int32 with a contiguous last dimension")
+        args = (k.data_ptr(), v.data_ptr(), 0, 0, 0, k.stride(0), v.stride(0),
+                cu_seqlens_q.data_ptr(), cu_seqlens_k.data_ptr(), rows, int(max_seqlen_q),
+                block_table.data_ptr(), block_table.stride(0), block_table.shape[1], NB, bs)
+    else:
+        Tk, Hkv, Dk = k.shape
+        if v.shape != k.shape or Dk != D or k.stride(1) != D or v.stride(1) != D:
+            raise SlokvError("k/v must be [tokens, Hkv, D] with contiguous heads")
+        args = (k.data_ptr(), v.data_ptr(), k.stride(0), v.stride(0), Tk, 0, 0,
+                cu_seqlens_q.data_ptr(), cu_seqlens_k.data_ptr(), rows, int(max_seqlen_q),
+                None, 0, 0, 0, 0)
+    if Tq == 0 or rows == 0:
+        return out
+    err = buffers.error_word(dev)
+    check(lib().slokv_paged_prefill(
+        out.data_ptr(), out.stride(0), out.stride(1), q.data_ptr(), q.stride(0), q.stride(1), Tq,
+        *args, Hq, Hkv, D, scale, _lib.dtype_code(q.dtype), err.data_ptr(), stream_ptr(dev)),
+        "paged_prefill")
+    return out

@@ -9,7 +9,8 @@ attention over the paged cache, or the mixed prefill/decode path.
 import torch
 from torch import nn
 
-from ..kvcache import flash_attn_varlen_func, flash_attn_with_kvcache, store_kvcache
+from ..kvcache import (flash_attn_varlen_func, flash_attn_with_kvcache,
+                       flash_attn_with_kvcache_fp8, store_kvcache, store_kvcache_fp8)
 from ..utils.context import get_context
 
 __all__ = ["Attention", "store_kvcache"]
@@ -24,10 +25,15 @@ class Attention(nn.Module):
         self.scale = scale
         self.num_kv_heads = num_kv_heads
         self.k_cache = self.v_cache = torch.tensor([])
+        # FP8-E4M3 pool: k_cache/v_cache hold uint8 codes and these hold the fp32
+        # per-(block, kv-head) scales; None for a bf16/f16 pool.
+        self.k_scale = self.v_scale = None
 
     def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor):
         context = get_context()
         k_cache, v_cache = self.k_cache, self.v_cache
+        if self.k_scale is not None:
+            return self._forward_fp8(q, k, v, context)
         if context.mixed is not None:
             from .mixed_attention import forward_mixed
             return forward_mixed(q, k, v, k_cache, v_cache, context, self.scale, store_kvcache)
@@ -47,3 +53,14 @@ class Attention(nn.Module):
                                        cache_seqlens=context.context_lens,
                                        block_table=context.block_tables,
                                        softmax_scale=self.scale, causal=True)
+
+    def _forward_fp8(self, q, k, v, context):
+        if context.mixed is not None or context.is_prefill:
+            raise RuntimeError("the FP8 KV pool is supported on the decode path only")
+        store_kvcache_fp8(k, v, self.k_cache, self.v_cache, self.k_scale, self.v_scale,
+                          context.slot_mapping)
+        return flash_attn_with_kvcache_fp8(q.unsqueeze(1), self.k_cache, self.v_cache,
+                                           self.k_scale, self.v_scale,
+                                           cache_seqlens=context.context_lens,
+                                           block_table=context.block_tables,
+                                           softmax_scale=self.scale, causal=True)

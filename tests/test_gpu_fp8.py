@@ -1,0 +1,200 @@
+"""GPU parity of the FP8-E4M3 KV path: codec and quantising append bit-exact
+against the oracle (whose encoder is pinned to the reference's), decode
+attention over the FP8 pool within the bf16 attention tolerance of the fp32
+oracle on the dequantised pool, and its error against the bf16 cache reported.
+
+Tolerance of the FP8 decode parity: the kernel and the oracle see identical
+codes and scales, so the remaining difference is arithmetic plus the rounding of
+the output to bf16.  Config-4 data carries x20 outliers, so outputs reach
+|o| ~ 60 where one bf16 ulp is 0.25; the bar is therefore
+|err| <= 2e-2 + 2^-7 |expected| (two bf16 ulps relative) per element and
+mean |err| <= 2e-3.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import kv_oracle as O
+from tests.golden import scenarios as S
+from tests.golden.detgen import det_ints, det_normal, det_outlier_mask, det_perm
+
+pytestmark = pytest.mark.gpu
+
+MAX_TOL, MEAN_TOL, REL_TOL = 2e-2, 2e-3, 2.0 ** -7
+
+
+def assert_fp8_close(actual, expected):
+    a = actual.float().cpu().reshape(expected.shape)
+    assert torch.isfinite(a).all()
+    err = (a - expected).abs()
+    bound = MAX_TOL + REL_TOL * expected.abs()
+    worst = (err - bound).max().item()
+    assert worst <= 0, f"max excess {worst:.3e} (max err {err.max().item():.3e})"
+    assert err.mean().item() <= MEAN_TOL, f"mean {err.mean().item():.3e}"
+
+
+def kv_values(seed, shape, outlier_frac=0.01):
+    """N(0,1)-like bf16 values with 1% outliers x20."""
+    x = det_normal(seed, shape)
+    x = np.where(det_outlier_mask(seed + 1, shape, outlier_frac), x * np.float32(20.0), x)
+    return torch.from_numpy(x.astype(np.float32)).bfloat16()
+
+
+def test_encoder_matches_reference_codes(pkg, golden):
+    _, arrays = golden
+    vals = torch.from_numpy(S.e4m3_probe_values())
+    codes = pkg.e4m3_encode(vals.cuda()).cpu().numpy()
+    np.testing.assert_array_equal(codes, arrays["e4m3/codes"])
+    assert pkg.read_device_errors() == 0
+
+
+def test_decoder_all_codes(pkg):
+    codes = torch.arange(256, dtype=torch.int32).to(torch.uint8)
+    vals = pkg.e4m3_decode(codes.cuda()).cpu().numpy()
+    lut = O.DECODE_LUT
+    finite = np.isfinite(lut)
+    np.testing.assert_array_equal(vals[finite], lut[finite])
+    assert np.isnan(vals[~finite]).all() and (~finite).sum() == 2
+
+
+def test_encoder_flags_nonfinite(pkg):
+    x = torch.tensor([1.0, float("nan"), float("inf"), -2.0], device="cuda")
+    codes = pkg.e4m3_encode(x).cpu().tolist()
+    assert codes[0] == O.encode_e4m3fn(1.0) and codes[3] == O.encode_e4m3fn(-2.0)
+    assert pkg.read_device_errors() & pkg._lib.DEVERR_NONFINITE
+
+
+def _pools(NB, bs=256, H=8, D=128):
+    return [torch.zeros(NB, bs, H, D, dtype=torch.uint8) for _ in range(2)] + \
+           [torch.zeros(NB, H, dtype=torch.float32) for _ in range(2)]
+
+
+def _gpu(ts):
+    return [t.cuda() for t in ts]
+
+
+def _assert_pool_equal(dev, ref):
+    for d, r in zip(dev, ref):
+        assert torch.equal(d.cpu(), r), "FP8 pool differs from the oracle"
+
+
+def test_prefill_runs_then_decode_appends_bit_exact(pkg):
+    """Prefill chunks that start mid-block and cross block boundaries, then
+    step-by-step decode appends (re-encoding when an outlier raises a block's
+    amax), with padding slots; codes and scales bit-exact after every call."""
+    H, D, bs, NB = 8, 128, 256, 24
+    ref = _pools(NB, H=H)
+    dev = _gpu(ref)
+    tables = [det_perm(70, NB)[:6].tolist(), det_perm(70, NB)[6:12].tolist()]
+    hist = [100, 300]
+    # prefill: rows 0 and 1 write positions [0, hist)
+    slots = [tables[r][p // bs] * bs + p % bs for r in range(2) for p in range(hist[r])]
+    x = kv_values(71, (len(slots), H, D))
+    y = kv_values(73, (len(slots), H, D))
+    sl = torch.tensor(slots, dtype=torch.int32)
+    O.fp8_append(x, y, *ref, sl)
+    pkg.store_kvcache_fp8(x.cuda(), y.cuda(), *dev, sl.cuda())
+    _assert_pool_equal(dev, ref)
+    # decode: one token per row per step, a padding row in between
+    for step in range(40):
+        pos = [hist[0] + step, hist[1] + step]
+        s = [tables[0][pos[0] // bs] * bs + pos[0] % bs, -1,
+             tables[1][pos[1] // bs] * bs + pos[1] % bs]
+        xs = kv_values(1000 + step, (3, H, D), outlier_frac=0.02)
+        ys = kv_values(2000 + step, (3, H, D), outlier_frac=0.02)
+        st = torch.tensor(s, dtype=torch.int32)
+        O.fp8_append(xs, ys, *ref, st)
+        pkg.store_kvcache_fp8(xs.cuda(), ys.cuda(), *dev, st.cuda())
+        if step % 8 == 7:
+            _assert_pool_equal(dev, ref)
+    _assert_pool_equal(dev, ref)
+    assert pkg.read_device_errors() == 0
+
+
+def _fp8_case(seed, B, lo, hi, Hq=32, Hkv=8, D=128, bs=256):
+    lens = det_ints(seed, B, lo, hi).tolist()
+    pages = [(L + bs - 1) // bs for L in lens]
+    NB = sum(pages) + 2
+    W = max(pages)
+    perm = det_perm(seed, NB).tolist()
+    tables, cur = [], 0
+    for n in pages:
+        tables.append(perm[cur:cur + n] + [-1] * (W - n))
+        cur += n
+    slots = [tables[b][p // bs] * bs + p % bs for b, L in enumerate(lens) for p in range(L)]
+    k = kv_values(seed + 1, (len(slots), Hkv, D))
+    v = kv_values(seed + 3, (len(slots), Hkv, D))
+    q = torch.from_numpy(det_normal(seed + 5, (B, Hq, D))).bfloat16()
+    return dict(lens=torch.tensor(lens, dtype=torch.int32), tables=torch.tensor(tables, dtype=torch.int32),
+                slots=torch.tensor(slots, dtype=torch.int32), k=k, v=v, q=q, NB=NB, Hkv=Hkv, D=D, bs=bs)
+
+
+@pytest.mark.parametrize("B,lo,hi,seed", [(6, 1024, 8192, 3000),   # config 4 distribution
+                                          (20, 1, 700, 3001),       # tails, short rows
+                                          (3, 9000, 12000, 3002)])  # long rows: many splits
+def test_fp8_decode_matches_oracle(pkg, B, lo, hi, seed):
+    c = _fp8_case(seed, B, lo, hi)
+    ref = _pools(c["NB"], H=c["Hkv"])
+    O.fp8_append(c["k"], c["v"], *ref, c["slots"])
+    dev = _gpu(_pools(c["NB"], H=c["Hkv"]))
+    pkg.store_kvcache_fp8(c["k"].cuda(), c["v"].cuda(), *dev, c["slots"].cuda())
+    _assert_pool_equal(dev, ref)
+    scale = 128 ** -0.5
+    out = pkg.flash_attn_with_kvcache_fp8(c["q"].cuda().unsqueeze(1), *dev,
+                                          cache_seqlens=c["lens"].cuda(),
+                                          block_table=c["tables"].cuda(), softmax_scale=scale)
+    torch.cuda.synchronize()
+    expect = O.fp8_decode(c["q"].unsqueeze(1), *ref, c["lens"], c["tables"], scale)
+    assert_fp8_close(out, expect)
+    assert pkg.read_device_errors() == 0
+
+
+def test_fp8_vs_bf16_cache_error_is_reported(pkg, capsys):
+    """Attention over the FP8 cache against attention over the bf16 cache of the
+    same K/V: the quantisation error the FP8 path trades for bandwidth.  The
+    kernel's difference must match the oracle's (dequantised vs bf16 values, both
+    in fp32): the error is the format's, not the kernel's."""
+    c = _fp8_case(3100, 8, 1024, 8192)
+    dev = _gpu(_pools(c["NB"], H=c["Hkv"]))
+    pkg.store_kvcache_fp8(c["k"].cuda(), c["v"].cuda(), *dev, c["slots"].cuda())
+    kc = torch.zeros(c["NB"], c["bs"], c["Hkv"], c["D"], dtype=torch.bfloat16, device="cuda")
+    vc = torch.zeros_like(kc)
+    pkg.store_kvcache(c["k"].cuda(), c["v"].cuda(), kc, vc, c["slots"].cuda())
+    qd, ld, td = c["q"].cuda().unsqueeze(1), c["lens"].cuda(), c["tables"].cuda()
+    o8 = pkg.flash_attn_with_kvcache_fp8(qd, *dev, cache_seqlens=ld, block_table=td)
+    o16 = pkg.flash_attn_with_kvcache(qd, kc, vc, cache_seqlens=ld, block_table=td)
+    k_err = (o8.float() - o16.float()).abs().cpu()
+    e16 = O.decode(c["q"].unsqueeze(1), kc.cpu(), vc.cpu(), c["lens"], c["tables"], 128 ** -0.5)
+    e8 = O.fp8_decode(c["q"].unsqueeze(1), *[t.cpu() for t in dev], c["lens"], c["tables"],
+                      128 ** -0.5)
+    o_err = (e8 - e16).abs()
+    with capsys.disabled():
+        print(f"\nFP8 vs bf16 cache attention (config 4 data, x20 outliers): kernel max "
+              f"{k_err.max().item():.3e} mean {k_err.mean().item():.3e}; oracle max "
+              f"{o_err.max().item():.3e} mean {o_err.mean().item():.3e}; "
+              f"mean |o| {e16.abs().mean().item():.3e}")
+    assert torch.isfinite(o8.float()).all()
+    assert abs(k_err.mean().item() - o_err.mean().item()) <= 0.1 * o_err.mean().item() + 2e-3
+
+
+def test_attention_module_fp8_decode(pkg):
+    """Attention.forward over an FP8 pool (k_scale/v_scale bound) = store + decode."""
+    c = _fp8_case(3200, 4, 10, 600)
+    dev = _gpu(_pools(c["NB"], H=c["Hkv"]))
+    # history = all but the last token of every row; the step appends the last token
+    last = torch.cumsum(c["lens"].long(), 0) - 1
+    keep = torch.ones(c["slots"].numel(), dtype=torch.bool)
+    keep[last] = False
+    pkg.store_kvcache_fp8(c["k"][keep].cuda(), c["v"][keep].cuda(), *dev, c["slots"][keep].cuda())
+    attn = pkg.Attention(32, 128, 128 ** -0.5, 8)
+    attn.k_cache, attn.v_cache, attn.k_scale, attn.v_scale = dev
+    pkg.set_context(False, slot_mapping=c["slots"][last].cuda(), context_lens=c["lens"].cuda(),
+                    block_tables=c["tables"].cuda())
+    out = attn(c["q"].cuda(), c["k"][last].cuda(), c["v"][last].cuda())
+    pkg.reset_context()
+    ref = _pools(c["NB"], H=c["Hkv"])
+    O.fp8_append(c["k"][keep], c["v"][keep], *ref, c["slots"][keep])
+    O.fp8_append(c["k"][last], c["v"][last], *ref, c["slots"][last])
+    _assert_pool_equal(dev, ref)
+    expect = O.fp8_decode(c["q"].unsqueeze(1), *ref, c["lens"], c["tables"], 128 ** -0.5)
+    assert_fp8_close(out, expect)
