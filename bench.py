@@ -365,7 +365,9 @@ def run_ours(args):
                            "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"],
                            "ms_per_step": round(e2e_ms, 3),
                            "path": "Attention.forward + Context per layer (store_kvcache + "
-                                   "flash_attn_with_kvcache), pinned host buffers"}
+                                   "flash_attn_with_kvcache), eager, from pinned host buffers; "
+                                   "H2D / D2H on side streams pipelined against neighbouring "
+                                   "layers"}
         if n == 1 and not args.no_cpu_baseline and not wl["fp8"]:
             line["cpu_baseline"] = cpu_baseline(args, sample_seconds=args.cpu_seconds)
         print(json.dumps(line), flush=True)
@@ -378,7 +380,12 @@ def run_ours(args):
 def run_e2e(args, pkg, wl, device, barrier):
     """The same decode step driven through the public Attention/Context API from
     pinned host buffers: per step the metadata and every layer's q/k/v go
-    host->device and every layer's attention output comes back device->host."""
+    host->device and every layer's attention output comes back device->host.
+
+    The copies run on their own streams, pipelined against the attention of
+    neighbouring layers as a serving loop would: H2D of layer l+1 (stream h2d)
+    overlaps layer l's kernels, D2H of layer l's output (stream d2h) overlaps
+    layer l+1; device input buffers alternate between two sets across steps."""
     L, B = args.layers, wl["B"]
     attn = []
     for l in range(L):
@@ -398,30 +405,56 @@ def run_e2e(args, pkg, wl, device, barrier):
         h_q[0].numel() + h_k[0].numel() + h_v[0].numel()) * 2
     d2h = L * h_out[0].numel() * 2
 
-    def one_step():
-        slots = h_slots.to(device, non_blocking=True)
-        lens = h_lens.to(device, non_blocking=True)
-        tables = h_tables.to(device, non_blocking=True)
-        pkg.set_context(False, slot_mapping=slots, context_lens=lens, block_tables=tables)
+    main = torch.cuda.current_stream(device)
+    s_in, s_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    sets = [dict(q=torch.empty_like(wl["q"]), k=torch.empty_like(wl["knew"]),
+                 v=torch.empty_like(wl["vnew"]), slots=torch.empty_like(wl["slots"]),
+                 lens=torch.empty_like(wl["lens"]), tables=torch.empty_like(wl["tables"]),
+                 free=torch.cuda.Event(), meta=torch.cuda.Event(),
+                 inp=[torch.cuda.Event() for _ in range(L)]) for _ in range(2)]
+    for st in sets:
+        st["free"].record(main)
+    done = [torch.cuda.Event() for _ in range(L)]
+
+    def one_step(i):
+        st = sets[i & 1]
+        with torch.cuda.stream(s_in):
+            s_in.wait_event(st["free"])          # the previous user of this set finished
+            st["slots"].copy_(h_slots, non_blocking=True)
+            st["lens"].copy_(h_lens, non_blocking=True)
+            st["tables"].copy_(h_tables, non_blocking=True)
+            st["meta"].record(s_in)
+            for l in range(L):
+                st["q"][l].copy_(h_q[l], non_blocking=True)
+                st["k"][l].copy_(h_k[l], non_blocking=True)
+                st["v"][l].copy_(h_v[l], non_blocking=True)
+                st["inp"][l].record(s_in)
+        main.wait_event(st["meta"])
+        pkg.set_context(False, slot_mapping=st["slots"], context_lens=st["lens"],
+                        block_tables=st["tables"])
         for l in range(L):
-            q = h_q[l].to(device, non_blocking=True)
-            k = h_k[l].to(device, non_blocking=True)
-            v = h_v[l].to(device, non_blocking=True)
-            o = attn[l](q, k, v)
-            h_out[l].copy_(o.view(B, wl["hq"], D), non_blocking=True)
+            main.wait_event(st["inp"][l])
+            o = attn[l](st["q"][l], st["k"][l], st["v"][l])
+            done[l].record(main)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(done[l])
+                h_out[l].copy_(o.view(B, wl["hq"], D), non_blocking=True)
+                o.record_stream(s_out)
+        st["free"].record(main)
         pkg.reset_context()
 
-    for _ in range(max(1, args.warmup)):
-        one_step()
+    for i in range(max(1, args.warmup)):
+        one_step(i)
     torch.cuda.synchronize()
     steps = max(2, args.steps // 2)
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     torch.cuda.synchronize()
-    s.record()
-    for _ in range(steps):
-        one_step()
-    e.record()
+    s.record(main)
+    for i in range(steps):
+        one_step(i)
+    main.wait_stream(s_out)                      # the last outputs are on the host
+    e.record(main)
     torch.cuda.synchronize()
     barrier()
     return {"ms": s.elapsed_time(e) / steps, "h2d": h2d, "d2h": d2h}
@@ -475,6 +508,183 @@ def cpu_baseline(args, sample_seconds=10.0):
                       f"tok/s = batch / (36 x median layer time {t * 1e3:.1f} ms)"}
 
 
+# ----------------------------------------------------------------------------
+# config 3: mixed prefill / decode step (reported separately, not the headline)
+# ----------------------------------------------------------------------------
+
+MIXED_DECODE, MIXED_CHUNK, MIXED_PREFIX = 64, 2048, (0, 1024, 3072)
+
+
+def measured_tensor_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    except Exception:
+        return 1590.0, "fallback"
+
+
+def run_mixed(args):
+    """36 layers of forward_mixed over 64 decode rows + 3 prefill chunks."""
+    torch.cuda.set_device(0)
+    device = torch.device("cuda", 0)
+    pkg = importlib.import_module("slo-aware-llm-serving-engine_b200")
+    L = args.layers
+    gen = torch.Generator().manual_seed(1)
+    dec_lens = torch.randint(256, 4097, (MIXED_DECODE,), generator=gen)
+    rows = [(int(n) - 1, 1) for n in dec_lens] + [(h, MIXED_CHUNK) for h in MIXED_PREFIX]
+    pages = [(h + n + BS - 1) // BS for h, n in rows]
+    W = max(pages)
+    block_bytes = 2 * L * BS * HKV * D * 2
+    free, total = torch.cuda.mem_get_info(device)
+    NB = args.pool_blocks or min(int(POOL_FRAC * total) // block_bytes,
+                                 int((free - (8 << 30)) // block_bytes))
+    perm = torch.randperm(NB, generator=gen)[:sum(pages)].tolist()
+    tables, cur = [], 0
+    for n in pages:
+        tables.append(perm[cur:cur + n] + [-1] * (W - n))
+        cur += n
+    slots = [t[pos // BS] * BS + pos % BS for t, (h, n) in zip(tables, rows)
+             for pos in range(h, h + n)]
+    T = len(slots)
+    kv = torch.empty(2, L, NB, BS, HKV, D, dtype=torch.bfloat16, device=device)
+    g = torch.Generator(device=device).manual_seed(77)
+    for i in range(2):
+        for l in range(L):
+            kv[i, l].normal_(0.0, 0.5, generator=g)
+    q = torch.randn(L, T, HQ, D, device=device, generator=g).bfloat16()
+    k = (torch.randn(L, T, HKV, D, device=device, generator=g) * 0.5).bfloat16()
+    v = (torch.randn(L, T, HKV, D, device=device, generator=g) * 0.5).bfloat16()
+    i32 = lambda x: torch.tensor(x, dtype=torch.int32, device=device)
+    cu_q, cu_k = [0], [0]
+    for h, n in rows[MIXED_DECODE:]:
+        cu_q.append(cu_q[-1] + n)
+        cu_k.append(cu_k[-1] + h + n)
+    meta = pkg.MixedAttentionContext(
+        MIXED_DECODE, T - MIXED_DECODE, i32(dec_lens.tolist()), i32(tables[:MIXED_DECODE]),
+        i32(cu_q), i32(cu_k), i32(tables[MIXED_DECODE:]), MIXED_CHUNK,
+        max(h + n for h, n in rows[MIXED_DECODE:]), True)
+    ctx = pkg.Context(slot_mapping=i32(slots), mixed=meta)
+    scale = D ** -0.5
+
+    def step():
+        for l in range(L):
+            pkg.forward_mixed(q[l], k[l], v[l], kv[0, l], kv[1, l], ctx, scale, pkg.store_kvcache)
+
+    def prefill_only():
+        for l in range(L):
+            pkg.flash_attn_varlen_func(q[l, MIXED_DECODE:], kv[0, l], kv[1, l], meta.prefill_cu_q,
+                                       meta.prefill_cu_k, meta.max_q, meta.max_k,
+                                       softmax_scale=scale, block_table=meta.prefill_tables)
+
+    step()
+    torch.cuda.synchronize()
+    graph, pgraph = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    with torch.cuda.graph(pgraph):
+        prefill_only()
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    clocks = Clocks(device)
+    with clocks:
+        ev[0].record()
+        for _ in range(args.steps):
+            graph.replay()
+        ev[1].record()
+        torch.cuda.synchronize()
+    ms = ev[0].elapsed_time(ev[1]) / args.steps
+    pgraph.replay()
+    ev[2].record()
+    for _ in range(args.steps):
+        pgraph.replay()
+    ev[3].record()
+    torch.cuda.synchronize()
+    pre_ms = ev[2].elapsed_time(ev[3]) / (args.steps * L)
+    pairs = sum(n * h + n * (n + 1) // 2 for h, n in rows[MIXED_DECODE:])
+    flops = 4 * HQ * D * pairs
+    peak, kind = measured_tensor_peak()
+    achieved = flops / (pre_ms * 1e-3) / 1e12
+    line = {
+        "metric": "mixed prefill/decode step tokens/s (config 3) and prefill tensor TFLOP/s",
+        "value": round(T / (ms * 1e-3), 1), "unit": "tok/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seed 1)",
+        "config": {"workload": "BASELINE config 3: 64 decode rows (context U[256,4096]) + 3 "
+                               "prefill chunks of 2048 over cached prefixes 0/1024/3072, 36 layers "
+                               "of forward_mixed (store + paged decode + paged varlen)",
+                   "tokens_per_step": T, "layers": L, "pool_blocks": NB},
+        "roofline": {"kernel": "paged_prefill (tcgen05, one layer)", "bound": "tensor",
+                     "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
+                     "frac": round(achieved / peak, 4), "peak_kind": peak_kind_str(kind),
+                     "algorithmic_flops": flops, "launch_ms": round(pre_ms, 4), "traffic": None},
+        "gpu_launches": args.steps * L * 4,
+        "clocks": clocks.summary(),
+        "device_errors": pkg.read_device_errors(),
+    }
+    print(json.dumps(line), flush=True)
+    del graph, pgraph
+
+
+def run_copy(args):
+    """Block-pool copy (copy-on-write / swap of whole block ids): `--batch` random
+    source blocks copied to distinct free blocks across all 72 K/V planes of the
+    36-layer bf16 pool, one launch per step."""
+    torch.cuda.set_device(0)
+    device = torch.device("cuda", 0)
+    pkg = importlib.import_module("slo-aware-llm-serving-engine_b200")
+    L = args.layers
+    block_bytes = 2 * L * BS * HKV * D * 2
+    free, total = torch.cuda.mem_get_info(device)
+    NB = args.pool_blocks or int((free - (8 << 30)) // block_bytes)
+    kv = torch.empty(2, L, NB, BS, HKV, D, dtype=torch.bfloat16, device=device)
+    kv.view(torch.int16).random_(-30000, 30000)
+    gen = torch.Generator().manual_seed(5)
+    perm = torch.randperm(NB, generator=gen)
+    n = args.batch
+    src = perm[:n].to(torch.int32).to(device)
+    dst = perm[n:2 * n].to(torch.int32).to(device)
+
+    def step():
+        pkg.kv_block_copy(kv, src, dst)
+
+    step()
+    torch.cuda.synchronize()
+    sample = kv[:, :, int(dst[0])].clone()
+    assert torch.equal(sample, kv[:, :, int(src[0])]), "copy mismatch"
+    for _ in range(args.warmup):
+        step()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    clocks = Clocks(device)
+    with clocks:
+        ev[0].record()
+        for _ in range(args.steps):
+            step()
+        ev[1].record()
+        torch.cuda.synchronize()
+    ms = ev[0].elapsed_time(ev[1]) / args.steps
+    moved = n * block_bytes * 2
+    peak, kind = measured_hbm_peak()
+    gbs = moved / (ms * 1e-3) / 1e9
+    print(json.dumps({
+        "metric": "block-pool copy GB/s (read + write), 36-layer bf16 pool", "value": round(gbs, 1),
+        "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16 (bit copy)", "data": "synthetic",
+        "config": {"workload": f"copy {n} block ids x {L} layers x K/V (CoW / swap)",
+                   "pool_blocks": NB, "bytes_per_step": moved},
+        "roofline": {"kernel": "kv_block_copy", "bound": "hbm", "achieved": round(gbs, 1),
+                     "peak": peak, "unit": "GB/s", "frac": round(gbs / peak, 4),
+                     "peak_kind": kind, "algorithmic_bytes": moved, "launch_ms": round(ms, 4),
+                     "traffic": None},
+        "gpu_launches": args.steps, "clocks": clocks.summary()}), flush=True)
+
+
+def peak_kind_str(kind):
+    return f"{kind} bf16 dense (burst)"
+
+
 def run_reference(args):
     """--impl reference: the reference's torch path for the hot path, as restated
     by the oracle, on the host cores (the reference has no CPU kernel of its own
@@ -515,6 +725,8 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["decode", "mixed", "copy"], default="decode",
+                    help="decode: config 2/4 (the headline); mixed: config 3 prefill + decode")
     ap.add_argument("--kv", choices=["bf16", "fp8"], default="bf16",
                     help="cache format: bf16 (config 2, the headline) or fp8 (config 4)")
     ap.add_argument("--batch", type=int, default=None, help="sequences per GPU")
@@ -541,6 +753,10 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "mixed":
+        run_mixed(args)
+    elif args.workload == "copy":
+        run_copy(args)
     else:
         run_ours(args)
 

@@ -456,16 +456,31 @@ __global__ void __launch_bounds__(Ring<kFp8>::kWarpsPerCta * 32, 1)
       // ---- online softmax (log2 domain) ----
       const float sl = kFp8 ? ks_tile * p.scale_log2 : p.scale_log2;
       float mx0 = -INFINITY, mx1 = -INFINITY;
+      // Unmasked fast path for full tiles: measured faster for the FP8 tile,
+      // slower for the bf16 one (longer loop body), so bf16 always masks.
+      if (kFp8 && valid == kTile) {
 #pragma unroll
-      for (int nt = 0; nt < 4; ++nt) {
+        for (int nt = 0; nt < 4; ++nt) {
 #pragma unroll
-        for (int e2 = 0; e2 < 2; ++e2) {
-          const int tok = nt * 8 + 2 * c + e2;
-          const bool ok = tok < valid;
-          sc[nt][e2] = ok ? sc[nt][e2] * sl : -INFINITY;
-          sc[nt][2 + e2] = ok ? sc[nt][2 + e2] * sl : -INFINITY;
-          mx0 = fmaxf(mx0, sc[nt][e2]);
-          mx1 = fmaxf(mx1, sc[nt][2 + e2]);
+          for (int e2 = 0; e2 < 2; ++e2) {
+            sc[nt][e2] *= sl;
+            sc[nt][2 + e2] *= sl;
+            mx0 = fmaxf(mx0, sc[nt][e2]);
+            mx1 = fmaxf(mx1, sc[nt][2 + e2]);
+          }
+        }
+      } else {
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt) {
+#pragma unroll
+          for (int e2 = 0; e2 < 2; ++e2) {
+            const int tok = nt * 8 + 2 * c + e2;
+            const bool ok = tok < valid;
+            sc[nt][e2] = ok ? sc[nt][e2] * sl : -INFINITY;
+            sc[nt][2 + e2] = ok ? sc[nt][2 + e2] * sl : -INFINITY;
+            mx0 = fmaxf(mx0, sc[nt][e2]);
+            mx1 = fmaxf(mx1, sc[nt][2 + e2]);
+          }
         }
       }
       mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
@@ -498,12 +513,17 @@ __global__ void __launch_bounds__(Ring<kFp8>::kWarpsPerCta * 32, 1)
         oa1 *= ratio;
         vs_cur = vs_tile;
       }
+      // FP8: rescale the accumulators only when some row's running max or the V
+      // unit moved (it settles after a few tiles).  The vote costs the bf16
+      // tile more than the multiplies it saves (measured), so bf16 always does them.
+      if (!kFp8 || (tt != t && __any_sync(0xffffffffu, oa0 != 1.f || oa1 != 1.f))) {
 #pragma unroll
-      for (int n = 0; n < 16; ++n) {
-        o[n][0] *= oa0;
-        o[n][1] *= oa0;
-        o[n][2] *= oa1;
-        o[n][3] *= oa1;
+        for (int n = 0; n < 16; ++n) {
+          o[n][0] *= oa0;
+          o[n][1] *= oa0;
+          o[n][2] *= oa1;
+          o[n][3] *= oa1;
+        }
       }
       uint32_t pa[2][4];
 #pragma unroll
