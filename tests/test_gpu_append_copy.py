@@ -116,3 +116,30 @@ def test_block_copy_full_layer_pool_fp8_container(pkg):
     dev = pool.cuda()
     pkg.kv_block_copy(dev, src.cuda(), dst.cuda())
     assert torch.equal(dev.cpu(), expect)
+
+
+def test_kv_pool_bind_copy_and_scale_lifecycle(pkg):
+    """KVPool binds layer views like allocate_kv_cache, copies whole blocks with
+    their FP8 scales (copy-on-write), and zeroes scales of reassigned blocks."""
+    pool = pkg.KVPool(num_layers=3, num_blocks=6, block_size=256, num_kv_heads=2, head_dim=128,
+                      kv_dtype="fp8")
+    attns = [pkg.Attention(8, 128, 128 ** -0.5, 2) for _ in range(3)]
+    assert pool.bind(attns) == 3
+    assert attns[2].k_cache.data_ptr() == pool.kv_cache[0, 2].data_ptr()
+    assert attns[1].v_scale.data_ptr() == pool.v_scale[1].data_ptr()
+    x = torch.from_numpy(det_normal(63, (300, 2, 128))).bfloat16().cuda()
+    slots = torch.arange(300, dtype=torch.int32, device="cuda") + 256 * 2   # blocks 2, 3
+    for a in attns:
+        pkg.store_kvcache_fp8(x, x, a.k_cache, a.v_cache, a.k_scale, a.v_scale, slots)
+    src = torch.tensor([2, 3], dtype=torch.int32, device="cuda")
+    dst = torch.tensor([5, 0], dtype=torch.int32, device="cuda")
+    pool.copy_blocks(src, dst)
+    assert torch.equal(pool.kv_cache[:, :, 5], pool.kv_cache[:, :, 2])
+    assert torch.equal(pool.kv_cache[:, :, 0], pool.kv_cache[:, :, 3])
+    assert torch.equal(pool.k_scale[:, 5], pool.k_scale[:, 2]) and pool.k_scale[:, 5].gt(0).all()
+    pool.reset_blocks(torch.tensor([5], device="cuda"))
+    assert pool.k_scale[:, 5].abs().sum() == 0 and pool.v_scale[:, 5].abs().sum() == 0
+    saved = pool.swap_out(torch.tensor([3], dtype=torch.int32, device="cuda"))
+    pool.kv_cache[:, :, 3].zero_()
+    pool.swap_in(saved, torch.tensor([3], dtype=torch.int32, device="cuda"))
+    assert torch.equal(pool.kv_cache[:, :, 3], pool.kv_cache[:, :, 0])

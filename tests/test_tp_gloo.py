@@ -1,0 +1,77 @@
+"""Multi-rank host logic on CPU with the gloo backend (world size 2): the pool
+capacity is the minimum over tensor-parallel ranks (as the reference's
+MixedModelRunner.allocate_kv_cache does with an NCCL all-reduce), head shards
+keep GQA groups rank-local, and every rank derives the same batch metadata."""
+import hashlib
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, queue):
+    import importlib
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, root)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        pkg = importlib.import_module("slo-aware-llm-serving-engine_b200")
+        per_block = pkg.block_bytes(36, 256, 8 // world, 128, "bf16")
+        # ranks see different free memory; both must settle on the smaller count
+        total = 180 * 2 ** 30
+        used = (10 + 15 * rank) * 2 ** 30
+        n = pkg.plan_num_blocks(total, used, 0, 0, per_block, 0.9)
+        q_heads, kv_heads = pkg.tp_shard(32, 8, world, rank)
+        import bench
+        B, lens, pages, _ = bench.make_metadata(world)
+        digest = hashlib.sha256(lens.numpy().tobytes()).hexdigest()
+        queue.put((rank, n, list(q_heads), list(kv_heads), digest))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_pool_sizing_sharding_and_metadata():
+    world = 2
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, queue)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = sorted(queue.get(timeout=240) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    counts = {r[1] for r in results}
+    assert len(counts) == 1
+    per_block = 2 * 36 * 256 * 4 * 128 * 2
+    expect = int(180 * 2 ** 30 * 0.9 - 25 * 2 ** 30) // per_block   # the tighter rank
+    assert counts == {expect}
+    (_, _, q0, k0, d0), (_, _, q1, k1, d1) = results
+    assert q0 == list(range(0, 16)) and q1 == list(range(16, 32))
+    assert k0 == list(range(0, 4)) and k1 == list(range(4, 8))
+    for qs, ks in ((q0, k0), (q1, k1)):
+        assert all(h // 4 in ks for h in qs)          # GQA group of every query head is local
+    assert d0 == d1
+
+
+def test_block_bytes_counts_fp8_scales():
+    import importlib
+    pkg = importlib.import_module("slo-aware-llm-serving-engine_b200")
+    assert pkg.block_bytes(36, 256, 8, 128, "bf16") == 36 * 2 ** 20
+    assert pkg.block_bytes(36, 256, 8, 128, "fp8") == 2 * 36 * (256 * 8 * 128 + 8 * 4)
+    with pytest.raises(ValueError):
+        pkg.tp_shard(32, 8, 3, 0)
+    with pytest.raises(RuntimeError):
+        pkg.plan_num_blocks(10, 10, 0, 0, 1)
