@@ -1,5 +1,5 @@
 // Shared device helpers for the sm_100a KV-cache kernels: mbarrier waits with a
-// time bound, TMA tensor loads (no cluster multicast anywhere in this library),
+// time bound, TMA tensor loads (each CTA loads only into its own shared memory),
 // warp-level MMA fragments and small numeric utilities.
 #pragma once
 
@@ -79,7 +79,8 @@ __device__ __forceinline__ uint64_t l2_evict_first_policy() {
 }
 
 // 4-D tiled TMA load into this CTA's shared memory, completion on `bar`.
-// Coordinates are element indices, innermost first.  No multicast.
+// Coordinates are element indices, innermost first; the destination is this
+// CTA's own shared memory.
 __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap *map, uint32_t bar,
                                             int c0, int c1, int c2, int c3, uint64_t policy) {
   asm volatile(

@@ -12,7 +12,7 @@
 // Design (one CTA = 128 queries of one head of one row, 4 warps):
 //  * TMA loads Q once and K/V tiles of 128 keys (two 64-dim halves each,
 //    128-byte swizzle = the canonical K-major UMMA layout) into double-buffered
-//    K and V rings; no cluster multicast.
+//    K and V rings; every CTA loads its own tiles.
 //  * One thread issues tcgen05.mma (kind::f16, M=128, fp32 accumulate in TMEM):
 //    S_j = Q K_j^T into one of two TMEM S buffers -- S_{j+1} is issued before the
 //    softmax of S_j, so the tensor core works while the CUDA cores do exp --
