@@ -321,7 +321,8 @@ def run_ours(args):
         try:
             with open(os.path.join(ROOT, "profiles", "paged_decode_traffic.json")) as f:
                 tr = json.load(f)
-            if not wl["fp8"]:
+            # the capture was taken on the one-GPU bf16 configuration only
+            if not wl["fp8"] and n == 1 and args.batch == BATCH_PER_GPU:
                 traffic = tr.get("dram_bytes_per_launch")
         except Exception:
             pass
