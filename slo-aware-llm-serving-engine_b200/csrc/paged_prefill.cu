@@ -363,6 +363,293 @@ __global__ void __launch_bounds__(128, 1)
   if (warp == 0) tc::tmem_dealloc(tmem, kTmemCols);
 }
 
+// ---- warp-specialised two-head variant ---------------------------------------
+//
+// One CTA = 128 queries of two query heads that share a KV head (GQA group of
+// even size), so one K/V stream feeds both.  Warps 0-3 / 4-7: softmax warpgroups
+// of head 0 / head 1 (thread = query row = TMEM lane).  Warp 8: tensor-core issue
+// (lane 0).  Warp 9: TMA producer (lane 0).  While one warpgroup runs the
+// softmax of tile j, the tensor core runs the other head's PV and next S.
+//
+// TMEM (512 columns): S_0 | S_1 | O_0 | O_1, 128 columns each.  P_h (bf16/f16)
+// is written over the first 64 columns of S_h and read as the TMEM A operand of
+// PV_h; S_h of the next tile is issued after PV_h, so the in-order tensor core
+// reads P_h before overwriting it.
+// Shared memory: Q_0 | Q_1 | K stage 0 | K stage 1 | V stage 0 | V stage 1.
+namespace ws {
+constexpr int kOffQ = 0;
+constexpr int kOffK = 2 * kTile;
+constexpr int kOffV = 4 * kTile;
+constexpr int kTilesBytes = 6 * kTile;
+enum Bar { kQ = 0, kK = 1, kV = 3, kFree = 5, kS = 7, kP = 9, kPV = 11, kNum = 13 };
+constexpr int kSmem = 1024 + kTilesBytes + kNum * 8 + 16;
+constexpr int kThreads = 320;
+constexpr uint32_t kColS = 0, kColO = 256;
+}  // namespace ws
+
+template <typename T>
+__global__ void __launch_bounds__(ws::kThreads, 1)
+    paged_prefill_ws_kernel(const __grid_constant__ CUtensorMap qmap,
+                            const __grid_constant__ CUtensorMap kmap,
+                            const __grid_constant__ CUtensorMap vmap, const Params p) {
+  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+  constexpr uint32_t kIdescS = tc::idesc_f16(kBf16, false, 128, 128);
+  constexpr uint32_t kIdescPV = tc::idesc_f16(kBf16, true, 128, 64);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int r = blockIdx.z;
+  const int h0 = 2 * blockIdx.y;                 // query heads h0, h0 + 1
+  const int m = gridDim.x - 1 - blockIdx.x;
+  const int q0 = __ldg(p.cu_q + r), q_len = __ldg(p.cu_q + r + 1) - q0;
+  const int k0 = __ldg(p.cu_k + r), k_len = __ldg(p.cu_k + r + 1) - k0;
+  if (m * kBM >= q_len) return;
+  const int hk = h0 / p.group;
+  const int qk_off = k_len - q_len;
+  const int last_q = min((m + 1) * kBM, q_len) - 1;
+  const int need = min(k_len, qk_off + last_q + 1);
+  const int nk = need > 0 ? (need + kBN - 1) / kBN : 0;
+  if (nk == 0) {
+    if (tid < 256) {
+      const int qi = m * kBM + (tid & 127);
+      if (qi < q_len) {
+        T *orow = static_cast<T *>(p.out) + static_cast<int64_t>(q0 + qi) * p.out_st +
+                  static_cast<int64_t>(h0 + (tid >> 7)) * p.out_sh;
+        for (int d = 0; d < kD; d += 8) *reinterpret_cast<uint4 *>(orow + d) = make_uint4(0, 0, 0, 0);
+      }
+    }
+    return;
+  }
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t *base_ptr = smem_raw + (base - raw);
+  const uint32_t bars = base + ws::kTilesBytes;
+  volatile uint32_t *tmem_slot =
+      reinterpret_cast<volatile uint32_t *>(base_ptr + ws::kTilesBytes + ws::kNum * 8);
+  volatile uint32_t *abort_flag = tmem_slot + 1;
+  auto bar = [&](int i) { return bars + i * 8; };
+
+  if (tid == 0) {
+    prefetch_tensormap(&qmap);
+    prefetch_tensormap(&kmap);
+    prefetch_tensormap(&vmap);
+    for (int i = 0; i < ws::kNum; ++i)
+      mbar_init(bar(i), (i == ws::kP || i == ws::kP + 1) ? 128u : 1u);
+    fence_barrier_init();
+    *abort_flag = 0;
+  }
+  if (warp == 0) {
+    tc::tmem_alloc(smem_u32(const_cast<uint32_t *>(tmem_slot)), kTmemCols);
+    tc::tmem_relinquish();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+
+  auto wait = [&](int i, uint32_t parity) {
+    if (*abort_flag) return false;
+    if (!mbar_wait(bar(i), parity)) {
+      record_error(p.err, SLOKV_DEVERR_TIMEOUT);
+      *abort_flag = 1;
+      return false;
+    }
+    return true;
+  };
+
+  if (warp == 9) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      const uint64_t policy = l2_evict_first_policy();
+      mbar_arrive_expect_tx(bar(ws::kQ), 2 * kTile);
+      for (int hh = 0; hh < 2; ++hh) {
+        const uint32_t dst = base + ws::kOffQ + hh * kTile;
+        tma_load_4d(dst, &qmap, bar(ws::kQ), 0, h0 + hh, q0 + m * kBM, 0, policy);
+        tma_load_4d(dst + kHalf, &qmap, bar(ws::kQ), 64, h0 + hh, q0 + m * kBM, 0, policy);
+      }
+      for (int j = 0; j < nk; ++j) {
+        const int st = j & 1;
+        if (j >= 2 && !wait(ws::kFree + st, ((j - 2) >> 1) & 1)) break;
+        const KvCoord c = kv_coord(p, r, k0, j);
+        if (!c.ok) record_error(p.err, SLOKV_DEVERR_BLOCK_RANGE);
+        const uint32_t kd = base + ws::kOffK + st * kTile, vd = base + ws::kOffV + st * kTile;
+        mbar_arrive_expect_tx(bar(ws::kK + st), kTile);
+        tma_load_4d(kd, &kmap, bar(ws::kK + st), 0, hk, c.c2, c.c3, policy);
+        tma_load_4d(kd + kHalf, &kmap, bar(ws::kK + st), 64, hk, c.c2, c.c3, policy);
+        mbar_arrive_expect_tx(bar(ws::kV + st), kTile);
+        tma_load_4d(vd, &vmap, bar(ws::kV + st), 0, hk, c.c2, c.c3, policy);
+        tma_load_4d(vd + kHalf, &vmap, bar(ws::kV + st), 64, hk, c.c2, c.c3, policy);
+      }
+    }
+  } else if (warp == 8) {
+    // ---------------- tensor-core issue (lane 0 issues, the warp helps zero V) ----
+    auto issue_s = [&](int hh, int j) {
+      const uint32_t qa = base + ws::kOffQ + hh * kTile;
+      const uint32_t kb = base + ws::kOffK + (j & 1) * kTile;
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint32_t off = (kk >> 2) * kHalf + (kk & 3) * 32;
+        tc::mma_f16_ss(tmem + ws::kColS + hh * 128, tc::smem_desc_sw128(qa + off, 16, 1024),
+                       tc::smem_desc_sw128(kb + off, 16, 1024), kIdescS, kk > 0);
+      }
+      tc::commit(bar(ws::kS + hh));
+    };
+    bool ok = wait(ws::kQ, 0) && wait(ws::kK, 0);
+    if (ok && lane == 0) {
+      tc::fence_after_sync();
+      issue_s(0, 0);
+      issue_s(1, 0);
+    }
+    __syncwarp();
+    for (int j = 0; j < nk && ok; ++j) {
+      const int st = j & 1;
+      for (int hh = 0; hh < 2 && ok; ++hh) {
+        ok = wait(ws::kP + hh, j & 1);                  // P_h(j) in TMEM, O_h rescaled
+        if (ok && hh == 0) {
+          ok = wait(ws::kV + st, (j >> 1) & 1);
+          const int key0 = j * kBN;
+          if (ok && key0 + kBN > k_len) {               // zero V rows past the sequence end
+            const int valid = k_len - key0;
+            uint8_t *vt = base_ptr + ws::kOffV + st * kTile;
+            for (int i = lane; i < (kBN - valid) * 16; i += 32) {
+              const int row = valid + (i >> 4), part = i & 15;
+              *reinterpret_cast<uint4 *>(vt + (part >> 3) * kHalf + row * 128 + (part & 7) * 16) =
+                  make_uint4(0, 0, 0, 0);
+            }
+            fence_proxy_async_smem();
+          }
+          __syncwarp();
+        }
+        if (ok && lane == 0) {
+          tc::fence_after_sync();
+          const uint32_t vb = base + ws::kOffV + st * kTile;
+          const uint32_t pa = tmem + ws::kColS + hh * 128;
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+#pragma unroll
+            for (int nh = 0; nh < 2; ++nh)
+              tc::mma_f16_ts(tmem + ws::kColO + hh * 128 + nh * 64, pa + kk * 8,
+                             tc::smem_desc_sw128(vb + nh * kHalf + kk * 16 * 128, 1024, 1024),
+                             kIdescPV, (j > 0 || kk > 0) ? 1u : 0u);
+          }
+          tc::commit(bar(ws::kPV + hh));
+        }
+        if (ok && j + 1 < nk) {
+          if (hh == 0) ok = wait(ws::kK + ((j + 1) & 1), ((j + 1) >> 1) & 1);
+          if (ok && lane == 0) issue_s(hh, j + 1);
+        }
+        __syncwarp();
+      }
+      if (ok && lane == 0) tc::commit(bar(ws::kFree + st));   // stage st free once these finish
+      __syncwarp();
+    }
+  } else {
+    // ---------------- softmax warpgroup hh (rows = TMEM lanes) ----------------
+    const int hh = warp >> 2;
+    const int row = tid & 127;
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const int qi = m * kBM + row;
+    const bool row_ok = qi < q_len;
+    const int kmax = row_ok ? min(qk_off + qi, k_len - 1) : -1;
+    const uint32_t s_addr = tmem + lane_base + ws::kColS + hh * 128;
+    const uint32_t o_addr = tmem + lane_base + ws::kColO + hh * 128;
+    float m_run = -INFINITY, l_run = 0.f;
+    uint32_t sreg[32];
+    bool ok = true;
+    for (int j = 0; j < nk && ok; ++j) {
+      ok = wait(ws::kS + hh, j & 1);
+      tc::fence_after_sync();
+      const int key0 = j * kBN;
+      const bool full = key0 + kBN - 1 <= kmax;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int cb = 0; cb < 4; ++cb) {
+        tc::ld32(s_addr + cb * 32, sreg);
+        tc::wait_ld();
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          const int key = key0 + cb * 32 + c;
+          if (full || key <= kmax) mx = fmaxf(mx, __uint_as_float(sreg[c]) * p.scale_log2);
+        }
+      }
+      const float m_new = fmaxf(m_run, mx);
+      const float mu = m_new == -INFINITY ? 0.f : m_new;
+      const float alpha = fast_exp2(m_run - mu);
+      m_run = m_new;
+      if (j > 0) {
+        ok = ok && wait(ws::kPV + hh, (j - 1) & 1);     // O_h stable
+        tc::fence_after_sync();
+        if (__any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll
+          for (int cb = 0; cb < 4; ++cb) {
+            tc::ld32(o_addr + cb * 32, sreg);
+            tc::wait_ld();
+#pragma unroll
+            for (int c = 0; c < 32; ++c)
+              sreg[c] = __float_as_uint(__uint_as_float(sreg[c]) * alpha);
+            tc::st32(o_addr + cb * 32, sreg);
+          }
+        }
+      }
+      // P = exp2(s - m) packed two per column over S_h's first 64 columns.
+      float rs = 0.f;
+#pragma unroll
+      for (int cb = 0; cb < 4; ++cb) {
+        tc::ld32(s_addr + cb * 32, sreg);
+        tc::wait_ld();
+        uint32_t pk[16];
+#pragma unroll
+        for (int c = 0; c < 32; c += 2) {
+          const int key = key0 + cb * 32 + c;
+          const float a = (full || key <= kmax)
+                              ? fast_exp2(__uint_as_float(sreg[c]) * p.scale_log2 - mu) : 0.f;
+          const float b = (full || key + 1 <= kmax)
+                              ? fast_exp2(__uint_as_float(sreg[c + 1]) * p.scale_log2 - mu) : 0.f;
+          rs += a + b;
+          pk[c >> 1] = Pack<T>::two(a, b);
+        }
+        // keys 32cb .. 32cb+31 -> columns 16cb .. 16cb+15 (already read as S)
+        tc::st16(s_addr + cb * 16, pk);
+      }
+      l_run = l_run * alpha + rs;
+      tc::wait_st();
+      tc::fence_before_sync();
+      mbar_arrive(bar(ws::kP + hh));
+    }
+    // epilogue: O_h / l -> out
+    ok = ok && wait(ws::kPV + hh, (nk - 1) & 1);
+    tc::fence_after_sync();
+    if (__all_sync(0xffffffffu, ok)) {
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      T *orow = static_cast<T *>(p.out) + static_cast<int64_t>(q0 + qi) * p.out_st +
+                static_cast<int64_t>(h0 + hh) * p.out_sh;
+#pragma unroll
+      for (int cb = 0; cb < 4; ++cb) {
+        tc::ld32(o_addr + cb * 32, sreg);
+        tc::wait_ld();
+        if (row_ok) {
+#pragma unroll
+          for (int c = 0; c < 32; c += 8) {
+            uint4 w;
+            w.x = Pack<T>::two(__uint_as_float(sreg[c]) * inv, __uint_as_float(sreg[c + 1]) * inv);
+            w.y = Pack<T>::two(__uint_as_float(sreg[c + 2]) * inv, __uint_as_float(sreg[c + 3]) * inv);
+            w.z = Pack<T>::two(__uint_as_float(sreg[c + 4]) * inv, __uint_as_float(sreg[c + 5]) * inv);
+            w.w = Pack<T>::two(__uint_as_float(sreg[c + 6]) * inv, __uint_as_float(sreg[c + 7]) * inv);
+            *reinterpret_cast<uint4 *>(orow + cb * 32 + c) = w;
+          }
+        }
+      }
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
 // ---- host side -------------------------------------------------------------
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -401,11 +688,18 @@ int launch(const Params &p, const CUtensorMap &qm, const CUtensorMap &km, const 
   static bool ok = false;
   std::call_once(once, [] {
     ok = cudaFuncSetAttribute(paged_prefill_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              kSmemBytes) == cudaSuccess;
+                              kSmemBytes) == cudaSuccess &&
+         cudaFuncSetAttribute(paged_prefill_ws_kernel<T>,
+                              cudaFuncAttributeMaxDynamicSharedMemorySize, ws::kSmem) == cudaSuccess;
   });
   if (!ok) return SLOKV_ERR_CUDA;
-  dim3 grid((max_q + kBM - 1) / kBM, p.hq, rows);
-  paged_prefill_kernel<T><<<grid, 128, kSmemBytes, stream>>>(qm, km, vm, p);
+  if (p.group % 2 == 0) {  // two query heads of one KV head per CTA
+    dim3 grid((max_q + kBM - 1) / kBM, p.hq / 2, rows);
+    paged_prefill_ws_kernel<T><<<grid, ws::kThreads, ws::kSmem, stream>>>(qm, km, vm, p);
+  } else {
+    dim3 grid((max_q + kBM - 1) / kBM, p.hq, rows);
+    paged_prefill_kernel<T><<<grid, 128, kSmemBytes, stream>>>(qm, km, vm, p);
+  }
   return cudaGetLastError() == cudaSuccess ? SLOKV_OK : SLOKV_ERR_CUDA;
 }
 
