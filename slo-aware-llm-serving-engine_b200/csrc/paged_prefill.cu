@@ -554,63 +554,91 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
     const int kmax = row_ok ? min(qk_off + qi, k_len - 1) : -1;
     const uint32_t s_addr = tmem + lane_base + ws::kColS + hh * 128;
     const uint32_t o_addr = tmem + lane_base + ws::kColO + hh * 128;
+    // Lazy rescaling: the row keeps using a stale max m_run until the tile max
+    // exceeds it by more than kLazy (log2 units), so P <= 2^kLazy (exact in
+    // bf16/f16 range) and O in TMEM is rescaled only on those rare jumps.
+    constexpr float kLazy = 8.f;
     float m_run = -INFINITY, l_run = 0.f;
-    uint32_t sreg[32];
+    uint32_t sa[32], sb[32];
     bool ok = true;
     for (int j = 0; j < nk && ok; ++j) {
       ok = wait(ws::kS + hh, j & 1);
       tc::fence_after_sync();
       const int key0 = j * kBN;
-      const bool full = key0 + kBN - 1 <= kmax;
+      const bool full = key0 + kBN - 1 <= kmax;   // no key of the tile is masked
+      // pass 1: row max of the raw scores, 64 columns per TMEM round trip
       float mx = -INFINITY;
 #pragma unroll
-      for (int cb = 0; cb < 4; ++cb) {
-        tc::ld32(s_addr + cb * 32, sreg);
+      for (int half = 0; half < 2; ++half) {
+        tc::ld32(s_addr + half * 64, sa);
+        tc::ld32(s_addr + half * 64 + 32, sb);
         tc::wait_ld();
+        if (full) {
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const int key = key0 + cb * 32 + c;
-          if (full || key <= kmax) mx = fmaxf(mx, __uint_as_float(sreg[c]) * p.scale_log2);
+          for (int c = 0; c < 32; ++c)
+            mx = fmaxf(mx, fmaxf(__uint_as_float(sa[c]), __uint_as_float(sb[c])));
+        } else {
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            if (key0 + half * 64 + c <= kmax) mx = fmaxf(mx, __uint_as_float(sa[c]));
+            if (key0 + half * 64 + 32 + c <= kmax) mx = fmaxf(mx, __uint_as_float(sb[c]));
+          }
         }
       }
-      const float m_new = fmaxf(m_run, mx);
-      const float mu = m_new == -INFINITY ? 0.f : m_new;
-      const float alpha = fast_exp2(m_run - mu);
-      m_run = m_new;
+      mx *= p.scale_log2;
+      float alpha = 1.f;
+      if (mx > m_run + kLazy || m_run == -INFINITY) {
+        const float m_new = fmaxf(m_run, mx);
+        alpha = m_run == -INFINITY ? 0.f : fast_exp2(m_run - m_new);
+        m_run = m_new;
+      }
+      const float mu = m_run == -INFINITY ? 0.f : m_run;
       if (j > 0) {
         ok = ok && wait(ws::kPV + hh, (j - 1) & 1);     // O_h stable
         tc::fence_after_sync();
         if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll
-          for (int cb = 0; cb < 4; ++cb) {
-            tc::ld32(o_addr + cb * 32, sreg);
+          for (int cb = 0; cb < 4; cb += 2) {
+            tc::ld32(o_addr + cb * 32, sa);
+            tc::ld32(o_addr + cb * 32 + 32, sb);
             tc::wait_ld();
 #pragma unroll
-            for (int c = 0; c < 32; ++c)
-              sreg[c] = __float_as_uint(__uint_as_float(sreg[c]) * alpha);
-            tc::st32(o_addr + cb * 32, sreg);
+            for (int c = 0; c < 32; ++c) {
+              sa[c] = __float_as_uint(__uint_as_float(sa[c]) * alpha);
+              sb[c] = __float_as_uint(__uint_as_float(sb[c]) * alpha);
+            }
+            tc::st32(o_addr + cb * 32, sa);
+            tc::st32(o_addr + cb * 32 + 32, sb);
           }
         }
       }
-      // P = exp2(s - m) packed two per column over S_h's first 64 columns.
+      // pass 2: P = exp2(s * scale - m) packed two per column over S_h's first 64
+      // columns; keys 64*half .. +63 go to columns 32*half .. +31, all already read.
       float rs = 0.f;
 #pragma unroll
-      for (int cb = 0; cb < 4; ++cb) {
-        tc::ld32(s_addr + cb * 32, sreg);
+      for (int half = 0; half < 2; ++half) {
+        tc::ld32(s_addr + half * 64, sa);
+        tc::ld32(s_addr + half * 64 + 32, sb);
         tc::wait_ld();
-        uint32_t pk[16];
+        uint32_t pk[32];
 #pragma unroll
         for (int c = 0; c < 32; c += 2) {
-          const int key = key0 + cb * 32 + c;
-          const float a = (full || key <= kmax)
-                              ? fast_exp2(__uint_as_float(sreg[c]) * p.scale_log2 - mu) : 0.f;
-          const float b = (full || key + 1 <= kmax)
-                              ? fast_exp2(__uint_as_float(sreg[c + 1]) * p.scale_log2 - mu) : 0.f;
-          rs += a + b;
+          const int ka = key0 + half * 64 + c;
+          float a = fast_exp2(fmaf(__uint_as_float(sa[c]), p.scale_log2, -mu));
+          float b = fast_exp2(fmaf(__uint_as_float(sa[c + 1]), p.scale_log2, -mu));
+          float x = fast_exp2(fmaf(__uint_as_float(sb[c]), p.scale_log2, -mu));
+          float y = fast_exp2(fmaf(__uint_as_float(sb[c + 1]), p.scale_log2, -mu));
+          if (!full) {
+            a = ka <= kmax ? a : 0.f;
+            b = ka + 1 <= kmax ? b : 0.f;
+            x = ka + 32 <= kmax ? x : 0.f;
+            y = ka + 33 <= kmax ? y : 0.f;
+          }
+          rs += (a + b) + (x + y);
           pk[c >> 1] = Pack<T>::two(a, b);
+          pk[16 + (c >> 1)] = Pack<T>::two(x, y);
         }
-        // keys 32cb .. 32cb+31 -> columns 16cb .. 16cb+15 (already read as S)
-        tc::st16(s_addr + cb * 16, pk);
+        tc::st32(s_addr + half * 32, pk);
       }
       l_run = l_run * alpha + rs;
       tc::wait_st();
@@ -626,16 +654,16 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
                 static_cast<int64_t>(h0 + hh) * p.out_sh;
 #pragma unroll
       for (int cb = 0; cb < 4; ++cb) {
-        tc::ld32(o_addr + cb * 32, sreg);
+        tc::ld32(o_addr + cb * 32, sa);
         tc::wait_ld();
         if (row_ok) {
 #pragma unroll
           for (int c = 0; c < 32; c += 8) {
             uint4 w;
-            w.x = Pack<T>::two(__uint_as_float(sreg[c]) * inv, __uint_as_float(sreg[c + 1]) * inv);
-            w.y = Pack<T>::two(__uint_as_float(sreg[c + 2]) * inv, __uint_as_float(sreg[c + 3]) * inv);
-            w.z = Pack<T>::two(__uint_as_float(sreg[c + 4]) * inv, __uint_as_float(sreg[c + 5]) * inv);
-            w.w = Pack<T>::two(__uint_as_float(sreg[c + 6]) * inv, __uint_as_float(sreg[c + 7]) * inv);
+            w.x = Pack<T>::two(__uint_as_float(sa[c]) * inv, __uint_as_float(sa[c + 1]) * inv);
+            w.y = Pack<T>::two(__uint_as_float(sa[c + 2]) * inv, __uint_as_float(sa[c + 3]) * inv);
+            w.z = Pack<T>::two(__uint_as_float(sa[c + 4]) * inv, __uint_as_float(sa[c + 5]) * inv);
+            w.w = Pack<T>::two(__uint_as_float(sa[c + 6]) * inv, __uint_as_float(sa[c + 7]) * inv);
             *reinterpret_cast<uint4 *>(orow + cb * 32 + c) = w;
           }
         }
