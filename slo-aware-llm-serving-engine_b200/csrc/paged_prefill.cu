@@ -381,7 +381,7 @@ constexpr int kOffQ = 0;
 constexpr int kOffK = 2 * kTile;
 constexpr int kOffV = 4 * kTile;
 constexpr int kTilesBytes = 6 * kTile;
-enum Bar { kQ = 0, kK = 1, kV = 3, kFree = 5, kS = 7, kP = 9, kPV = 11, kNum = 13 };
+enum Bar { kQ = 0, kK = 1, kV = 3, kFreeK = 5, kFreeV = 7, kS = 9, kP = 11, kPV = 13, kNum = 15 };
 constexpr int kSmem = 1024 + kTilesBytes + kNum * 8 + 16;
 constexpr int kThreads = 320;
 constexpr uint32_t kColS = 0, kColO = 256;
@@ -470,13 +470,16 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
       }
       for (int j = 0; j < nk; ++j) {
         const int st = j & 1;
-        if (j >= 2 && !wait(ws::kFree + st, ((j - 2) >> 1) & 1)) break;
+        // K stage st frees once both S MMAs of tile j-2 finish, V stage st once
+        // both PV MMAs of tile j-2 finish (later): K loads run ahead.
+        if (j >= 2 && !wait(ws::kFreeK + st, ((j - 2) >> 1) & 1)) break;
         const KvCoord c = kv_coord(p, r, k0, j);
         if (!c.ok) record_error(p.err, SLOKV_DEVERR_BLOCK_RANGE);
         const uint32_t kd = base + ws::kOffK + st * kTile, vd = base + ws::kOffV + st * kTile;
         mbar_arrive_expect_tx(bar(ws::kK + st), kTile);
         tma_load_4d(kd, &kmap, bar(ws::kK + st), 0, hk, c.c2, c.c3, policy);
         tma_load_4d(kd + kHalf, &kmap, bar(ws::kK + st), 64, hk, c.c2, c.c3, policy);
+        if (j >= 2 && !wait(ws::kFreeV + st, ((j - 2) >> 1) & 1)) break;
         mbar_arrive_expect_tx(bar(ws::kV + st), kTile);
         tma_load_4d(vd, &vmap, bar(ws::kV + st), 0, hk, c.c2, c.c3, policy);
         tma_load_4d(vd + kHalf, &vmap, bar(ws::kV + st), 64, hk, c.c2, c.c3, policy);
@@ -500,6 +503,7 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
       tc::fence_after_sync();
       issue_s(0, 0);
       issue_s(1, 0);
+      tc::commit(bar(ws::kFreeK));                      // K stage 0 free after S(0)
     }
     __syncwarp();
     for (int j = 0; j < nk && ok; ++j) {
@@ -541,7 +545,10 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
         }
         __syncwarp();
       }
-      if (ok && lane == 0) tc::commit(bar(ws::kFree + st));   // stage st free once these finish
+      if (ok && lane == 0) {
+        tc::commit(bar(ws::kFreeV + st));                   // after PV(j) of both heads
+        if (j + 1 < nk) tc::commit(bar(ws::kFreeK + ((j + 1) & 1)));   // after S(j+1)
+      }
       __syncwarp();
     }
   } else {
