@@ -565,45 +565,97 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
     // exceeds it by more than kLazy (log2 units), so P <= 2^kLazy (exact in
     // bf16/f16 range) and O in TMEM is rescaled only on those rare jumps.
     constexpr float kLazy = 8.f;
-    float m_run = -INFINITY, l_run = 0.f;
+    // Padding rows (no query) start from a finite max so they never force the
+    // exact path; all their keys are masked, so P = 0 and l = 0.
+    float m_run = row_ok ? -INFINITY : 0.f, l_run = 0.f;
     uint32_t sa[32], sb[32];
     bool ok = true;
+    // P of 64 columns (sa = keys 64*half + 0..31, sb = keys 64*half + 32..63)
+    // against max mu, packed two per 32-bit word: pk[c/2] keys c, c+1 of sa and
+    // pk[16 + c/2] of sb.  Returns the row sum of the unrounded values.
+    auto exp_pack = [&](int half, int key0, bool full, float mu, uint32_t (&pk)[32]) {
+      float rs = 0.f;
+#pragma unroll
+      for (int c = 0; c < 32; c += 2) {
+        const int ka = key0 + half * 64 + c;
+        float a = fast_exp2(fmaf(__uint_as_float(sa[c]), p.scale_log2, -mu));
+        float b = fast_exp2(fmaf(__uint_as_float(sa[c + 1]), p.scale_log2, -mu));
+        float x = fast_exp2(fmaf(__uint_as_float(sb[c]), p.scale_log2, -mu));
+        float y = fast_exp2(fmaf(__uint_as_float(sb[c + 1]), p.scale_log2, -mu));
+        if (!full) {
+          a = ka <= kmax ? a : 0.f;
+          b = ka + 1 <= kmax ? b : 0.f;
+          x = ka + 32 <= kmax ? x : 0.f;
+          y = ka + 33 <= kmax ? y : 0.f;
+        }
+        rs += (a + b) + (x + y);
+        pk[c >> 1] = Pack<T>::two(a, b);
+        pk[16 + (c >> 1)] = Pack<T>::two(x, y);
+      }
+      return rs;
+    };
+    auto raw_max = [&](int half, int key0, bool full) {
+      float mx = -INFINITY;
+      if (full) {
+#pragma unroll
+        for (int c = 0; c < 32; ++c)
+          mx = fmaxf(mx, fmaxf(__uint_as_float(sa[c]), __uint_as_float(sb[c])));
+      } else {
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          if (key0 + half * 64 + c <= kmax) mx = fmaxf(mx, __uint_as_float(sa[c]));
+          if (key0 + half * 64 + 32 + c <= kmax) mx = fmaxf(mx, __uint_as_float(sb[c]));
+        }
+      }
+      return mx;
+    };
+    auto load_half = [&](int half) {
+      tc::ld32(s_addr + half * 64, sa);
+      tc::ld32(s_addr + half * 64 + 32, sb);
+      tc::wait_ld();
+    };
     for (int j = 0; j < nk && ok; ++j) {
+      // S_h(j) complete implies PV_h(j-1) complete (both issued in order by one
+      // thread; a commit covers every earlier MMA): O_h and the P columns are free.
       ok = wait(ws::kS + hh, j & 1);
       tc::fence_after_sync();
       const int key0 = j * kBN;
       const bool full = key0 + kBN - 1 <= kmax;   // no key of the tile is masked
-      // pass 1: row max of the raw scores, 64 columns per TMEM round trip
-      float mx = -INFINITY;
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        tc::ld32(s_addr + half * 64, sa);
-        tc::ld32(s_addr + half * 64 + 32, sb);
-        tc::wait_ld();
-        if (full) {
-#pragma unroll
-          for (int c = 0; c < 32; ++c)
-            mx = fmaxf(mx, fmaxf(__uint_as_float(sa[c]), __uint_as_float(sb[c])));
-        } else {
-#pragma unroll
-          for (int c = 0; c < 32; ++c) {
-            if (key0 + half * 64 + c <= kmax) mx = fmaxf(mx, __uint_as_float(sa[c]));
-            if (key0 + half * 64 + 32 + c <= kmax) mx = fmaxf(mx, __uint_as_float(sb[c]));
+      // Common case, one TMEM read of S: P against the running max, valid while
+      // no score of the tile exceeds it by more than kLazy.  Nothing is written
+      // to TMEM (P overlays S) until both halves have passed that test.
+      bool slow = __any_sync(0xffffffffu, m_run == -INFINITY);
+      float rs = 0.f;
+      if (!slow) {
+        load_half(0);
+        slow = __any_sync(0xffffffffu, raw_max(0, key0, full) * p.scale_log2 > m_run + kLazy);
+        if (!slow) {
+          uint32_t pk0[32];
+          rs = exp_pack(0, key0, full, m_run, pk0);
+          load_half(1);
+          slow = __any_sync(0xffffffffu, raw_max(1, key0, full) * p.scale_log2 > m_run + kLazy);
+          if (!slow) {
+            uint32_t pk1[32];
+            tc::st32(s_addr, pk0);
+            rs += exp_pack(1, key0, full, m_run, pk1);
+            tc::st32(s_addr + 32, pk1);
           }
         }
       }
-      mx *= p.scale_log2;
       float alpha = 1.f;
-      if (mx > m_run + kLazy || m_run == -INFINITY) {
-        const float m_new = fmaxf(m_run, mx);
-        alpha = m_run == -INFINITY ? 0.f : fast_exp2(m_run - m_new);
-        m_run = m_new;
-      }
-      const float mu = m_run == -INFINITY ? 0.f : m_run;
-      if (j > 0) {
-        ok = ok && wait(ws::kPV + hh, (j - 1) & 1);     // O_h stable
-        tc::fence_after_sync();
-        if (__any_sync(0xffffffffu, alpha != 1.f)) {
+      if (slow) {
+        // exact path: row max over the tile, O rescale, then P from S again
+        load_half(0);
+        float mx = raw_max(0, key0, full);
+        load_half(1);
+        mx = fmaxf(mx, raw_max(1, key0, full)) * p.scale_log2;
+        if (mx > m_run + kLazy || m_run == -INFINITY) {
+          const float m_new = fmaxf(m_run, mx);
+          alpha = m_run == -INFINITY ? 0.f : fast_exp2(m_run - m_new);
+          m_run = m_new;
+        }
+        const float mu = m_run == -INFINITY ? 0.f : m_run;
+        if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll
           for (int cb = 0; cb < 4; cb += 2) {
             tc::ld32(o_addr + cb * 32, sa);
@@ -617,35 +669,16 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
             tc::st32(o_addr + cb * 32, sa);
             tc::st32(o_addr + cb * 32 + 32, sb);
           }
+          tc::wait_st();
         }
-      }
-      // pass 2: P = exp2(s * scale - m) packed two per column over S_h's first 64
-      // columns; keys 64*half .. +63 go to columns 32*half .. +31, all already read.
-      float rs = 0.f;
+        rs = 0.f;
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        tc::ld32(s_addr + half * 64, sa);
-        tc::ld32(s_addr + half * 64 + 32, sb);
-        tc::wait_ld();
-        uint32_t pk[32];
-#pragma unroll
-        for (int c = 0; c < 32; c += 2) {
-          const int ka = key0 + half * 64 + c;
-          float a = fast_exp2(fmaf(__uint_as_float(sa[c]), p.scale_log2, -mu));
-          float b = fast_exp2(fmaf(__uint_as_float(sa[c + 1]), p.scale_log2, -mu));
-          float x = fast_exp2(fmaf(__uint_as_float(sb[c]), p.scale_log2, -mu));
-          float y = fast_exp2(fmaf(__uint_as_float(sb[c + 1]), p.scale_log2, -mu));
-          if (!full) {
-            a = ka <= kmax ? a : 0.f;
-            b = ka + 1 <= kmax ? b : 0.f;
-            x = ka + 32 <= kmax ? x : 0.f;
-            y = ka + 33 <= kmax ? y : 0.f;
-          }
-          rs += (a + b) + (x + y);
-          pk[c >> 1] = Pack<T>::two(a, b);
-          pk[16 + (c >> 1)] = Pack<T>::two(x, y);
+        for (int half = 0; half < 2; ++half) {
+          uint32_t pk[32];
+          load_half(half);
+          rs += exp_pack(half, key0, full, mu, pk);
+          tc::st32(s_addr + half * 32, pk);
         }
-        tc::st32(s_addr + half * 32, pk);
       }
       l_run = l_run * alpha + rs;
       tc::wait_st();
