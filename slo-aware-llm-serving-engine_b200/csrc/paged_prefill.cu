@@ -368,8 +368,12 @@ __global__ void __launch_bounds__(128, 1)
 // One CTA = 128 queries of two query heads that share a KV head (GQA group of
 // even size), so one K/V stream feeds both.  Warps 0-3 / 4-7: softmax warpgroups
 // of head 0 / head 1 (thread = query row = TMEM lane).  Warp 8: tensor-core issue
-// (lane 0).  Warp 9: TMA producer (lane 0).  While one warpgroup runs the
-// softmax of tile j, the tensor core runs the other head's PV and next S.
+// (lane 0).  Warp 9: TMA producer (lane 0).  Warps 10-11 only complete the
+// issue warpgroup, whose registers setmaxnreg moves to the softmax warpgroups:
+// a softmax thread holds its whole 128-key S row after one TMEM load, so each
+// tile costs one TMEM round trip, one row max and one exponentiation pass.
+// While one warpgroup runs the softmax of tile j, the tensor core runs the
+// other head's PV and next S.
 //
 // TMEM (512 columns): S_0 | S_1 | O_0 | O_1, 128 columns each.  P_h (bf16/f16)
 // is written over the first 64 columns of S_h and read as the TMEM A operand of
@@ -383,7 +387,14 @@ constexpr int kOffV = 4 * kTile;
 constexpr int kTilesBytes = 6 * kTile;
 enum Bar { kQ = 0, kK = 1, kV = 3, kFreeK = 5, kFreeV = 7, kS = 9, kP = 11, kPV = 13, kNum = 15 };
 constexpr int kSmem = 1024 + kTilesBytes + kNum * 8 + 16;
-constexpr int kThreads = 320;
+constexpr int kThreads = 384;
+// Register split (setmaxnreg): the block launches with 168 registers a thread
+// (384 threads x 168 = 64512); warps 8-11 drop to kRegsIssue and the two softmax
+// warpgroups rise to kRegsSoftmax: 2*128*kRegsSoftmax + 128*kRegsIssue = 64512.
+constexpr int kRegsLaunch = 168, kRegsIssue = 56, kRegsSoftmax = 224;
+static_assert(2 * 128 * kRegsSoftmax + 128 * kRegsIssue <= kThreads * kRegsLaunch,
+              "register split exceeds the launch allocation");
+
 constexpr uint32_t kColS = 0, kColO = 256;
 }  // namespace ws
 
@@ -396,7 +407,9 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
   constexpr uint32_t kIdescS = tc::idesc_f16(kBf16, false, 128, 128);
   constexpr uint32_t kIdescPV = tc::idesc_f16(kBf16, true, 128, 64);
 
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tid = threadIdx.x, lane = tid & 31;
+  // warp index made visibly warp-uniform for the compiler (role dispatch, setmaxnreg)
+  const int warp = __shfl_sync(0xffffffffu, tid >> 5, 0);
   const int r = blockIdx.z;
   const int h0 = 2 * blockIdx.y;                 // query heads h0, h0 + 1
   const int m = gridDim.x - 1 - blockIdx.x;
@@ -458,100 +471,105 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
     return true;
   };
 
-  if (warp == 9) {
-    // ---------------- TMA producer ----------------
-    if (lane == 0) {
-      const uint64_t policy = l2_evict_first_policy();
-      mbar_arrive_expect_tx(bar(ws::kQ), 2 * kTile);
-      for (int hh = 0; hh < 2; ++hh) {
-        const uint32_t dst = base + ws::kOffQ + hh * kTile;
-        tma_load_4d(dst, &qmap, bar(ws::kQ), 0, h0 + hh, q0 + m * kBM, 0, policy);
-        tma_load_4d(dst + kHalf, &qmap, bar(ws::kQ), 64, h0 + hh, q0 + m * kBM, 0, policy);
+  if (warp >= 8) {
+    // Warps 8-11 (one warpgroup) give registers to the softmax warpgroups.
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(ws::kRegsIssue));
+    if (warp == 9) {
+      // ---------------- TMA producer ----------------
+      if (lane == 0) {
+        const uint64_t policy = l2_evict_first_policy();
+        mbar_arrive_expect_tx(bar(ws::kQ), 2 * kTile);
+        for (int hh = 0; hh < 2; ++hh) {
+          const uint32_t dst = base + ws::kOffQ + hh * kTile;
+          tma_load_4d(dst, &qmap, bar(ws::kQ), 0, h0 + hh, q0 + m * kBM, 0, policy);
+          tma_load_4d(dst + kHalf, &qmap, bar(ws::kQ), 64, h0 + hh, q0 + m * kBM, 0, policy);
+        }
+        for (int j = 0; j < nk; ++j) {
+          const int st = j & 1;
+          // K stage st frees once both S MMAs of tile j-2 finish, V stage st once
+          // both PV MMAs of tile j-2 finish (later): K loads run ahead.
+          if (j >= 2 && !wait(ws::kFreeK + st, ((j - 2) >> 1) & 1)) break;
+          const KvCoord c = kv_coord(p, r, k0, j);
+          if (!c.ok) record_error(p.err, SLOKV_DEVERR_BLOCK_RANGE);
+          const uint32_t kd = base + ws::kOffK + st * kTile, vd = base + ws::kOffV + st * kTile;
+          mbar_arrive_expect_tx(bar(ws::kK + st), kTile);
+          tma_load_4d(kd, &kmap, bar(ws::kK + st), 0, hk, c.c2, c.c3, policy);
+          tma_load_4d(kd + kHalf, &kmap, bar(ws::kK + st), 64, hk, c.c2, c.c3, policy);
+          if (j >= 2 && !wait(ws::kFreeV + st, ((j - 2) >> 1) & 1)) break;
+          mbar_arrive_expect_tx(bar(ws::kV + st), kTile);
+          tma_load_4d(vd, &vmap, bar(ws::kV + st), 0, hk, c.c2, c.c3, policy);
+          tma_load_4d(vd + kHalf, &vmap, bar(ws::kV + st), 64, hk, c.c2, c.c3, policy);
+        }
       }
-      for (int j = 0; j < nk; ++j) {
-        const int st = j & 1;
-        // K stage st frees once both S MMAs of tile j-2 finish, V stage st once
-        // both PV MMAs of tile j-2 finish (later): K loads run ahead.
-        if (j >= 2 && !wait(ws::kFreeK + st, ((j - 2) >> 1) & 1)) break;
-        const KvCoord c = kv_coord(p, r, k0, j);
-        if (!c.ok) record_error(p.err, SLOKV_DEVERR_BLOCK_RANGE);
-        const uint32_t kd = base + ws::kOffK + st * kTile, vd = base + ws::kOffV + st * kTile;
-        mbar_arrive_expect_tx(bar(ws::kK + st), kTile);
-        tma_load_4d(kd, &kmap, bar(ws::kK + st), 0, hk, c.c2, c.c3, policy);
-        tma_load_4d(kd + kHalf, &kmap, bar(ws::kK + st), 64, hk, c.c2, c.c3, policy);
-        if (j >= 2 && !wait(ws::kFreeV + st, ((j - 2) >> 1) & 1)) break;
-        mbar_arrive_expect_tx(bar(ws::kV + st), kTile);
-        tma_load_4d(vd, &vmap, bar(ws::kV + st), 0, hk, c.c2, c.c3, policy);
-        tma_load_4d(vd + kHalf, &vmap, bar(ws::kV + st), 64, hk, c.c2, c.c3, policy);
-      }
-    }
-  } else if (warp == 8) {
-    // ---------------- tensor-core issue (lane 0 issues, the warp helps zero V) ----
-    auto issue_s = [&](int hh, int j) {
-      const uint32_t qa = base + ws::kOffQ + hh * kTile;
-      const uint32_t kb = base + ws::kOffK + (j & 1) * kTile;
+    } else if (warp == 8) {
+      // ---------------- tensor-core issue (lane 0 issues, the warp helps zero V) ----
+      auto issue_s = [&](int hh, int j) {
+        const uint32_t qa = base + ws::kOffQ + hh * kTile;
+        const uint32_t kb = base + ws::kOffK + (j & 1) * kTile;
 #pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
-        const uint32_t off = (kk >> 2) * kHalf + (kk & 3) * 32;
-        tc::mma_f16_ss(tmem + ws::kColS + hh * 128, tc::smem_desc_sw128(qa + off, 16, 1024),
-                       tc::smem_desc_sw128(kb + off, 16, 1024), kIdescS, kk > 0);
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t off = (kk >> 2) * kHalf + (kk & 3) * 32;
+          tc::mma_f16_ss(tmem + ws::kColS + hh * 128, tc::smem_desc_sw128(qa + off, 16, 1024),
+                         tc::smem_desc_sw128(kb + off, 16, 1024), kIdescS, kk > 0);
+        }
+        tc::commit(bar(ws::kS + hh));
+      };
+      bool ok = wait(ws::kQ, 0) && wait(ws::kK, 0);
+      if (ok && lane == 0) {
+        tc::fence_after_sync();
+        issue_s(0, 0);
+        issue_s(1, 0);
+        tc::commit(bar(ws::kFreeK));                      // K stage 0 free after S(0)
       }
-      tc::commit(bar(ws::kS + hh));
-    };
-    bool ok = wait(ws::kQ, 0) && wait(ws::kK, 0);
-    if (ok && lane == 0) {
-      tc::fence_after_sync();
-      issue_s(0, 0);
-      issue_s(1, 0);
-      tc::commit(bar(ws::kFreeK));                      // K stage 0 free after S(0)
-    }
-    __syncwarp();
-    for (int j = 0; j < nk && ok; ++j) {
-      const int st = j & 1;
-      for (int hh = 0; hh < 2 && ok; ++hh) {
-        ok = wait(ws::kP + hh, j & 1);                  // P_h(j) in TMEM, O_h rescaled
-        if (ok && hh == 0) {
-          ok = wait(ws::kV + st, (j >> 1) & 1);
-          const int key0 = j * kBN;
-          if (ok && key0 + kBN > k_len) {               // zero V rows past the sequence end
-            const int valid = k_len - key0;
-            uint8_t *vt = base_ptr + ws::kOffV + st * kTile;
-            for (int i = lane; i < (kBN - valid) * 16; i += 32) {
-              const int row = valid + (i >> 4), part = i & 15;
-              *reinterpret_cast<uint4 *>(vt + (part >> 3) * kHalf + row * 128 + (part & 7) * 16) =
-                  make_uint4(0, 0, 0, 0);
+      __syncwarp();
+      for (int j = 0; j < nk && ok; ++j) {
+        const int st = j & 1;
+        for (int hh = 0; hh < 2 && ok; ++hh) {
+          ok = wait(ws::kP + hh, j & 1);                  // P_h(j) in TMEM, O_h rescaled
+          if (ok && hh == 0) {
+            ok = wait(ws::kV + st, (j >> 1) & 1);
+            const int key0 = j * kBN;
+            if (ok && key0 + kBN > k_len) {               // zero V rows past the sequence end
+              const int valid = k_len - key0;
+              uint8_t *vt = base_ptr + ws::kOffV + st * kTile;
+              for (int i = lane; i < (kBN - valid) * 16; i += 32) {
+                const int row = valid + (i >> 4), part = i & 15;
+                *reinterpret_cast<uint4 *>(vt + (part >> 3) * kHalf + row * 128 + (part & 7) * 16) =
+                    make_uint4(0, 0, 0, 0);
+              }
+              fence_proxy_async_smem();
             }
-            fence_proxy_async_smem();
+            __syncwarp();
+          }
+          if (ok && lane == 0) {
+            tc::fence_after_sync();
+            const uint32_t vb = base + ws::kOffV + st * kTile;
+            const uint32_t pa = tmem + ws::kColS + hh * 128;
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {
+#pragma unroll
+              for (int nh = 0; nh < 2; ++nh)
+                tc::mma_f16_ts(tmem + ws::kColO + hh * 128 + nh * 64, pa + kk * 8,
+                               tc::smem_desc_sw128(vb + nh * kHalf + kk * 16 * 128, 1024, 1024),
+                               kIdescPV, (j > 0 || kk > 0) ? 1u : 0u);
+            }
+            tc::commit(bar(ws::kPV + hh));
+          }
+          if (ok && j + 1 < nk) {
+            if (hh == 0) ok = wait(ws::kK + ((j + 1) & 1), ((j + 1) >> 1) & 1);
+            if (ok && lane == 0) issue_s(hh, j + 1);
           }
           __syncwarp();
         }
         if (ok && lane == 0) {
-          tc::fence_after_sync();
-          const uint32_t vb = base + ws::kOffV + st * kTile;
-          const uint32_t pa = tmem + ws::kColS + hh * 128;
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-#pragma unroll
-            for (int nh = 0; nh < 2; ++nh)
-              tc::mma_f16_ts(tmem + ws::kColO + hh * 128 + nh * 64, pa + kk * 8,
-                             tc::smem_desc_sw128(vb + nh * kHalf + kk * 16 * 128, 1024, 1024),
-                             kIdescPV, (j > 0 || kk > 0) ? 1u : 0u);
-          }
-          tc::commit(bar(ws::kPV + hh));
-        }
-        if (ok && j + 1 < nk) {
-          if (hh == 0) ok = wait(ws::kK + ((j + 1) & 1), ((j + 1) >> 1) & 1);
-          if (ok && lane == 0) issue_s(hh, j + 1);
+          tc::commit(bar(ws::kFreeV + st));                   // after PV(j) of both heads
+          if (j + 1 < nk) tc::commit(bar(ws::kFreeK + ((j + 1) & 1)));   // after S(j+1)
         }
         __syncwarp();
       }
-      if (ok && lane == 0) {
-        tc::commit(bar(ws::kFreeV + st));                   // after PV(j) of both heads
-        if (j + 1 < nk) tc::commit(bar(ws::kFreeK + ((j + 1) & 1)));   // after S(j+1)
-      }
-      __syncwarp();
     }
   } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(ws::kRegsSoftmax));
     // ---------------- softmax warpgroup hh (rows = TMEM lanes) ----------------
     const int hh = warp >> 2;
     const int row = tid & 127;
@@ -565,55 +583,11 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
     // exceeds it by more than kLazy (log2 units), so P <= 2^kLazy (exact in
     // bf16/f16 range) and O in TMEM is rescaled only on those rare jumps.
     constexpr float kLazy = 8.f;
-    // Padding rows (no query) start from a finite max so they never force the
-    // exact path; all their keys are masked, so P = 0 and l = 0.
+    // Padding rows (no query) start from a finite max; all their keys are
+    // masked, so P = 0 and l = 0.
     float m_run = row_ok ? -INFINITY : 0.f, l_run = 0.f;
-    uint32_t sa[32], sb[32];
+    uint32_t s[4][32];                            // S row of the tile, keys 32*i + c
     bool ok = true;
-    // P of 64 columns (sa = keys 64*half + 0..31, sb = keys 64*half + 32..63)
-    // against max mu, packed two per 32-bit word: pk[c/2] keys c, c+1 of sa and
-    // pk[16 + c/2] of sb.  Returns the row sum of the unrounded values.
-    auto exp_pack = [&](int half, int key0, bool full, float mu, uint32_t (&pk)[32]) {
-      float rs = 0.f;
-#pragma unroll
-      for (int c = 0; c < 32; c += 2) {
-        const int ka = key0 + half * 64 + c;
-        float a = fast_exp2(fmaf(__uint_as_float(sa[c]), p.scale_log2, -mu));
-        float b = fast_exp2(fmaf(__uint_as_float(sa[c + 1]), p.scale_log2, -mu));
-        float x = fast_exp2(fmaf(__uint_as_float(sb[c]), p.scale_log2, -mu));
-        float y = fast_exp2(fmaf(__uint_as_float(sb[c + 1]), p.scale_log2, -mu));
-        if (!full) {
-          a = ka <= kmax ? a : 0.f;
-          b = ka + 1 <= kmax ? b : 0.f;
-          x = ka + 32 <= kmax ? x : 0.f;
-          y = ka + 33 <= kmax ? y : 0.f;
-        }
-        rs += (a + b) + (x + y);
-        pk[c >> 1] = Pack<T>::two(a, b);
-        pk[16 + (c >> 1)] = Pack<T>::two(x, y);
-      }
-      return rs;
-    };
-    auto raw_max = [&](int half, int key0, bool full) {
-      float mx = -INFINITY;
-      if (full) {
-#pragma unroll
-        for (int c = 0; c < 32; ++c)
-          mx = fmaxf(mx, fmaxf(__uint_as_float(sa[c]), __uint_as_float(sb[c])));
-      } else {
-#pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          if (key0 + half * 64 + c <= kmax) mx = fmaxf(mx, __uint_as_float(sa[c]));
-          if (key0 + half * 64 + 32 + c <= kmax) mx = fmaxf(mx, __uint_as_float(sb[c]));
-        }
-      }
-      return mx;
-    };
-    auto load_half = [&](int half) {
-      tc::ld32(s_addr + half * 64, sa);
-      tc::ld32(s_addr + half * 64 + 32, sb);
-      tc::wait_ld();
-    };
     for (int j = 0; j < nk && ok; ++j) {
       // S_h(j) complete implies PV_h(j-1) complete (both issued in order by one
       // thread; a commit covers every earlier MMA): O_h and the P columns are free.
@@ -621,66 +595,62 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
       tc::fence_after_sync();
       const int key0 = j * kBN;
       const bool full = key0 + kBN - 1 <= kmax;   // no key of the tile is masked
-      // Common case, one TMEM read of S: P against the running max, valid while
-      // no score of the tile exceeds it by more than kLazy.  Nothing is written
-      // to TMEM (P overlays S) until both halves have passed that test.
-      bool slow = __any_sync(0xffffffffu, m_run == -INFINITY);
-      float rs = 0.f;
-      if (!slow) {
-        load_half(0);
-        slow = __any_sync(0xffffffffu, raw_max(0, key0, full) * p.scale_log2 > m_run + kLazy);
-        if (!slow) {
-          uint32_t pk0[32];
-          rs = exp_pack(0, key0, full, m_run, pk0);
-          load_half(1);
-          slow = __any_sync(0xffffffffu, raw_max(1, key0, full) * p.scale_log2 > m_run + kLazy);
-          if (!slow) {
-            uint32_t pk1[32];
-            tc::st32(s_addr, pk0);
-            rs += exp_pack(1, key0, full, m_run, pk1);
-            tc::st32(s_addr + 32, pk1);
-          }
-        }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) tc::ld32(s_addr + 32 * i, s[i]);
+      tc::wait_ld();
+      float mx = -INFINITY;
+      if (full) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int c = 0; c < 32; ++c) mx = fmaxf(mx, __uint_as_float(s[i][c]));
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int c = 0; c < 32; ++c)
+            if (key0 + 32 * i + c <= kmax) mx = fmaxf(mx, __uint_as_float(s[i][c]));
       }
+      mx *= p.scale_log2;
       float alpha = 1.f;
-      if (slow) {
-        // exact path: row max over the tile, O rescale, then P from S again
-        load_half(0);
-        float mx = raw_max(0, key0, full);
-        load_half(1);
-        mx = fmaxf(mx, raw_max(1, key0, full)) * p.scale_log2;
-        if (mx > m_run + kLazy || m_run == -INFINITY) {
-          const float m_new = fmaxf(m_run, mx);
-          alpha = m_run == -INFINITY ? 0.f : fast_exp2(m_run - m_new);
-          m_run = m_new;
-        }
-        const float mu = m_run == -INFINITY ? 0.f : m_run;
-        if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+      if (mx > m_run + kLazy) {                   // first tile: m_run = -inf, alpha = 0
+        alpha = fast_exp2(m_run - mx);
+        m_run = mx;
+      }
+      const float mu = m_run == -INFINITY ? 0.f : m_run;
+      // P (keys 2w, 2w+1 packed into column w) over the first 64 columns of S.
+      float rs[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-          for (int cb = 0; cb < 4; cb += 2) {
-            tc::ld32(o_addr + cb * 32, sa);
-            tc::ld32(o_addr + cb * 32 + 32, sb);
-            tc::wait_ld();
+      for (int hb = 0; hb < 2; ++hb) {
+        uint32_t pk[32];
 #pragma unroll
-            for (int c = 0; c < 32; ++c) {
-              sa[c] = __float_as_uint(__uint_as_float(sa[c]) * alpha);
-              sb[c] = __float_as_uint(__uint_as_float(sb[c]) * alpha);
-            }
-            tc::st32(o_addr + cb * 32, sa);
-            tc::st32(o_addr + cb * 32 + 32, sb);
+        for (int w = 0; w < 32; ++w) {
+          const int i = 2 * hb + (w >> 4), c = (w & 15) * 2;
+          const float xa = fmaf(__uint_as_float(s[i][c]), p.scale_log2, -mu);
+          const float xb = fmaf(__uint_as_float(s[i][c + 1]), p.scale_log2, -mu);
+          float a = fast_exp2(xa);
+          float b = fast_exp2(xb);
+          if (!full) {
+            a = key0 + 32 * i + c <= kmax ? a : 0.f;
+            b = key0 + 32 * i + c + 1 <= kmax ? b : 0.f;
           }
-          tc::wait_st();
+          rs[w & 3] += a + b;
+          pk[w] = Pack<T>::two(a, b);
         }
-        rs = 0.f;
+        tc::st32(s_addr + 32 * hb, pk);
+      }
+      l_run = l_run * alpha + ((rs[0] + rs[1]) + (rs[2] + rs[3]));
+      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          uint32_t pk[32];
-          load_half(half);
-          rs += exp_pack(half, key0, full, mu, pk);
-          tc::st32(s_addr + half * 32, pk);
+        for (int i = 0; i < 4; ++i) tc::ld32(o_addr + 32 * i, s[i]);
+        tc::wait_ld();
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+#pragma unroll
+          for (int c = 0; c < 32; ++c) s[i][c] = __float_as_uint(__uint_as_float(s[i][c]) * alpha);
+          tc::st32(o_addr + 32 * i, s[i]);
         }
       }
-      l_run = l_run * alpha + rs;
       tc::wait_st();
       tc::fence_before_sync();
       mbar_arrive(bar(ws::kP + hh));
@@ -693,18 +663,19 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
       T *orow = static_cast<T *>(p.out) + static_cast<int64_t>(q0 + qi) * p.out_st +
                 static_cast<int64_t>(h0 + hh) * p.out_sh;
 #pragma unroll
-      for (int cb = 0; cb < 4; ++cb) {
-        tc::ld32(o_addr + cb * 32, sa);
-        tc::wait_ld();
-        if (row_ok) {
+      for (int i = 0; i < 4; ++i) tc::ld32(o_addr + 32 * i, s[i]);
+      tc::wait_ld();
+      if (row_ok) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
 #pragma unroll
           for (int c = 0; c < 32; c += 8) {
             uint4 w;
-            w.x = Pack<T>::two(__uint_as_float(sa[c]) * inv, __uint_as_float(sa[c + 1]) * inv);
-            w.y = Pack<T>::two(__uint_as_float(sa[c + 2]) * inv, __uint_as_float(sa[c + 3]) * inv);
-            w.z = Pack<T>::two(__uint_as_float(sa[c + 4]) * inv, __uint_as_float(sa[c + 5]) * inv);
-            w.w = Pack<T>::two(__uint_as_float(sa[c + 6]) * inv, __uint_as_float(sa[c + 7]) * inv);
-            *reinterpret_cast<uint4 *>(orow + cb * 32 + c) = w;
+            w.x = Pack<T>::two(__uint_as_float(s[i][c]) * inv, __uint_as_float(s[i][c + 1]) * inv);
+            w.y = Pack<T>::two(__uint_as_float(s[i][c + 2]) * inv, __uint_as_float(s[i][c + 3]) * inv);
+            w.z = Pack<T>::two(__uint_as_float(s[i][c + 4]) * inv, __uint_as_float(s[i][c + 5]) * inv);
+            w.w = Pack<T>::two(__uint_as_float(s[i][c + 6]) * inv, __uint_as_float(s[i][c + 7]) * inv);
+            *reinterpret_cast<uint4 *>(orow + 32 * i + c) = w;
           }
         }
       }
@@ -753,15 +724,21 @@ template <typename T>
 int launch(const Params &p, const CUtensorMap &qm, const CUtensorMap &km, const CUtensorMap &vm,
            int rows, int max_q, cudaStream_t stream) {
   static std::once_flag once;
-  static bool ok = false;
+  static bool ok = false, ws_ok = false;
   std::call_once(once, [] {
     ok = cudaFuncSetAttribute(paged_prefill_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                               kSmemBytes) == cudaSuccess &&
          cudaFuncSetAttribute(paged_prefill_ws_kernel<T>,
                               cudaFuncAttributeMaxDynamicSharedMemorySize, ws::kSmem) == cudaSuccess;
+    // The register split in the two-head kernel hands out exactly the launch
+    // allocation; with any other per-thread count setmaxnreg.inc could not be
+    // satisfied, so that kernel is used only when the build matches.
+    cudaFuncAttributes fa;
+    ws_ok = ok && cudaFuncGetAttributes(&fa, paged_prefill_ws_kernel<T>) == cudaSuccess &&
+            fa.numRegs == ws::kRegsLaunch;
   });
   if (!ok) return SLOKV_ERR_CUDA;
-  if (p.group % 2 == 0) {  // two query heads of one KV head per CTA
+  if (p.group % 2 == 0 && ws_ok) {  // two query heads of one KV head per CTA
     dim3 grid((max_q + kBM - 1) / kBM, p.hq / 2, rows);
     paged_prefill_ws_kernel<T><<<grid, ws::kThreads, ws::kSmem, stream>>>(qm, km, vm, p);
   } else {
