@@ -144,7 +144,16 @@ int slokv_paged_prefill(void *out, int64_t out_stride_t, int64_t out_stride_h,
                         const int32_t *block_tables, int64_t block_table_stride,
                         int32_t max_blocks_per_seq, int32_t num_blocks, int32_t block_size,
                         int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
-                        float softmax_scale, int32_t dtype, uint32_t *dev_error, void *stream);
+                        float softmax_scale, int32_t dtype, void *workspace,
+                        size_t workspace_bytes, uint32_t *dev_error, void *stream);
+
+/* Bytes of the optional prefill workspace: num_rows * ceil(max_seqlen_q / 128)
+ * int32 (rounded up to 256), holding the longest-first order of the query
+ * tiles that a small pre-kernel writes on the same stream.  With a null or
+ * smaller workspace slokv_paged_prefill runs the tiles in row-major order
+ * (same results, longer tail).  No counterpart in the reference (its
+ * flash-attn call schedules internally). */
+size_t slokv_paged_prefill_workspace_bytes(int32_t num_rows, int32_t max_seqlen_q);
 
 /*
  * FP8-E4M3 KV cache.

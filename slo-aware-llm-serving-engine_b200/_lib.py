@@ -64,7 +64,8 @@ SIGNATURES = {
         _c_vp, _c_vp, _c_i32, _c_i32,             # cu_q, cu_k, rows, max_seqlen_q
         _c_vp, _c_i64, _c_i32, _c_i32, _c_i32,    # tables, stride, width, num_blocks, bs
         _c_i32, _c_i32, _c_i32, _c_f32, _c_i32,   # Hq, Hkv, D, scale, dtype
-        _c_vp, _c_vp]),                           # dev_error, stream
+        _c_vp, _c_sz, _c_vp, _c_vp]),             # workspace, bytes, dev_error, stream
+    "slokv_paged_prefill_workspace_bytes": (_c_sz, [_c_i32, _c_i32]),
     "slokv_kv_append_fp8": (ctypes.c_int, [
         _c_vp, _c_i64, _c_vp, _c_i64, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_i32, _c_i32,
         _c_i32, _c_i32, _c_i32, _c_i32, _c_vp, _c_vp]),

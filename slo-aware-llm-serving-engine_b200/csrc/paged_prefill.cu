@@ -62,12 +62,46 @@ struct Params {
   int32_t hq, hkv, group;
   float scale_log2;
   uint32_t *err;
+  // Two-head kernel work order: linear block b runs query tile order[b / (hq/2)]
+  // (row * m_tiles + m, longest first; -1 = no tile); null: row-major order.
+  const int32_t *order;
+  int32_t m_tiles;                        // ceil(max_seqlen_q / 128)
 };
 
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// Three-input max (sm_100).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// Packed pairs of fp32 for the sm_100 f32x2 arithmetic (each lane rounds as
+// the scalar instruction does).
+__device__ __forceinline__ uint64_t f32x2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ float2 f32x2_split(uint64_t v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
 }
 
 template <typename T>
@@ -363,6 +397,78 @@ __global__ void __launch_bounds__(128, 1)
   if (warp == 0) tc::tmem_dealloc(tmem, kTmemCols);
 }
 
+// ---- longest-first work order ------------------------------------------------
+//
+// A query tile's cost is its number of key tiles, which grows along the causal
+// diagonal and with the row's cached prefix.  Blocks are dispatched in linear
+// order, so listing the tiles longest first (list scheduling by decreasing
+// cost) keeps the long tiles out of the last wave.  One block counting-sorts
+// the rows x m_tiles tiles by cost (costs above kSchedBuckets - 1 share the top
+// bucket); ties come out in any order.
+constexpr int kSchedBuckets = 2048;
+constexpr int kSchedThreads = 1024;
+
+__device__ __forceinline__ int tile_cost(const int32_t *cu_q, const int32_t *cu_k, int idx,
+                                         int m_tiles) {
+  const int r = idx / m_tiles, m = idx - r * m_tiles;
+  const int q_len = __ldg(cu_q + r + 1) - __ldg(cu_q + r);
+  if (m * kBM >= q_len) return -1;
+  const int k_len = __ldg(cu_k + r + 1) - __ldg(cu_k + r);
+  const int need = min(k_len, k_len - q_len + min((m + 1) * kBM, q_len));
+  const int nk = need > 0 ? (need + kBN - 1) / kBN : 0;
+  return min(nk, kSchedBuckets - 1);
+}
+
+__global__ void __launch_bounds__(kSchedThreads)
+    prefill_schedule_kernel(const int32_t *cu_q, const int32_t *cu_k, int rows, int m_tiles,
+                            int32_t *order) {
+  __shared__ int start[kSchedBuckets];
+  __shared__ int warp_tot[kSchedThreads / 32];
+  __shared__ int total;
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  const int n = rows * m_tiles;
+  for (int i = tid; i < kSchedBuckets; i += kSchedThreads) start[i] = 0;
+  __syncthreads();
+  for (int i = tid; i < n; i += kSchedThreads) {
+    const int c = tile_cost(cu_q, cu_k, i, m_tiles);
+    if (c >= 0) atomicAdd(&start[c], 1);
+  }
+  __syncthreads();
+  // exclusive scan of the counts from the highest cost down: thread t owns
+  // costs hi = top - 2t and hi - 1
+  static_assert(kSchedBuckets == 2 * kSchedThreads, "two buckets per thread");
+  const int hi = kSchedBuckets - 1 - 2 * tid;
+  const int c_hi = start[hi], c_lo = start[hi - 1];
+  int incl = c_hi + c_lo;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == 31) warp_tot[w] = incl;
+  __syncthreads();
+  if (w == 0) {
+    int t = warp_tot[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, t, o);
+      if (lane >= o) t += y;
+    }
+    warp_tot[lane] = t;                       // inclusive over warps
+    if (lane == 31) total = t;
+  }
+  __syncthreads();
+  const int excl = incl - (c_hi + c_lo) + (w > 0 ? warp_tot[w - 1] : 0);
+  start[hi] = excl;
+  start[hi - 1] = excl + c_hi;
+  __syncthreads();
+  for (int i = tid; i < n; i += kSchedThreads) {
+    const int c = tile_cost(cu_q, cu_k, i, m_tiles);
+    if (c >= 0) order[atomicAdd(&start[c], 1)] = i;
+  }
+  for (int i = total + tid; i < n; i += kSchedThreads) order[i] = -1;
+}
+
 // ---- warp-specialised two-head variant ---------------------------------------
 //
 // One CTA = 128 queries of two query heads that share a KV head (GQA group of
@@ -410,9 +516,20 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
   const int tid = threadIdx.x, lane = tid & 31;
   // warp index made visibly warp-uniform for the compiler (role dispatch, setmaxnreg)
   const int warp = __shfl_sync(0xffffffffu, tid >> 5, 0);
-  const int r = blockIdx.z;
-  const int h0 = 2 * blockIdx.y;                 // query heads h0, h0 + 1
-  const int m = gridDim.x - 1 - blockIdx.x;
+  // 1-D grid: head pair fastest, then query tiles (longest first when ordered)
+  const int pairs = p.hq >> 1;
+  const int rank = blockIdx.x / pairs;
+  const int h0 = 2 * (blockIdx.x - rank * pairs);   // query heads h0, h0 + 1
+  int r, m;
+  if (p.order != nullptr) {
+    const int item = __ldg(p.order + rank);
+    if (item < 0) return;
+    r = item / p.m_tiles;
+    m = item - r * p.m_tiles;
+  } else {
+    r = rank / p.m_tiles;
+    m = p.m_tiles - 1 - (rank - r * p.m_tiles);
+  }
   const int q0 = __ldg(p.cu_q + r), q_len = __ldg(p.cu_q + r + 1) - q0;
   const int k0 = __ldg(p.cu_k + r), k_len = __ldg(p.cu_k + r + 1) - k0;
   if (m * kBM >= q_len) return;
@@ -618,28 +735,31 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
         m_run = mx;
       }
       const float mu = m_run == -INFINITY ? 0.f : m_run;
-      // P (keys 2w, 2w+1 packed into column w) over the first 64 columns of S.
-      float rs[4] = {0.f, 0.f, 0.f, 0.f};
+      // P (keys 2w, 2w+1 packed into column w) over the first 64 columns of S;
+      // the scale-and-shift and the row sum run two keys per f32x2 instruction.
+      const uint64_t sl2 = f32x2(p.scale_log2, p.scale_log2), nmu2 = f32x2(-mu, -mu);
+      uint64_t rs2[4] = {0ull, 0ull, 0ull, 0ull};  // {0.f, 0.f}
 #pragma unroll
       for (int hb = 0; hb < 2; ++hb) {
         uint32_t pk[32];
 #pragma unroll
         for (int w = 0; w < 32; ++w) {
           const int i = 2 * hb + (w >> 4), c = (w & 15) * 2;
-          const float xa = fmaf(__uint_as_float(s[i][c]), p.scale_log2, -mu);
-          const float xb = fmaf(__uint_as_float(s[i][c + 1]), p.scale_log2, -mu);
-          float a = fast_exp2(xa);
-          float b = fast_exp2(xb);
+          const float2 x = f32x2_split(ffma2(
+              f32x2(__uint_as_float(s[i][c]), __uint_as_float(s[i][c + 1])), sl2, nmu2));
+          float a = fast_exp2(x.x);
+          float b = fast_exp2(x.y);
           if (!full) {
             a = key0 + 32 * i + c <= kmax ? a : 0.f;
             b = key0 + 32 * i + c + 1 <= kmax ? b : 0.f;
           }
-          rs[w & 3] += a + b;
+          rs2[w & 3] = fadd2(rs2[w & 3], f32x2(a, b));
           pk[w] = Pack<T>::two(a, b);
         }
         tc::st32(s_addr + 32 * hb, pk);
       }
-      l_run = l_run * alpha + ((rs[0] + rs[1]) + (rs[2] + rs[3]));
+      const float2 r01 = f32x2_split(fadd2(rs2[0], rs2[1])), r23 = f32x2_split(fadd2(rs2[2], rs2[3]));
+      l_run = l_run * alpha + ((r01.x + r01.y) + (r23.x + r23.y));
       if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll
         for (int i = 0; i < 4; ++i) tc::ld32(o_addr + 32 * i, s[i]);
@@ -739,8 +859,14 @@ int launch(const Params &p, const CUtensorMap &qm, const CUtensorMap &km, const 
   });
   if (!ok) return SLOKV_ERR_CUDA;
   if (p.group % 2 == 0 && ws_ok) {  // two query heads of one KV head per CTA
-    dim3 grid((max_q + kBM - 1) / kBM, p.hq / 2, rows);
-    paged_prefill_ws_kernel<T><<<grid, ws::kThreads, ws::kSmem, stream>>>(qm, km, vm, p);
+    if (p.order != nullptr) {
+      prefill_schedule_kernel<<<1, kSchedThreads, 0, stream>>>(
+          p.cu_q, p.cu_k, rows, p.m_tiles, const_cast<int32_t *>(p.order));
+    }
+    const int64_t blocks = static_cast<int64_t>(rows) * p.m_tiles * (p.hq / 2);
+    if (blocks > 0x7fffffff) return SLOKV_ERR_UNSUPPORTED;
+    paged_prefill_ws_kernel<T><<<static_cast<unsigned>(blocks), ws::kThreads, ws::kSmem,
+                                 stream>>>(qm, km, vm, p);
   } else {
     dim3 grid((max_q + kBM - 1) / kBM, p.hq, rows);
     paged_prefill_kernel<T><<<grid, 128, kSmemBytes, stream>>>(qm, km, vm, p);
@@ -750,6 +876,14 @@ int launch(const Params &p, const CUtensorMap &qm, const CUtensorMap &km, const 
 
 }  // namespace prefill
 }  // namespace slokv
+
+extern "C" size_t slokv_paged_prefill_workspace_bytes(int32_t num_rows, int32_t max_seqlen_q) {
+  if (num_rows <= 0 || max_seqlen_q <= 0) return 0;
+  const size_t items = static_cast<size_t>(num_rows) *
+                       static_cast<size_t>((max_seqlen_q + slokv::prefill::kBM - 1) /
+                                           slokv::prefill::kBM);
+  return (items * sizeof(int32_t) + 255) & ~static_cast<size_t>(255);
+}
 
 extern "C" int slokv_paged_prefill(void *out, int64_t out_stride_t, int64_t out_stride_h,
                                    const void *q, int64_t q_stride_t, int64_t q_stride_h,
@@ -762,6 +896,7 @@ extern "C" int slokv_paged_prefill(void *out, int64_t out_stride_t, int64_t out_
                                    int32_t max_blocks_per_seq, int32_t num_blocks,
                                    int32_t block_size, int32_t num_q_heads, int32_t num_kv_heads,
                                    int32_t head_dim, float softmax_scale, int32_t dtype,
+                                   void *workspace, size_t workspace_bytes,
                                    uint32_t *dev_error, void *stream) {
   using namespace slokv;
   using namespace slokv::prefill;
@@ -816,6 +951,14 @@ extern "C" int slokv_paged_prefill(void *out, int64_t out_stride_t, int64_t out_
   p.group = num_q_heads / num_kv_heads;
   p.scale_log2 = softmax_scale * 1.4426950408889634f;
   p.err = dev_error;
+  p.m_tiles = (max_seqlen_q + kBM - 1) / kBM;
+  // The work order needs rows x m_tiles int32 (slokv_paged_prefill_workspace_bytes);
+  // without it the tiles run in row-major order.
+  p.order = workspace != nullptr &&
+                    workspace_bytes >= slokv_paged_prefill_workspace_bytes(num_rows, max_seqlen_q) &&
+                    (reinterpret_cast<uintptr_t>(workspace) & 3u) == 0
+                ? static_cast<const int32_t *>(workspace)
+                : nullptr;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   return dtype == SLOKV_DTYPE_BF16
              ? launch<__nv_bfloat16>(p, qm, km, vm, num_rows, max_seqlen_q, st)

@@ -350,8 +350,30 @@ def flash_attn_varlen_func(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, ma
     if Tq == 0 or rows == 0:
         return out
     err = buffers.error_word(dev)
+    ws, ws_bytes = _prefill_workspace(dev, rows, int(max_seqlen_q))
     check(lib().slokv_paged_prefill(
         out.data_ptr(), out.stride(0), out.stride(1), q.data_ptr(), q.stride(0), q.stride(1), Tq,
-        *args, Hq, Hkv, D, scale, _lib.dtype_code(q.dtype), err.data_ptr(), stream_ptr(dev)),
+        *args, Hq, Hkv, D, scale, _lib.dtype_code(q.dtype), ws, ws_bytes, err.data_ptr(),
+        stream_ptr(dev)),
         "paged_prefill")
     return out
+
+
+# Smallest prefill work-order buffer (16K query tiles, e.g. 256 rows of 8K-token
+# chunks), so graphs captured after a small warm-up rarely need a larger one.
+_PREFILL_WS_MIN = 64 << 10
+
+
+def _prefill_workspace(dev: torch.device, rows: int, max_seqlen_q: int):
+    """(pointer, bytes) of the per-device prefill work-order buffer.  During graph
+    capture a buffer too small for this geometry is not grown: the call then
+    passes none and the tiles run in row-major order (same results)."""
+    need = lib().slokv_paged_prefill_workspace_bytes(rows, max_seqlen_q)
+    if need == 0:
+        return None, 0
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    t = buffers._ws.get((idx, "prefill"))
+    if (t is None or t.numel() < need) and torch.cuda.is_current_stream_capturing():
+        return None, 0
+    t = buffers.workspace(dev, "prefill", max(need, _PREFILL_WS_MIN))
+    return t.data_ptr(), t.numel()

@@ -203,3 +203,31 @@ def test_attention_module_prefill_with_prefix_cache(pkg):
     out = attn(q.cuda(), k.cuda(), v.cuda())
     pkg.reset_context()
     assert_attn_close(out, expect)
+
+
+@pytest.mark.parametrize("q_lens,hist,seed", [
+    ([2048, 2048, 2048], [0, 1024, 3072], 5400),
+    ([1, 127, 128, 129, 300, 2000, 5], [0, 5, 256, 1000, 40, 9000, 3], 5401),
+])
+def test_longest_first_order_matches_row_major(pkg, q_lens, hist, seed):
+    """The longest-first work order (workspace given) and the row-major order
+    (no workspace) compute every query tile identically: outputs bit-equal."""
+    from importlib import import_module
+    _lib = import_module("slo-aware-llm-serving-engine_b200._lib")
+    q, kc, vc, cu_q, cu_k, tables, mq, mk = _varlen_case(seed, q_lens, hist, 32, 8)
+    q, kc, vc, cu_q, cu_k, tables = (t.cuda() for t in (q, kc, vc, cu_q, cu_k, tables))
+    ordered = pkg.flash_attn_varlen_func(q, kc, vc, cu_q, cu_k, mq, mk,
+                                         softmax_scale=128 ** -0.5, block_table=tables)
+    plain = torch.full_like(ordered, float("nan"))
+    rows = cu_q.numel() - 1
+    assert _lib.lib().slokv_paged_prefill_workspace_bytes(rows, mq) >= rows * ((mq + 127) // 128) * 4
+    err = _lib.buffers.error_word(q.device)
+    _lib.check(_lib.lib().slokv_paged_prefill(
+        plain.data_ptr(), plain.stride(0), plain.stride(1), q.data_ptr(), q.stride(0), q.stride(1),
+        q.shape[0], kc.data_ptr(), vc.data_ptr(), 0, 0, 0, kc.stride(0), vc.stride(0),
+        cu_q.data_ptr(), cu_k.data_ptr(), rows, mq, tables.data_ptr(), tables.stride(0),
+        tables.shape[1], kc.shape[0], 256, 32, 8, 128, 128 ** -0.5, _lib.DTYPE_BF16, None, 0,
+        err.data_ptr(), _lib.stream_ptr(q.device)), "paged_prefill")
+    torch.cuda.synchronize()
+    assert torch.equal(ordered, plain)
+    assert pkg.read_device_errors() == 0
