@@ -715,19 +715,18 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
 #pragma unroll
       for (int i = 0; i < 4; ++i) tc::ld32(s_addr + 32 * i, s[i]);
       tc::wait_ld();
-      float mx = -INFINITY;
-      if (full) {
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-#pragma unroll
-          for (int c = 0; c < 32; ++c) mx = fmaxf(mx, __uint_as_float(s[i][c]));
-      } else {
+      if (!full) {                                // masked keys -> -inf (exp2 -> 0)
 #pragma unroll
         for (int i = 0; i < 4; ++i)
 #pragma unroll
           for (int c = 0; c < 32; ++c)
-            if (key0 + 32 * i + c <= kmax) mx = fmaxf(mx, __uint_as_float(s[i][c]));
+            if (key0 + 32 * i + c > kmax) s[i][c] = 0xff800000u;
       }
+      float mx = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int c = 0; c < 32; ++c) mx = fmaxf(mx, __uint_as_float(s[i][c]));
       mx *= p.scale_log2;
       float alpha = 1.f;
       if (mx > m_run + kLazy) {                   // first tile: m_run = -inf, alpha = 0
@@ -747,12 +746,8 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
           const int i = 2 * hb + (w >> 4), c = (w & 15) * 2;
           const float2 x = f32x2_split(ffma2(
               f32x2(__uint_as_float(s[i][c]), __uint_as_float(s[i][c + 1])), sl2, nmu2));
-          float a = fast_exp2(x.x);
-          float b = fast_exp2(x.y);
-          if (!full) {
-            a = key0 + 32 * i + c <= kmax ? a : 0.f;
-            b = key0 + 32 * i + c + 1 <= kmax ? b : 0.f;
-          }
+          const float a = fast_exp2(x.x);
+          const float b = fast_exp2(x.y);
           rs2[w & 3] = fadd2(rs2[w & 3], f32x2(a, b));
           pk[w] = Pack<T>::two(a, b);
         }
