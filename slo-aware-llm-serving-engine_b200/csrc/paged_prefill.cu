@@ -511,7 +511,7 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
                             const __grid_constant__ CUtensorMap vmap, const Params p) {
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
   constexpr uint32_t kIdescS = tc::idesc_f16(kBf16, false, 128, 128);
-  constexpr uint32_t kIdescPV = tc::idesc_f16(kBf16, true, 128, 64);
+  constexpr uint32_t kIdescPV = tc::idesc_f16(kBf16, true, 128, 128);
 
   const int tid = threadIdx.x, lane = tid & 31;
   // warp index made visibly warp-uniform for the compiler (role dispatch, setmaxnreg)
@@ -662,14 +662,14 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
             tc::fence_after_sync();
             const uint32_t vb = base + ws::kOffV + st * kTile;
             const uint32_t pa = tmem + ws::kColS + hh * 128;
+            // N = 128 in one instruction: V is MN-major with the two 64-dim
+            // halves (128-byte swizzle atoms along N) kHalf bytes apart (LBO);
+            // 8-key row groups are 1024 bytes apart (SBO).
 #pragma unroll
-            for (int kk = 0; kk < 8; ++kk) {
-#pragma unroll
-              for (int nh = 0; nh < 2; ++nh)
-                tc::mma_f16_ts(tmem + ws::kColO + hh * 128 + nh * 64, pa + kk * 8,
-                               tc::smem_desc_sw128(vb + nh * kHalf + kk * 16 * 128, 1024, 1024),
-                               kIdescPV, (j > 0 || kk > 0) ? 1u : 0u);
-            }
+            for (int kk = 0; kk < 8; ++kk)
+              tc::mma_f16_ts(tmem + ws::kColO + hh * 128, pa + kk * 8,
+                             tc::smem_desc_sw128(vb + kk * 16 * 128, kHalf, 1024), kIdescPV,
+                             (j > 0 || kk > 0) ? 1u : 0u);
             tc::commit(bar(ws::kPV + hh));
           }
           if (ok && j + 1 < nk) {
