@@ -9,7 +9,12 @@
 // from contiguous k/v rows (cold prefill).  GQA: query head h uses kv head
 // h / (Hq/Hkv).
 //
-// Design (one CTA = 128 queries of one head of one row, 4 warps):
+// Two kernels.  GQA groups of even size (the engine's geometries) run the
+// warp-specialised two-head kernel further down (two query heads share one
+// K/V stream; tensor-core issue, TMA and two softmax warpgroups in separate
+// warps, P kept in TMEM).  Odd groups run the single-head kernel described here.
+//
+// Single-head design (one CTA = 128 queries of one head of one row, 4 warps):
 //  * TMA loads Q once and K/V tiles of 128 keys (two 64-dim halves each,
 //    128-byte swizzle = the canonical K-major UMMA layout) into double-buffered
 //    K and V rings; every CTA loads its own tiles.
@@ -696,46 +701,19 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
     const int kmax = row_ok ? min(qk_off + qi, k_len - 1) : -1;
     const uint32_t s_addr = tmem + lane_base + ws::kColS + hh * 128;
     const uint32_t o_addr = tmem + lane_base + ws::kColO + hh * 128;
-    // Lazy rescaling: the row keeps using a stale max m_run until the tile max
-    // exceeds it by more than kLazy (log2 units), so P <= 2^kLazy (exact in
-    // bf16/f16 range) and O in TMEM is rescaled only on those rare jumps.
-    constexpr float kLazy = 8.f;
+    // Lazy rescaling: the row keeps a stale max m_run while a tile's P row sum
+    // against it stays <= kSumLimit, so every P <= 2^8 (exact in the bf16/f16
+    // range) and O in TMEM is rescaled only when that bound would break.
+    constexpr float kSumLimit = 256.f;
     // Padding rows (no query) start from a finite max; all their keys are
     // masked, so P = 0 and l = 0.
     float m_run = row_ok ? -INFINITY : 0.f, l_run = 0.f;
     uint32_t s[4][32];                            // S row of the tile, keys 32*i + c
     bool ok = true;
-    for (int j = 0; j < nk && ok; ++j) {
-      // S_h(j) complete implies PV_h(j-1) complete (both issued in order by one
-      // thread; a commit covers every earlier MMA): O_h and the P columns are free.
-      ok = wait(ws::kS + hh, j & 1);
-      tc::fence_after_sync();
-      const int key0 = j * kBN;
-      const bool full = key0 + kBN - 1 <= kmax;   // no key of the tile is masked
-#pragma unroll
-      for (int i = 0; i < 4; ++i) tc::ld32(s_addr + 32 * i, s[i]);
-      tc::wait_ld();
-      if (!full) {                                // masked keys -> -inf (exp2 -> 0)
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-#pragma unroll
-          for (int c = 0; c < 32; ++c)
-            if (key0 + 32 * i + c > kmax) s[i][c] = 0xff800000u;
-      }
-      float mx = -INFINITY;
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int c = 0; c < 32; ++c) mx = fmaxf(mx, __uint_as_float(s[i][c]));
-      mx *= p.scale_log2;
-      float alpha = 1.f;
-      if (mx > m_run + kLazy) {                   // first tile: m_run = -inf, alpha = 0
-        alpha = fast_exp2(m_run - mx);
-        m_run = mx;
-      }
-      const float mu = m_run == -INFINITY ? 0.f : m_run;
-      // P (keys 2w, 2w+1 packed into column w) over the first 64 columns of S;
-      // the scale-and-shift and the row sum run two keys per f32x2 instruction.
+    // P = 2^(S * scale_log2 - mu) of the S row in registers, packed (keys 2w,
+    // 2w+1 in column w) over the first 64 columns of S; returns the row sum.
+    // The scale-and-shift and the sum run two keys per f32x2 instruction.
+    auto exp_store = [&](float mu) {
       const uint64_t sl2 = f32x2(p.scale_log2, p.scale_log2), nmu2 = f32x2(-mu, -mu);
       uint64_t rs2[4] = {0ull, 0ull, 0ull, 0ull};  // {0.f, 0.f}
 #pragma unroll
@@ -753,8 +731,52 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
         }
         tc::st32(s_addr + 32 * hb, pk);
       }
-      const float2 r01 = f32x2_split(fadd2(rs2[0], rs2[1])), r23 = f32x2_split(fadd2(rs2[2], rs2[3]));
-      l_run = l_run * alpha + ((r01.x + r01.y) + (r23.x + r23.y));
+      const float2 r01 = f32x2_split(fadd2(rs2[0], rs2[1]));
+      const float2 r23 = f32x2_split(fadd2(rs2[2], rs2[3]));
+      return (r01.x + r01.y) + (r23.x + r23.y);
+    };
+    for (int j = 0; j < nk && ok; ++j) {
+      // S_h(j) complete implies PV_h(j-1) complete (both issued in order by one
+      // thread; a commit covers every earlier MMA): O_h and the P columns are free.
+      ok = wait(ws::kS + hh, j & 1);
+      tc::fence_after_sync();
+      const int key0 = j * kBN;
+      const bool full = key0 + kBN - 1 <= kmax;   // no key of the tile is masked
+#pragma unroll
+      for (int i = 0; i < 4; ++i) tc::ld32(s_addr + 32 * i, s[i]);
+      tc::wait_ld();
+      if (!full) {                                // masked keys -> -inf (exp2 -> 0)
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int c = 0; c < 32; ++c)
+            if (key0 + 32 * i + c > kmax) s[i][c] = 0xff800000u;
+      }
+      // P against the running max without a row max first.  A warp with a row
+      // sum above kSumLimit (or on a row's first tile) takes the row max,
+      // rescales and recomputes P from the S row still in registers.
+      const bool fresh = __any_sync(0xffffffffu, m_run == -INFINITY);
+      float alpha = 1.f, rs = 0.f;
+      bool redo = fresh;
+      if (!fresh) {
+        rs = exp_store(m_run);
+        redo = __any_sync(0xffffffffu, !(rs <= kSumLimit));
+      }
+      if (redo) {
+        float mx = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int c = 0; c < 32; ++c) mx = fmaxf(mx, __uint_as_float(s[i][c]));
+        mx *= p.scale_log2;
+        if (mx > m_run) {                          // first tile: m_run = -inf, alpha = 0
+          alpha = fast_exp2(m_run - mx);
+          m_run = mx;
+        }
+        if (!fresh) tc::wait_st();                 // first P stores land before rewrite
+        rs = exp_store(m_run == -INFINITY ? 0.f : m_run);
+      }
+      l_run = l_run * alpha + rs;
       if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll
         for (int i = 0; i < 4; ++i) tc::ld32(o_addr + 32 * i, s[i]);
