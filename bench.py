@@ -620,7 +620,8 @@ def run_mixed(args):
                      "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind_str(kind),
                      "algorithmic_flops": flops, "launch_ms": round(pre_ms, 4), "traffic": None},
-        "gpu_launches": args.steps * L * 4,
+        # per layer: append, decode + merge, prefill work order + prefill
+        "gpu_launches": args.steps * L * 5,
         "clocks": clocks.summary(),
         "device_errors": pkg.read_device_errors(),
     }

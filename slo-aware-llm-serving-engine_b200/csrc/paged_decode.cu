@@ -654,43 +654,42 @@ __global__ void __launch_bounds__(Ring<kFp8>::kWarpsPerCta * 32, 1)
   if (lane == 0) p.jobs[s] = job;
 }
 
-// Combine the partials of every segment that straddles warp ranges.  One warp
+// Combine the partials of every segment that straddles warp ranges.  One CTA
 // per warp slot of the main kernel; the slot's job names the segment whose
 // last piece it holds (pieces: slot s_lo's tail partial, then the head partial
-// of every non-empty slot up to this one).  Lane l owns dims [4l, 4l+4).
+// of every non-empty slot up to this one).  Warp w merges query-head rows w,
+// w + 4, ... in one pass with a running max, so each piece costs one round of
+// independent loads; lane l owns dims [4l, 4l+4).
 template <typename T>
 __global__ void __launch_bounds__(128) paged_decode_merge_kernel(const Params p) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t s = static_cast<int64_t>(blockIdx.x) * 4 + warp;
+  const int64_t s = blockIdx.x;
   if (s >= p.nslots) return;
   const int4 job = p.jobs[s];
   if (job.x < 0) return;
   const int G = p.group;
   const int64_t total = job.w, s_lo = job.z;
-  for (int row = 0; row < G; ++row) {
-    float mmax = -INFINITY;
+  for (int row = warp; row < G; row += 4) {
+    float m = -INFINITY, l = 0.f;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
     for (int64_t t = s_lo; t <= s; ++t) {
       if (t > s_lo && range_start(t + 1, total, p.nslots) == range_start(t, total, p.nslots))
         continue;
       const float *pr = p.partials + ((t * 2 + (t == s_lo ? 1 : 0)) * G + row) *
                                          static_cast<int64_t>(kRowFloats);
-      mmax = fmaxf(mmax, pr[0]);
-    }
-    float acc[4] = {0.f, 0.f, 0.f, 0.f}, lsum = 0.f;
-    for (int64_t t = s_lo; t <= s; ++t) {
-      if (t > s_lo && range_start(t + 1, total, p.nslots) == range_start(t, total, p.nslots))
-        continue;
-      const float *pr = p.partials + ((t * 2 + (t == s_lo ? 1 : 0)) * G + row) *
-                                         static_cast<int64_t>(kRowFloats);
-      const float w = fast_exp2(pr[0] - mmax);
-      lsum += w * pr[1];
+      const float mt = pr[0], lt = pr[1];
       const float4 v = *reinterpret_cast<const float4 *>(pr + kAccOff + lane * 4);
-      acc[0] += w * v.x;
-      acc[1] += w * v.y;
-      acc[2] += w * v.z;
-      acc[3] += w * v.w;
+      const float mn = fmaxf(m, mt);
+      const float a = m == -INFINITY ? 0.f : fast_exp2(m - mn);
+      const float b = mt == -INFINITY ? 0.f : fast_exp2(mt - mn);
+      l = l * a + lt * b;
+      acc[0] = acc[0] * a + v.x * b;
+      acc[1] = acc[1] * a + v.y * b;
+      acc[2] = acc[2] * a + v.z * b;
+      acc[3] = acc[3] * a + v.w * b;
+      m = mn;
     }
-    const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+    const float inv = l > 0.f ? 1.f / l : 0.f;
     T *ob = static_cast<T *>(p.out) + static_cast<int64_t>(job.x) * p.out_sb +
             static_cast<int64_t>(job.y * G + row) * p.out_sh + lane * 4;
     *reinterpret_cast<uint2 *>(ob) = make_uint2(Mma<T>::pack(acc[0] * inv, acc[1] * inv),
@@ -769,7 +768,7 @@ int launch(const Params &p0, const CUtensorMap &km, const CUtensorMap &vm, int s
   if (!ok) return SLOKV_ERR_CUDA;
   paged_decode_kernel<T, kFp8><<<sms, kW * 32, smem, stream>>>(km, vm, p0);
   if (cudaGetLastError() != cudaSuccess) return SLOKV_ERR_CUDA;
-  paged_decode_merge_kernel<T><<<(p0.nslots + 3) / 4, 128, 0, stream>>>(p0);
+  paged_decode_merge_kernel<T><<<p0.nslots, 128, 0, stream>>>(p0);
   return cudaGetLastError() == cudaSuccess ? SLOKV_OK : SLOKV_ERR_CUDA;
 }
 
