@@ -607,6 +607,12 @@ def run_mixed(args):
     flops = 4 * HQ * D * pairs
     peak, kind = measured_tensor_peak()
     achieved = flops / (pre_ms * 1e-3) / 1e12
+    traffic = None
+    try:
+        with open(os.path.join(ROOT, "profiles", "paged_prefill_traffic.json")) as f:
+            traffic = json.load(f).get("dram_bytes_per_launch")
+    except Exception:
+        pass
     line = {
         "metric": "mixed prefill/decode step tokens/s (config 3) and prefill tensor TFLOP/s",
         "value": round(T / (ms * 1e-3), 1), "unit": "tok/s", "n_gpus": 1, "steps": args.steps,
@@ -619,7 +625,8 @@ def run_mixed(args):
         "roofline": {"kernel": "paged_prefill (tcgen05, one layer)", "bound": "tensor",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind_str(kind),
-                     "algorithmic_flops": flops, "launch_ms": round(pre_ms, 4), "traffic": None},
+                     "algorithmic_flops": flops, "launch_ms": round(pre_ms, 4),
+                     "traffic": traffic},
         # per layer: append, decode + merge, prefill work order + prefill
         "gpu_launches": args.steps * L * 5,
         "clocks": clocks.summary(),
