@@ -691,6 +691,103 @@ def run_copy(args):
         "gpu_launches": args.steps, "clocks": clocks.summary()}), flush=True)
 
 
+MODEL_METRIC = "full-model greedy decode tokens/s, random-init Qwen3-4B (config 5), TP = n_gpus"
+
+
+def run_model(args):
+    """random-init Qwen3-4B (36 layers, N(0, 0.02) weights)
+    decode step at TP = --gpus.  Prompts of random ids with context U[512, 4096]
+    are prefilled through the tcgen05 varlen kernel, then the graph-captured
+    decode step (dense torch + this package's append / paged decode, NCCL
+    all-reduce after o_proj and down_proj) is timed; max over ranks."""
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=device)
+    h = importlib.import_module("slo-aware-llm-serving-engine_b200.qwen3_harness")
+    pkg = importlib.import_module("slo-aware-llm-serving-engine_b200")
+    cfg = h.Qwen3Config()
+    B = args.batch
+    gen = torch.Generator().manual_seed(5)
+    lens = torch.randint(args.ctx_lo, args.ctx_hi + 1, (B,), generator=gen).tolist()
+    ids = torch.randint(0, cfg.vocab_size, (sum(lens),), generator=gen).tolist()
+    prompts, cur = [], 0
+    for n in lens:
+        prompts.append(ids[cur:cur + n])
+        cur += n
+    model = h.Qwen3Model(cfg, rank, world, None, seed=0, device=device)
+    runner = h.GreedyRunner(model, lens, args.warmup + args.steps + 2, seed=1, kv_dtype=args.kv)
+    t0 = time.time()
+    tok = runner.prefill(prompts, chunk_tokens=32768)
+    torch.cuda.synchronize()
+    prefill_s = time.time() - t0
+    for _ in range(args.warmup):
+        tok = runner.decode(tok)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = Clocks(device)
+    with clocks:
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+        start.record()
+        for _ in range(args.steps):
+            tok = runner.decode(tok)
+        end.record()
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+    ms = start.elapsed_time(end) / args.steps
+    errs = pkg.read_device_errors()
+    t = torch.tensor([ms], device=device)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = t.item()
+    if rank == 0:
+        # per-rank HBM bytes of one step: the KV read by attention (mean context
+        # over the timed steps) + the append + this rank's weights
+        ctx = sum(lens) + B * (args.warmup + args.steps // 2 + 1)
+        kv_bytes = 2 * cfg.num_layers * ctx * runner.model.hkv * cfg.head_dim * (
+            1 if args.kv == "fp8" else 2)
+        w_bytes = sum(t.numel() * 2 for lw in model.layers
+                      for t in (lw.wqkv, lw.wo, lw.wgu, lw.wd)) + model.embed.numel() * 2
+        peak, peak_kind = measured_hbm_peak()
+        achieved = (kv_bytes + w_bytes) / (ms * 1e-3) / 1e9
+        line = {
+            "metric": MODEL_METRIC, "value": round(B / (ms * 1e-3), 1), "unit": "tok/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic: random-init weights "
+            "N(0, 0.02), random prompt ids (seed 5)",
+            "config": {"workload": "BASELINE config 5: random-init Qwen3-4B greedy decode step "
+                                   f"(36 layers), batch {B}, context U[{args.ctx_lo}, "
+                                   f"{args.ctx_hi}] after prefill, KV {args.kv}",
+                       "parallelism": f"tp{world}", "global_batch": B,
+                       "prefill_seconds": round(prefill_s, 2)},
+            "roofline": {"kernel": "whole decode step per rank (KV read + weights)",
+                         "bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "peak_kind": peak_kind, "algorithmic_bytes": kv_bytes + w_bytes,
+                         "traffic": None},
+            "clocks": clocks.summary(),
+            "device_errors": errs,
+        }
+        print(json.dumps(line), flush=True)
+    runner.release()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def peak_kind_str(kind):
     return f"{kind} bf16 dense (burst)"
 
@@ -735,8 +832,9 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["decode", "mixed", "copy"], default="decode",
-                    help="decode: config 2/4 (the headline); mixed: config 3 prefill + decode")
+    ap.add_argument("--workload", choices=["decode", "mixed", "copy", "model"], default="decode",
+                    help="decode: config 2/4 (the headline); mixed: config 3 prefill + decode; "
+                         "model: config 5 full random-init model at TP = --gpus")
     ap.add_argument("--kv", choices=["bf16", "fp8"], default="bf16",
                     help="cache format: bf16 (config 2, the headline) or fp8 (config 4)")
     ap.add_argument("--batch", type=int, default=None, help="sequences per GPU")
@@ -752,6 +850,13 @@ def main():
     ap.add_argument("--cpu-batch", type=int, default=BATCH_PER_GPU)
     args = ap.parse_args()
     fp8_defaults = args.kv == "fp8"
+    if args.workload == "model":
+        # config 5: batch 512, context U[512, 4096]; at TP = 1 a bf16 cache of
+        # that batch (~174 GB) does not fit one B200, so TP = 1 bf16 runs 256
+        if args.batch is None:
+            args.batch = 512 if (args.gpus > 1 or fp8_defaults) else 256
+        args.ctx_lo = args.ctx_lo or CTX_LO
+        args.ctx_hi = args.ctx_hi or CTX_HI
     if args.batch is None:
         args.batch = 128 if fp8_defaults else BATCH_PER_GPU
     if args.ctx_lo is None:
@@ -767,6 +872,8 @@ def main():
         run_mixed(args)
     elif args.workload == "copy":
         run_copy(args)
+    elif args.workload == "model":
+        run_model(args)
     else:
         run_ours(args)
 

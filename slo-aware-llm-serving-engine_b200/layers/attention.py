@@ -55,10 +55,18 @@ class Attention(nn.Module):
                                        softmax_scale=self.scale, causal=True)
 
     def _forward_fp8(self, q, k, v, context):
-        if context.mixed is not None or context.is_prefill:
-            raise RuntimeError("the FP8 KV pool is supported on the decode path only")
+        cold_prefill = context.is_prefill and context.block_tables is None
+        if context.mixed is not None or (context.is_prefill and not cold_prefill):
+            raise RuntimeError("the FP8 KV pool supports decode and cold (no prefix) prefill only")
         store_kvcache_fp8(k, v, self.k_cache, self.v_cache, self.k_scale, self.v_scale,
                           context.slot_mapping)
+        if cold_prefill:     # keys are the step's own bf16 k/v; the pool only stores codes
+            return flash_attn_varlen_func(q, k, v,
+                                          max_seqlen_q=context.max_seqlen_q,
+                                          cu_seqlens_q=context.cu_seqlens_q,
+                                          max_seqlen_k=context.max_seqlen_k,
+                                          cu_seqlens_k=context.cu_seqlens_k,
+                                          softmax_scale=self.scale, causal=True)
         return flash_attn_with_kvcache_fp8(q.unsqueeze(1), self.k_cache, self.v_cache,
                                            self.k_scale, self.v_scale,
                                            cache_seqlens=context.context_lens,
