@@ -164,33 +164,68 @@ __device__ __forceinline__ int64_t owner_slot(int64_t t, int64_t total, int64_t 
   return s;
 }
 
-// Issue the TMA loads of global tile t into `stage` of this warp's ring.
-template <bool kFp8>
-__device__ __forceinline__ void issue_tile(const Params &p, const int32_t *prefix,
-                                           const CUtensorMap *kmap, const CUtensorMap *vmap,
-                                           uint32_t ring, uint32_t bars, int stage, int64_t t,
-                                           uint64_t policy) {
+// The next tile a warp's producer lane issues, advanced tile by tile in the
+// work-list order (segment (b, h) after segment, tiles in order) so the issue
+// path needs no search; the page's block id is read once per page.
+struct IssueCursor {
+  int32_t b, h, j, nt, page, blk;
+};
+
+__device__ __forceinline__ void cursor_init(IssueCursor &c, const Params &p,
+                                            const int32_t *prefix, int64_t t) {
   const TileRef r = locate(p, prefix, t);
+  c.b = r.b;
+  c.h = r.h;
+  c.j = r.j;
+  c.nt = r.nt;
+  c.page = -1;
+  c.blk = 0;
+}
+
+// Step to the following tile; call only when one exists (it then lies in a
+// later non-empty sequence at worst, so b stays below batch).
+__device__ __forceinline__ void cursor_next(IssueCursor &c, const Params &p,
+                                            const int32_t *prefix) {
+  if (++c.j < c.nt) return;
+  c.j = 0;
+  c.page = -1;
+  if (++c.h < p.hkv) return;
+  c.h = 0;
+  do {
+    ++c.b;
+    c.nt = (prefix[c.b + 1] - prefix[c.b]) / p.hkv;
+  } while (c.nt == 0 && c.b + 1 < p.batch);
+}
+
+// Issue the TMA loads of the cursor's tile into `stage` of this warp's ring.
+template <bool kFp8>
+__device__ __forceinline__ void issue_cursor_tile(const Params &p, IssueCursor &c,
+                                                  const CUtensorMap *kmap,
+                                                  const CUtensorMap *vmap, uint32_t ring,
+                                                  uint32_t bars, int stage, uint64_t policy) {
   const int tiles_per_block = p.block_size / kTile;
-  const int page = r.j / tiles_per_block;
-  const int off = (r.j - page * tiles_per_block) * kTile;
-  const int32_t blk = __ldg(p.block_tables + static_cast<int64_t>(r.b) * p.bt_stride + page);
-  if (blk < 0 || blk >= p.num_blocks) record_error(p.err, SLOKV_DEVERR_BLOCK_RANGE);
+  const int page = c.j / tiles_per_block;
+  if (page != c.page) {
+    c.page = page;
+    c.blk = __ldg(p.block_tables + static_cast<int64_t>(c.b) * p.bt_stride + page);
+    if (c.blk < 0 || c.blk >= p.num_blocks) record_error(p.err, SLOKV_DEVERR_BLOCK_RANGE);
+  }
+  const int off = (c.j - page * tiles_per_block) * kTile;
   // Out-of-range block ids load as zeros (TMA bounds fill); never a fault.
   const uint32_t bar = bars + stage * 8;
   fence_proxy_async_smem();
   if constexpr (kFp8) {
     const uint32_t dst = ring + stage * (2 * kTile * 128);
     mbar_arrive_expect_tx(bar, 2 * kTile * 128);
-    tma_load_4d(dst, kmap, bar, 0, r.h, off, blk, policy);
-    tma_load_4d(dst + kTile * 128, vmap, bar, 0, r.h, off, blk, policy);
+    tma_load_4d(dst, kmap, bar, 0, c.h, off, c.blk, policy);
+    tma_load_4d(dst + kTile * 128, vmap, bar, 0, c.h, off, c.blk, policy);
   } else {
     const uint32_t dst = ring + stage * kStageBytes;
     mbar_arrive_expect_tx(bar, kStageBytes);
-    tma_load_4d(dst + 0 * kHalfBytes, kmap, bar, 0, r.h, off, blk, policy);
-    tma_load_4d(dst + 1 * kHalfBytes, kmap, bar, 64, r.h, off, blk, policy);
-    tma_load_4d(dst + 2 * kHalfBytes, vmap, bar, 0, r.h, off, blk, policy);
-    tma_load_4d(dst + 3 * kHalfBytes, vmap, bar, 64, r.h, off, blk, policy);
+    tma_load_4d(dst + 0 * kHalfBytes, kmap, bar, 0, c.h, off, c.blk, policy);
+    tma_load_4d(dst + 1 * kHalfBytes, kmap, bar, 64, c.h, off, c.blk, policy);
+    tma_load_4d(dst + 2 * kHalfBytes, vmap, bar, 0, c.h, off, c.blk, policy);
+    tma_load_4d(dst + 3 * kHalfBytes, vmap, bar, 64, c.h, off, c.blk, policy);
   }
 }
 
@@ -312,9 +347,14 @@ __global__ void __launch_bounds__(Ring<kFp8>::kWarpsPerCta * 32, 1)
   const uint64_t policy = l2_evict_first_policy();
   const int tiles_per_block = p.block_size / kTile;
 
+  IssueCursor cur;                        // lane 0: next tile to issue (a + issued)
+  int64_t issued = 0;
   if (lane == 0) {
-    for (int i = 0; i < kStages && a + i < e; ++i)
-      issue_tile<kFp8>(p, prefix, &kmap, &vmap, ring, bars, i, a + i, policy);
+    cursor_init(cur, p, prefix, a);
+    for (; issued < kStages && a + issued < e; ++issued) {
+      issue_cursor_tile<kFp8>(p, cur, &kmap, &vmap, ring, bars, static_cast<int>(issued), policy);
+      if (a + issued + 1 < e) cursor_next(cur, p, prefix);
+    }
   }
   __syncwarp();
 
@@ -370,25 +410,30 @@ __global__ void __launch_bounds__(Ring<kFp8>::kWarpsPerCta * 32, 1)
     for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
     float vs_cur = 1.f;  // FP8: o is kept in units of this page's V scale
+    float ks_tile = 1.f, vs_tile = 1.f;
+    int scale_page = -1;
 
     for (int64_t tt = t; tt < piece_end; ++tt) {
       const int64_t idx = tt - a;
       const int stage = static_cast<int>(idx % kStages);
       const uint32_t parity = static_cast<uint32_t>((idx / kStages) & 1);
       const int j = static_cast<int>(tt - r.seg_start);
-      float ks_tile = 1.f, vs_tile = 1.f;
       if constexpr (kFp8) {
         const int page = j / tiles_per_block;
-        const int32_t blk = __ldg(p.block_tables + static_cast<int64_t>(r.b) * p.bt_stride + page);
-        if (blk >= 0 && blk < p.num_blocks) {
-          const int64_t si = static_cast<int64_t>(blk) * p.hkv + r.h;
-          ks_tile = __ldg(p.k_scale + si);
-          vs_tile = __ldg(p.v_scale + si);
-        } else {
-          ks_tile = 0.f;
-          vs_tile = 0.f;
+        if (page != scale_page) {          // scales change per page (8 tiles)
+          scale_page = page;
+          const int32_t blk =
+              __ldg(p.block_tables + static_cast<int64_t>(r.b) * p.bt_stride + page);
+          if (blk >= 0 && blk < p.num_blocks) {
+            const int64_t si = static_cast<int64_t>(blk) * p.hkv + r.h;
+            ks_tile = __ldg(p.k_scale + si);
+            vs_tile = __ldg(p.v_scale + si);
+          } else {
+            ks_tile = 0.f;
+            vs_tile = 0.f;
+          }
+          if (!(vs_tile > 0.f)) vs_tile = 1.f;  // an all-zero page: any unit works
         }
-        if (!(vs_tile > 0.f)) vs_tile = 1.f;  // an all-zero page: any unit works
       }
       if (!mbar_wait(bars + stage * 8, parity)) {
         if (lane == 0) record_error(p.err, SLOKV_DEVERR_TIMEOUT);
@@ -439,15 +484,18 @@ __global__ void __launch_bounds__(Ring<kFp8>::kWarpsPerCta * 32, 1)
         // Lane (g, c) reads 16-byte chunks c (dims 16c..) and c + 4 (dims
         // 64 + 16c..) of token row 8*nt + g: word t of a chunk feeds k-step
         // 4*gi + t (see the Q fragment order above).
+        uint4 w0[4], w1[4];
 #pragma unroll
         for (int nt = 0; nt < 4; ++nt) {
-          const int row = nt * 8 + g;
-          const uint4 w0 = lds128(kb + swz128(row, c));
-          const uint4 w1 = lds128(kb + swz128(row, c + 4));
+          w0[nt] = lds128(kb + swz128(nt * 8 + g, c));
+          w1[nt] = lds128(kb + swz128(nt * 8 + g, c + 4));
+        }
 #pragma unroll
-          for (int ks = 0; ks < 8; ++ks) {
+        for (int ks = 0; ks < 8; ++ks) {
+#pragma unroll
+          for (int nt = 0; nt < 4; ++nt) {
             uint32_t b0, b1;
-            e4m3x4_to_f16x2x2(word(ks < 4 ? w0 : w1, ks & 3), b0, b1);
+            e4m3x4_to_f16x2x2(word(ks < 4 ? w0[nt] : w1[nt], ks & 3), b0, b1);
             MQ::run(sc[nt], qa[ks], b0, b1);
           }
         }
@@ -577,8 +625,10 @@ __global__ void __launch_bounds__(Ring<kFp8>::kWarpsPerCta * 32, 1)
         }
       }
       __syncwarp();
-      if (lane == 0 && tt + kStages < e)
-        issue_tile<kFp8>(p, prefix, &kmap, &vmap, ring, bars, stage, tt + kStages, policy);
+      if (lane == 0 && tt + kStages < e) {
+        issue_cursor_tile<kFp8>(p, cur, &kmap, &vmap, ring, bars, stage, policy);
+        if (tt + kStages + 1 < e) cursor_next(cur, p, prefix);
+      }
     }
 
     // ---- finish the piece ----
