@@ -319,10 +319,11 @@ def run_ours(args):
         tok_s = B / (ms * 1e-3)
         traffic = None
         try:
-            with open(os.path.join(ROOT, "profiles", "paged_decode_traffic.json")) as f:
+            name = "paged_decode_fp8_traffic.json" if wl["fp8"] else "paged_decode_traffic.json"
+            with open(os.path.join(ROOT, "profiles", name)) as f:
                 tr = json.load(f)
-            # the capture was taken on the one-GPU bf16 configuration only
-            if not wl["fp8"] and n == 1 and args.batch == BATCH_PER_GPU:
+            # the captures were taken on the one-GPU configurations 2 and 4 only
+            if n == 1 and args.batch == (128 if wl["fp8"] else BATCH_PER_GPU):
                 traffic = tr.get("dram_bytes_per_launch")
         except Exception:
             pass
