@@ -725,7 +725,8 @@ def run_model(args):
     for n in lens:
         prompts.append(ids[cur:cur + n])
         cur += n
-    model = h.Qwen3Model(cfg, rank, world, None, seed=0, device=device)
+    model = h.Qwen3Model(cfg, rank, world, None, seed=0, device=device,
+                         fused_qk_norm_rope=not args.unfused_qk)
     runner = h.GreedyRunner(model, lens, args.warmup + args.steps + 2, seed=1, kv_dtype=args.kv)
     t0 = time.time()
     tok = runner.prefill(prompts, chunk_tokens=32768)
@@ -771,7 +772,8 @@ def run_model(args):
             "N(0, 0.02), random prompt ids (seed 5)",
             "config": {"workload": "BASELINE config 5: random-init Qwen3-4B greedy decode step "
                                    f"(36 layers), batch {B}, context U[{args.ctx_lo}, "
-                                   f"{args.ctx_hi}] after prefill, KV {args.kv}",
+                                   f"{args.ctx_hi}] after prefill, KV {args.kv}, q/k norm + "
+                                   f"RoPE {'torch ops' if args.unfused_qk else 'fused with the append'}",
                        "parallelism": f"tp{world}", "global_batch": B,
                        "prefill_seconds": round(prefill_s, 2)},
             "roofline": {"kernel": "whole decode step per rank (KV read + weights)",
@@ -846,6 +848,8 @@ def main():
     ap.add_argument("--pool-blocks", type=int, default=0,
                     help="pool size in blocks (default: ~70%% of HBM); profiling only")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--unfused-qk", action="store_true",
+                    help="model workload: q/k norm + RoPE as torch ops and the plain append")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--cpu-batch", type=int, default=BATCH_PER_GPU)

@@ -156,6 +156,28 @@ int slokv_paged_prefill(void *out, int64_t out_stride_t, int64_t out_stride_h,
 size_t slokv_paged_prefill_workspace_bytes(int32_t num_rows, int32_t max_seqlen_q);
 
 /*
+ * Fused q/k RMSNorm + rotary embedding + append (the layer chain between the
+ * qkv projection and attention: nanovllm/models/qwen3.py:76-86 with
+ * nanovllm/layers/layernorm.py, nanovllm/layers/rotary_embedding.py and
+ * store_kvcache, nanovllm/layers/attention.py:10-40).  qkv: [T, (Hq + 2 Hkv) x
+ * 128] rows (element stride qkv_row_stride); q_weight / k_weight: [128];
+ * positions: [T] int64; cos_sin: fp32 [max_position, 128] = cos[64] | sin[64]
+ * per position (the reference's cos_sin_cache); q_out: [T, Hq, 128] (token
+ * stride q_out_row_stride); k_out: [T, Hkv, 128] or NULL.  Cache row
+ * slot_mapping[t] (slot -1 skips) receives the normed, rotated k and the raw v.
+ * RMS statistics in fp32, the normed row rounded, times the weight (rounded),
+ * rotation in fp32 of the rounded values, rounded.  head_dim 128, bf16/f16.  A
+ * position outside [0, max_position) sets SLOKV_DEVERR_CONTEXT_LEN. */
+int slokv_qk_norm_rope_append(const void *qkv, int64_t qkv_row_stride, int32_t num_tokens,
+                              int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                              const void *q_weight, const void *k_weight, float eps,
+                              const int64_t *positions, const float *cos_sin,
+                              int32_t max_position, const int32_t *slot_mapping, void *k_cache,
+                              void *v_cache, int64_t num_slots, void *q_out,
+                              int64_t q_out_row_stride, void *k_out, int64_t k_out_row_stride,
+                              int32_t dtype, uint32_t *dev_error, void *stream);
+
+/*
  * FP8-E4M3 KV cache.
  *
  * Pool: codes uint8 [num_blocks, block_size, num_kv_heads, head_dim] (one tensor

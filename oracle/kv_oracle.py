@@ -115,6 +115,47 @@ def forward_mixed(q, k, v, k_cache, v_cache, meta, slot_mapping, scale):
 
 
 # ---------------------------------------------------------------------------
+# q/k RMSNorm + rotary embedding of one layer -- nanovllm/layers/layernorm.py
+# rms_forward (fp32 statistics, rounded, times the weight) and
+# nanovllm/layers/rotary_embedding.py (cos/sin table, rotate-half in fp32),
+# as nanovllm/models/qwen3.py:76-85 chains them.  Eager torch on the CPU.
+# ---------------------------------------------------------------------------
+
+
+def rms_norm(x, weight, eps):
+    xf = x.float()
+    var = xf.pow(2).mean(dim=-1, keepdim=True)
+    xf = xf * torch.rsqrt(var + eps)
+    return xf.to(x.dtype) * weight
+
+
+def rope_cos_sin(max_position, head_dim, base):
+    """[max_position, head_dim] fp32: cos of the head_dim/2 frequencies, then sin
+    (rotary_embedding.py RotaryEmbedding.__init__ with the unit axis squeezed)."""
+    inv_freq = 1.0 / (base ** (torch.arange(0, head_dim, 2, dtype=torch.float) / head_dim))
+    t = torch.arange(max_position, dtype=torch.float)
+    freqs = torch.einsum("i,j -> ij", t, inv_freq)
+    return torch.cat((freqs.cos(), freqs.sin()), dim=-1)
+
+
+def apply_rope(x, cos, sin):
+    x1, x2 = torch.chunk(x.float(), 2, dim=-1)
+    return torch.cat((x1 * cos - x2 * sin, x2 * cos + x1 * sin), dim=-1).to(x.dtype)
+
+
+def qk_norm_rope(qkv, num_q_heads, num_kv_heads, q_weight, k_weight, eps, positions, cos_sin):
+    """(q, k, v) of one layer from the fused qkv rows [T, (Hq + 2 Hkv) * D]."""
+    T = qkv.shape[0]
+    D = cos_sin.shape[-1]
+    q, k, v = qkv.split([num_q_heads * D, num_kv_heads * D, num_kv_heads * D], dim=-1)
+    q = rms_norm(q.reshape(T, num_q_heads, D), q_weight, eps)
+    k = rms_norm(k.reshape(T, num_kv_heads, D), k_weight, eps)
+    cos, sin = cos_sin[positions.long()].chunk(2, dim=-1)
+    cos, sin = cos.unsqueeze(1), sin.unsqueeze(1)
+    return apply_rope(q, cos, sin), apply_rope(k, cos, sin), v.reshape(T, num_kv_heads, D)
+
+
+# ---------------------------------------------------------------------------
 # Page copy -- diagnostics/online_token_replay/tensors.py:34-43 (restore_kv):
 # pool[:, :, page].copy_(saved[:, :, j]) for every page, all planes.
 # ---------------------------------------------------------------------------

@@ -14,16 +14,18 @@ from . import _lib
 from ._lib import SlokvError, read_device_errors
 from .kvcache import (decode_workspace, e4m3_decode, e4m3_encode, flash_attn_varlen_func,
                       flash_attn_with_kvcache, flash_attn_with_kvcache_fp8, kv_block_copy,
-                      kv_block_gather, kv_block_scatter, store_kvcache, store_kvcache_fp8)
+                      kv_block_gather, kv_block_scatter, qk_norm_rope_append, store_kvcache,
+                      store_kvcache_fp8)
 from .layers.attention import Attention
 from .pool import KVPool, block_bytes, plan_num_blocks, tp_shard
 from .layers.mixed_attention import MixedAttentionContext, forward_mixed
 from .utils.context import Context, get_context, reset_context, set_context
 
 __all__ = [
-    "Attention", "Context", "KVPool", "block_bytes", "plan_num_blocks", "tp_shard", "MixedAttentionContext", "SlokvError", "decode_workspace",
+    "Attention", "Context", "KVPool", "block_bytes", "plan_num_blocks", "tp_shard",
+    "MixedAttentionContext", "SlokvError", "decode_workspace",
     "e4m3_decode", "e4m3_encode", "flash_attn_varlen_func", "flash_attn_with_kvcache",
     "flash_attn_with_kvcache_fp8", "forward_mixed", "get_context", "store_kvcache_fp8",
-    "kv_block_copy", "kv_block_gather", "kv_block_scatter", "read_device_errors",
-    "reset_context", "set_context", "store_kvcache",
+    "kv_block_copy", "kv_block_gather", "kv_block_scatter", "qk_norm_rope_append",
+    "read_device_errors", "reset_context", "set_context", "store_kvcache",
 ]

@@ -66,6 +66,13 @@ SIGNATURES = {
         _c_i32, _c_i32, _c_i32, _c_f32, _c_i32,   # Hq, Hkv, D, scale, dtype
         _c_vp, _c_sz, _c_vp, _c_vp]),             # workspace, bytes, dev_error, stream
     "slokv_paged_prefill_workspace_bytes": (_c_sz, [_c_i32, _c_i32]),
+    "slokv_qk_norm_rope_append": (ctypes.c_int, [
+        _c_vp, _c_i64, _c_i32, _c_i32, _c_i32, _c_i32,  # qkv, row stride, T, Hq, Hkv, D
+        _c_vp, _c_vp, _c_f32,                         # q_weight, k_weight, eps
+        _c_vp, _c_vp, _c_i32,                         # positions, cos_sin, max_position
+        _c_vp, _c_vp, _c_vp, _c_i64,                  # slot_mapping, k_cache, v_cache, slots
+        _c_vp, _c_i64, _c_vp, _c_i64,                 # q_out, stride, k_out, stride
+        _c_i32, _c_vp, _c_vp]),                       # dtype, dev_error, stream
     "slokv_kv_append_fp8": (ctypes.c_int, [
         _c_vp, _c_i64, _c_vp, _c_i64, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_i32, _c_i32,
         _c_i32, _c_i32, _c_i32, _c_i32, _c_vp, _c_vp]),

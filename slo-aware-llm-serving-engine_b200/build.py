@@ -26,6 +26,7 @@ SOURCES = [
     "kv_block_copy.cu",
     "kv_append_fp8.cu",
     "paged_prefill.cu",
+    "qk_norm_rope.cu",
 ]
 HEADERS = ["common.cuh", "fp8_e4m3.cuh", "tcgen05.cuh"]
 

@@ -65,6 +65,54 @@ def store_kvcache(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Tensor,
         key.element_size(), num_slots, err.data_ptr(), stream_ptr(dev)), "kv_append")
 
 
+def qk_norm_rope_append(qkv: torch.Tensor, num_q_heads: int, num_kv_heads: int,
+                        q_weight: torch.Tensor, k_weight: torch.Tensor, eps: float,
+                        positions: torch.Tensor, cos_sin: torch.Tensor, slot_mapping: torch.Tensor,
+                        k_cache: torch.Tensor, v_cache: torch.Tensor, k_out: bool = False):
+    """Fused q_norm / k_norm + rotary embedding + store_kvcache of one layer.
+
+    qkv: [T, (Hq + 2 Hkv) * 128] (the qkv projection output, last dim
+    contiguous); q_weight / k_weight: [128]; positions: [T] int64; cos_sin: fp32
+    [max_position, 128] (cos | sin halves, the reference's cos_sin_cache
+    squeezed); k_cache / v_cache: [num_blocks, block_size, Hkv, 128].  Writes the
+    normed, rotated k and the raw v to cache row slot_mapping[t] (slot -1 skips)
+    and returns q [T, Hq, 128] (and k [T, Hkv, 128] when k_out is set, for cold
+    prefill attention on the step's own rows).
+    """
+    T = qkv.shape[0]
+    D = 128
+    dev = require_cuda(qkv, q_weight, k_weight, positions, cos_sin, slot_mapping, k_cache, v_cache)
+    if qkv.dim() != 2 or qkv.shape[1] != (num_q_heads + 2 * num_kv_heads) * D or qkv.stride(1) != 1:
+        raise SlokvError("qkv must be [tokens, (Hq + 2 Hkv) * 128] with a contiguous last dim")
+    if (q_weight.numel() != D or k_weight.numel() != D or not q_weight.is_contiguous()
+            or not k_weight.is_contiguous()):
+        raise SlokvError("q_weight / k_weight must be contiguous [128]")
+    if q_weight.dtype != qkv.dtype or k_weight.dtype != qkv.dtype or k_cache.dtype != qkv.dtype:
+        raise SlokvError("qkv, norm weights and cache dtypes differ")
+    if positions.dtype != torch.int64 or not positions.is_contiguous() or positions.numel() != T:
+        raise SlokvError("positions must be contiguous int64 [tokens]")
+    if cos_sin.dtype != torch.float32 or cos_sin.shape[-1] != D or not cos_sin.is_contiguous():
+        raise SlokvError("cos_sin must be contiguous fp32 [max_position, 128]")
+    _i32_contig("slot_mapping", slot_mapping)
+    for name, c in (("k_cache", k_cache), ("v_cache", v_cache)):
+        if (c.shape[-1] != D or c.shape[-2] != num_kv_heads
+                or c.stride(0) != c.shape[1] * num_kv_heads * D):
+            raise SlokvError(f"{name} must be [num_blocks, block_size, {num_kv_heads}, 128] "
+                             "with contiguous blocks")
+    q = torch.empty(T, num_q_heads, D, dtype=qkv.dtype, device=qkv.device)
+    k = torch.empty(T, num_kv_heads, D, dtype=qkv.dtype, device=qkv.device) if k_out else None
+    if T:
+        err = buffers.error_word(dev)
+        check(lib().slokv_qk_norm_rope_append(
+            qkv.data_ptr(), qkv.stride(0), T, num_q_heads, num_kv_heads, D, q_weight.data_ptr(),
+            k_weight.data_ptr(), float(eps), positions.data_ptr(), cos_sin.data_ptr(),
+            cos_sin.numel() // D, slot_mapping.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+            k_cache.shape[0] * k_cache.shape[1], q.data_ptr(), q.stride(0),
+            k.data_ptr() if k is not None else None, k.stride(0) if k is not None else 0,
+            _lib.dtype_code(qkv.dtype), err.data_ptr(), stream_ptr(dev)), "qk_norm_rope_append")
+    return (q, k) if k_out else q
+
+
 def decode_workspace(device: torch.device, num_q_heads: int, num_kv_heads: int,
                      head_dim: int) -> torch.Tensor:
     """The fixed per-device split-K workspace used by paged decode."""

@@ -39,9 +39,20 @@ class Attention(nn.Module):
             return forward_mixed(q, k, v, k_cache, v_cache, context, self.scale, store_kvcache)
         if k_cache.numel() and v_cache.numel():
             store_kvcache(k, v, k_cache, v_cache, context.slot_mapping)
+        return self._attend(q, k, v, context)
+
+    def attend(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor):
+        """forward() without the store, for callers whose K/V rows already went
+        into the pool (qk_norm_rope_append); bf16/f16 pools, prefill or decode."""
+        context = get_context()
+        if self.k_scale is not None or context.mixed is not None:
+            raise RuntimeError("attend() covers the bf16/f16 prefill and decode paths")
+        return self._attend(q, k, v, context)
+
+    def _attend(self, q, k, v, context):
         if context.is_prefill:
             if context.block_tables is not None:    # prefix cache: keys come from the pool
-                k, v = k_cache, v_cache
+                k, v = self.k_cache, self.v_cache
             return flash_attn_varlen_func(q, k, v,
                                           max_seqlen_q=context.max_seqlen_q,
                                           cu_seqlens_q=context.cu_seqlens_q,
@@ -49,7 +60,7 @@ class Attention(nn.Module):
                                           cu_seqlens_k=context.cu_seqlens_k,
                                           softmax_scale=self.scale, causal=True,
                                           block_table=context.block_tables)
-        return flash_attn_with_kvcache(q.unsqueeze(1), k_cache, v_cache,
+        return flash_attn_with_kvcache(q.unsqueeze(1), self.k_cache, self.v_cache,
                                        cache_seqlens=context.context_lens,
                                        block_table=context.block_tables,
                                        softmax_scale=self.scale, causal=True)

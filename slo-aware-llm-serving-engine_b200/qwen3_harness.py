@@ -24,9 +24,10 @@ from dataclasses import dataclass
 import torch
 import torch.nn.functional as F
 
+from .kvcache import qk_norm_rope_append
 from .layers.attention import Attention
 from .pool import KVPool, tp_shard
-from .utils.context import reset_context, set_context
+from .utils.context import get_context, reset_context, set_context
 
 
 @dataclass(frozen=True)
@@ -69,8 +70,12 @@ class Qwen3Model:
     """One tensor-parallel rank of a random-init Qwen3 decoder."""
 
     def __init__(self, cfg: Qwen3Config, tp_rank: int = 0, tp_size: int = 1, group=None,
-                 seed: int = 0, device="cuda", dtype=torch.bfloat16):
+                 seed: int = 0, device="cuda", dtype=torch.bfloat16,
+                 fused_qk_norm_rope: bool = True):
         self.cfg, self.tp_rank, self.tp_size, self.group = cfg, tp_rank, tp_size, group
+        # q/k RMSNorm + RoPE + append in one kernel (qk_norm_rope_append) for
+        # layers whose attention is this package's module on a bf16/f16 pool
+        self.fused_qk_norm_rope = fused_qk_norm_rope
         self.device, self.dtype = torch.device(device), dtype
         qh, kh = tp_shard(cfg.num_heads, cfg.num_kv_heads, tp_size, tp_rank)
         if cfg.intermediate_size % tp_size:
@@ -104,6 +109,7 @@ class Qwen3Model:
         freqs = torch.outer(torch.arange(cfg.max_position, dtype=torch.float32), inv_freq)
         self.cos = freqs.cos().to(self.device)
         self.sin = freqs.sin().to(self.device)
+        self.cos_sin = torch.cat((self.cos, self.sin), dim=-1).contiguous()
 
     def _normal(self, shape, seed: int, idx: int) -> torch.Tensor:
         g = torch.Generator(device=self.device)
@@ -138,12 +144,24 @@ class Qwen3Model:
                 x, res = rms_norm(h, lw.ln1, eps), h
             else:
                 x, res = add_rms_norm(h, res, lw.ln1, eps)
-            q, k, v = F.linear(x, lw.wqkv).split([qs, kvs, kvs], dim=-1)
-            q = rms_norm(q.view(-1, self.hq, D), lw.qn, eps)
-            k = rms_norm(k.view(-1, self.hkv, D), lw.kn, eps)
-            v = v.view(-1, self.hkv, D)                    # strided view, as the reference
-            q, k = self._rope(positions, q), self._rope(positions, k)
-            o = lw.attn(q, k, v)
+            qkv = F.linear(x, lw.wqkv)
+            if (self.fused_qk_norm_rope and type(lw.attn) is Attention
+                    and lw.attn.k_scale is None and lw.attn.k_cache.numel()):
+                ctx = get_context()
+                cold = ctx.is_prefill and ctx.block_tables is None   # attends on its own rows
+                out = qk_norm_rope_append(qkv, self.hq, self.hkv, lw.qn, lw.kn, eps, positions,
+                                          self.cos_sin, ctx.slot_mapping, lw.attn.k_cache,
+                                          lw.attn.v_cache, k_out=cold)
+                q, k = out if cold else (out, None)
+                v = qkv[:, qs + kvs:].view(-1, self.hkv, D)
+                o = lw.attn.attend(q, k, v)
+            else:
+                q, k, v = qkv.split([qs, kvs, kvs], dim=-1)
+                q = rms_norm(q.view(-1, self.hq, D), lw.qn, eps)
+                k = rms_norm(k.view(-1, self.hkv, D), lw.kn, eps)
+                v = v.view(-1, self.hkv, D)                # strided view, as the reference
+                q, k = self._rope(positions, q), self._rope(positions, k)
+                o = lw.attn(q, k, v)
             h = self._all_reduce(F.linear(o.flatten(1, -1), lw.wo))
             x, res = add_rms_norm(h, res, lw.ln2, eps)
             gate, up = F.linear(x, lw.wgu).chunk(2, dim=-1)

@@ -12,7 +12,10 @@ What runs (all reference code, unmodified, imported from its checkout):
     reference's FP32 diagnostic installs it);
   * forward_mixed (nanovllm/layers/mixed_attention.py:29-57);
   * encode_e4m3fn (benchmarks/v0/probe_quant_support.py:39-56);
-  * restore_kv (diagnostics/online_token_replay/tensors.py:34-43).
+  * restore_kv (diagnostics/online_token_replay/tensors.py:34-43);
+  * RMSNorm (nanovllm/layers/layernorm.py) and RotaryEmbedding
+    (nanovllm/layers/rotary_embedding.py) as qwen3.py:82-85 apply them to q/k,
+    eager (TORCHDYNAMO_DISABLE=1 turns their torch.compile into a no-op).
 Inputs come from tests/golden/scenarios.py (deterministic), so only outputs and
 digests are stored, in tests/golden/golden.npz + golden.json.
 """
@@ -116,6 +119,25 @@ def main():
     restore_kv(pool, image)
     arrays["restore/pool"] = pool.numpy()
     manifest["scenarios"]["restore"] = {"block_ids": [4, 1, 5]}
+
+    # --- q/k RMSNorm + rotary embedding of one layer (qwen3.py:82-85)
+    from nanovllm.layers.layernorm import RMSNorm
+    from nanovllm.layers.rotary_embedding import RotaryEmbedding
+    nc = S.qk_norm_rope_case()
+    T, Hq, Hkv, D = nc["qkv"].shape[0], nc["Hq"], nc["Hkv"], nc["D"]
+    q, k, _ = nc["qkv"].split([Hq * D, Hkv * D, Hkv * D], dim=-1)
+    q_norm, k_norm = RMSNorm(D, eps=nc["eps"]), RMSNorm(D, eps=nc["eps"])
+    q_norm.weight.data = nc["wq"].clone()
+    k_norm.weight.data = nc["wk"].clone()
+    rope = RotaryEmbedding(D, D, nc["max_position"], nc["base"])
+    with torch.no_grad():
+        qn = q_norm(q.reshape(T, Hq, D))
+        kn = k_norm(k.reshape(T, Hkv, D))
+        qr, kr = rope(nc["pos"], qn, kn)
+    arrays["qk_norm_rope/q"] = qr.float().numpy()
+    arrays["qk_norm_rope/k"] = kr.float().numpy()
+    manifest["scenarios"]["qk_norm_rope"] = {"q_sha256": sha(qr), "k_sha256": sha(kr)}
+    print("qk_norm_rope", tuple(qr.shape), tuple(kr.shape))
 
     np.savez_compressed(os.path.join(HERE, "golden.npz"), **arrays)
     with open(os.path.join(HERE, "golden.json"), "w") as f:

@@ -151,6 +151,18 @@ def cold_prefill():
     return _mixed_from_rows("cold_prefill", 700, 8, 2, 2, rows, (0.0, 0.0))
 
 
+def qk_norm_rope_case():
+    """q/k RMSNorm + rotary inputs in Qwen3 head geometry (8 q heads, 2 kv heads
+    of 128, non-unit norm weights, positions spread over a 4096-entry table)."""
+    T, Hq, Hkv, D = 37, 8, 2, 128
+    qkv = torch.from_numpy(det_normal(960, (T, (Hq + 2 * Hkv) * D)) * 3.0).bfloat16()
+    wq = torch.from_numpy(det_normal(961, (D,)) * 0.3 + 1.0).bfloat16()
+    wk = torch.from_numpy(det_normal(962, (D,)) * 0.3 + 1.0).bfloat16()
+    pos = torch.from_numpy(det_ints(963, T, 0, 4095).astype(np.int64))
+    return dict(name="qk_norm_rope", qkv=qkv, Hq=Hq, Hkv=Hkv, D=D, wq=wq, wk=wk, pos=pos,
+                eps=1e-6, base=1e6, max_position=4096)
+
+
 def e4m3_probe_values():
     """fp32 values for the E4M3 encoder: every finite bf16 pattern, every
     midpoint between adjacent codes and its fp32 neighbours, and a detgen sweep

@@ -66,6 +66,18 @@ def test_restore_matches_reference(golden):
     np.testing.assert_array_equal(pool.numpy(), arrays["restore/pool"])
 
 
+def test_qk_norm_rope_matches_reference(golden):
+    """The oracle's RMSNorm + rotary embedding reproduces the reference's own
+    RMSNorm / RotaryEmbedding modules bit for bit (both eager torch on the CPU)."""
+    manifest, _ = golden
+    nc = S.qk_norm_rope_case()
+    cos_sin = O.rope_cos_sin(nc["max_position"], nc["D"], nc["base"])
+    q, k, _ = O.qk_norm_rope(nc["qkv"], nc["Hq"], nc["Hkv"], nc["wq"], nc["wk"], nc["eps"],
+                             nc["pos"], cos_sin)
+    ref = manifest["scenarios"]["qk_norm_rope"]
+    assert _sha(q) == ref["q_sha256"] and _sha(k) == ref["k_sha256"]
+
+
 # ---- the reference tests' own known answers ---------------------------------
 
 def test_e4m3_known_answers():
