@@ -134,6 +134,10 @@ int slokv_paged_decode(void *out, int64_t out_stride_b, int64_t out_stride_h,
  * k/v ([kv_rows, Hkv, 128] with row strides kv_stride_t / v_stride_t).
  * q/out: [q_rows, Hq, 128] with the given token / head strides.  bf16 or f16.
  * tcgen05.mma with TMEM accumulators; block_size must be a multiple of 128.
+ * k_page_scale (NULL: none): fp32 [num_blocks, Hkv]; when given, the paged K
+ * holds unscaled FP8 code values and the logits of keys in page b are
+ * S * k_page_scale[b * Hkv + kv head] (FP8 pools; even GQA groups only, else
+ * SLOKV_ERR_UNSUPPORTED).
  */
 int slokv_paged_prefill(void *out, int64_t out_stride_t, int64_t out_stride_h,
                         const void *q, int64_t q_stride_t, int64_t q_stride_h, int64_t q_rows,
@@ -144,8 +148,9 @@ int slokv_paged_prefill(void *out, int64_t out_stride_t, int64_t out_stride_h,
                         const int32_t *block_tables, int64_t block_table_stride,
                         int32_t max_blocks_per_seq, int32_t num_blocks, int32_t block_size,
                         int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
-                        float softmax_scale, int32_t dtype, void *workspace,
-                        size_t workspace_bytes, uint32_t *dev_error, void *stream);
+                        float softmax_scale, int32_t dtype, const float *k_page_scale,
+                        void *workspace, size_t workspace_bytes, uint32_t *dev_error,
+                        void *stream);
 
 /* Bytes of the optional prefill workspace: num_rows * ceil(max_seqlen_q / 128)
  * int32 (rounded up to 256), holding the longest-first order of the query
@@ -205,6 +210,28 @@ int slokv_kv_append_fp8(const void *key, int64_t key_row_stride,
                         int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
                         int32_t num_blocks, int32_t in_dtype,
                         uint32_t *dev_error, void *stream);
+
+/* Prefix-cache prefill over an FP8 pool (the prefill half of
+ * flash_attn_varlen_func / forward_mixed, nanovllm/layers/attention.py:69-74,
+ * nanovllm/layers/mixed_attention.py:123-133, when the pool is FP8): page p of
+ * row r (p < pages_per_row, p * block_size < cu_seqlens_k[r+1] - cu_seqlens_k[r])
+ * is written to page r * pages_per_row + p of f16 buffers dst_k / dst_v
+ * ([num_rows * pages_per_row, block_size, Hkv, 128]): K as its unscaled code
+ * values (exact in f16) with the page's K scale in dst_k_scale[page * Hkv + h],
+ * V as decode(code) * scale in fp32 rounded to f16.  slokv_paged_prefill (f16,
+ * k_page_scale = dst_k_scale) then attends through table row r = r *
+ * pages_per_row + 0 .. pages_per_row - 1, applying the K scale to the logits as
+ * the FP8 decode does.  Pages past a row's keys are not written; an id outside
+ * the pool writes zeros (scale 0) and sets SLOKV_DEVERR_BLOCK_RANGE.  Codes,
+ * strides and destinations 16-byte aligned. */
+int slokv_fp8_pages_dequant(const void *k_codes, const void *v_codes, int64_t k_block_stride,
+                            int64_t v_block_stride, const float *k_scale, const float *v_scale,
+                            int32_t num_blocks, int32_t block_size, int32_t num_kv_heads,
+                            int32_t head_dim, const int32_t *block_tables,
+                            int64_t block_table_stride, int32_t max_blocks_per_seq,
+                            const int32_t *cu_seqlens_k, int32_t num_rows, int32_t pages_per_row,
+                            void *dst_k, void *dst_v, float *dst_k_scale, uint32_t *dev_error,
+                            void *stream);
 
 /* Workspace of slokv_paged_decode_fp8 (8 warp slots per SM), in bytes. */
 size_t slokv_paged_decode_fp8_workspace_bytes(int32_t device, int32_t num_q_heads,

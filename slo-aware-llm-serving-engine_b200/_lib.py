@@ -64,8 +64,14 @@ SIGNATURES = {
         _c_vp, _c_vp, _c_i32, _c_i32,             # cu_q, cu_k, rows, max_seqlen_q
         _c_vp, _c_i64, _c_i32, _c_i32, _c_i32,    # tables, stride, width, num_blocks, bs
         _c_i32, _c_i32, _c_i32, _c_f32, _c_i32,   # Hq, Hkv, D, scale, dtype
+        _c_vp,                                    # k_page_scale (FP8 pools) or None
         _c_vp, _c_sz, _c_vp, _c_vp]),             # workspace, bytes, dev_error, stream
     "slokv_paged_prefill_workspace_bytes": (_c_sz, [_c_i32, _c_i32]),
+    "slokv_fp8_pages_dequant": (ctypes.c_int, [
+        _c_vp, _c_vp, _c_i64, _c_i64, _c_vp, _c_vp,   # codes, block strides, scales
+        _c_i32, _c_i32, _c_i32, _c_i32,               # num_blocks, block_size, Hkv, D
+        _c_vp, _c_i64, _c_i32, _c_vp, _c_i32, _c_i32,  # tables, stride, width, cu_k, rows, pages
+        _c_vp, _c_vp, _c_vp, _c_vp, _c_vp]),          # dst_k, dst_v, dst_k_scale, err, stream
     "slokv_qk_norm_rope_append": (ctypes.c_int, [
         _c_vp, _c_i64, _c_i32, _c_i32, _c_i32, _c_i32,  # qkv, row stride, T, Hq, Hkv, D
         _c_vp, _c_vp, _c_f32,                         # q_weight, k_weight, eps
@@ -191,6 +197,12 @@ class _PerDevice:
                             device=torch.device("cuda", idx))
             self._ws[(idx, key)] = t
         return t
+
+    def workspace_fits(self, device: torch.device, key: str, nbytes: int) -> bool:
+        """Whether workspace `key` of `device` already holds nbytes (no allocation)."""
+        idx = device.index if device.index is not None else torch.cuda.current_device()
+        t = self._ws.get((idx, key))
+        return t is not None and t.numel() >= nbytes
 
 
 buffers = _PerDevice()

@@ -27,6 +27,7 @@ SOURCES = [
     "kv_append_fp8.cu",
     "paged_prefill.cu",
     "qk_norm_rope.cu",
+    "fp8_pages_dequant.cu",
 ]
 HEADERS = ["common.cuh", "fp8_e4m3.cuh", "tcgen05.cuh"]
 

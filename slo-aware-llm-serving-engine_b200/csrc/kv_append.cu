@@ -116,4 +116,4 @@ extern "C" const char *slokv_status_string(int status) {
   }
 }
 
-extern "C" int slokv_abi_version(void) { return 2; }
+extern "C" int slokv_abi_version(void) { return 3; }

@@ -71,6 +71,10 @@ struct Params {
   // (row * m_tiles + m, longest first; -1 = no tile); null: row-major order.
   const int32_t *order;
   int32_t m_tiles;                        // ceil(max_seqlen_q / 128)
+  // Optional per-(page, kv head) factor of S (two-head kernel only): K holds
+  // unscaled FP8 codes and the logits of a key tile in page `pid` are
+  // S * k_page_scale[pid * hkv + kv head].  Null: 1.
+  const float *k_page_scale;
 };
 
 __device__ __forceinline__ float fast_exp2(float x) {
@@ -710,11 +714,12 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
     float m_run = row_ok ? -INFINITY : 0.f, l_run = 0.f;
     uint32_t s[4][32];                            // S row of the tile, keys 32*i + c
     bool ok = true;
-    // P = 2^(S * scale_log2 - mu) of the S row in registers, packed (keys 2w,
-    // 2w+1 in column w) over the first 64 columns of S; returns the row sum.
-    // The scale-and-shift and the sum run two keys per f32x2 instruction.
-    auto exp_store = [&](float mu) {
-      const uint64_t sl2 = f32x2(p.scale_log2, p.scale_log2), nmu2 = f32x2(-mu, -mu);
+    // P = 2^(S * sl - mu) of the S row in registers (sl: scale_log2 times the
+    // tile's K page scale), packed (keys 2w, 2w+1 in column w) over the first 64
+    // columns of S; returns the row sum.  The scale-and-shift and the sum run
+    // two keys per f32x2 instruction.
+    auto exp_store = [&](float mu, float sl) {
+      const uint64_t sl2 = f32x2(sl, sl), nmu2 = f32x2(-mu, -mu);
       uint64_t rs2[4] = {0ull, 0ull, 0ull, 0ull};  // {0.f, 0.f}
 #pragma unroll
       for (int hb = 0; hb < 2; ++hb) {
@@ -742,6 +747,18 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
       tc::fence_after_sync();
       const int key0 = j * kBN;
       const bool full = key0 + kBN - 1 <= kmax;   // no key of the tile is masked
+      float sl = p.scale_log2;
+      if (p.k_page_scale != nullptr) {
+        // a zero scale (page of zero codes) must keep masked -inf keys at -inf
+        const int page = key0 / p.block_size;
+        const int32_t pid = page < p.max_blocks
+                                ? __ldg(p.block_tables + static_cast<int64_t>(r) * p.bt_stride + page)
+                                : -1;
+        const float ks = pid >= 0 && pid < p.num_blocks
+                             ? __ldg(p.k_page_scale + static_cast<int64_t>(pid) * p.hkv + hk)
+                             : 0.f;
+        sl *= fmaxf(ks, 1e-30f);
+      }
 #pragma unroll
       for (int i = 0; i < 4; ++i) tc::ld32(s_addr + 32 * i, s[i]);
       tc::wait_ld();
@@ -759,7 +776,7 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
       float alpha = 1.f, rs = 0.f;
       bool redo = fresh;
       if (!fresh) {
-        rs = exp_store(m_run);
+        rs = exp_store(m_run, sl);
         redo = __any_sync(0xffffffffu, !(rs <= kSumLimit));
       }
       if (redo) {
@@ -768,13 +785,13 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
         for (int i = 0; i < 4; ++i)
 #pragma unroll
           for (int c = 0; c < 32; ++c) mx = fmaxf(mx, __uint_as_float(s[i][c]));
-        mx *= p.scale_log2;
+        mx *= sl;
         if (mx > m_run) {                          // first tile: m_run = -inf, alpha = 0
           alpha = fast_exp2(m_run - mx);
           m_run = mx;
         }
         if (!fresh) tc::wait_st();                 // first P stores land before rewrite
-        rs = exp_store(m_run == -INFINITY ? 0.f : m_run);
+        rs = exp_store(m_run == -INFINITY ? 0.f : m_run, sl);
       }
       l_run = l_run * alpha + rs;
       if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
@@ -875,6 +892,7 @@ int launch(const Params &p, const CUtensorMap &qm, const CUtensorMap &km, const 
             fa.numRegs == ws::kRegsLaunch;
   });
   if (!ok) return SLOKV_ERR_CUDA;
+  if (p.k_page_scale != nullptr && !(p.group % 2 == 0 && ws_ok)) return SLOKV_ERR_UNSUPPORTED;
   if (p.group % 2 == 0 && ws_ok) {  // two query heads of one KV head per CTA
     if (p.order != nullptr) {
       prefill_schedule_kernel<<<1, kSchedThreads, 0, stream>>>(
@@ -913,8 +931,8 @@ extern "C" int slokv_paged_prefill(void *out, int64_t out_stride_t, int64_t out_
                                    int32_t max_blocks_per_seq, int32_t num_blocks,
                                    int32_t block_size, int32_t num_q_heads, int32_t num_kv_heads,
                                    int32_t head_dim, float softmax_scale, int32_t dtype,
-                                   void *workspace, size_t workspace_bytes,
-                                   uint32_t *dev_error, void *stream) {
+                                   const float *k_page_scale, void *workspace,
+                                   size_t workspace_bytes, uint32_t *dev_error, void *stream) {
   using namespace slokv;
   using namespace slokv::prefill;
   if (num_rows < 0 || max_seqlen_q < 0 || num_q_heads <= 0 || num_kv_heads <= 0)
@@ -969,6 +987,9 @@ extern "C" int slokv_paged_prefill(void *out, int64_t out_stride_t, int64_t out_
   p.scale_log2 = softmax_scale * 1.4426950408889634f;
   p.err = dev_error;
   p.m_tiles = (max_seqlen_q + kBM - 1) / kBM;
+  p.k_page_scale = k_page_scale;
+  // page scales are applied by the two-head kernel only (even GQA groups, paged)
+  if (k_page_scale != nullptr && (p.group % 2 != 0 || !paged)) return SLOKV_ERR_UNSUPPORTED;
   // The work order needs rows x m_tiles int32 (slokv_paged_prefill_workspace_bytes);
   // without it the tiles run in row-major order.
   p.order = workspace != nullptr &&

@@ -358,6 +358,15 @@ def flash_attn_varlen_func(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, ma
     row r's keys are gathered through block_table[r].  Query i of row r sees
     keys 0 .. k_len - q_len + i (bottom-right aligned).  Returns [Tq, Hq, D].
     """
+    return _varlen_attention(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, softmax_scale,
+                             causal, block_table, out, None)
+
+
+def _varlen_attention(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, softmax_scale, causal,
+                      block_table, out, k_page_scale):
+    """flash_attn_varlen_func's body; k_page_scale (fp32 [num_blocks, Hkv], paged
+    only) multiplies the logits of each page's keys, for K pages that hold
+    unscaled FP8 code values."""
     if not causal:
         raise SlokvError("only causal varlen attention is implemented (the engine's only use)")
     if q.dim() != 3:
@@ -401,9 +410,74 @@ def flash_attn_varlen_func(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, ma
     ws, ws_bytes = _prefill_workspace(dev, rows, int(max_seqlen_q))
     check(lib().slokv_paged_prefill(
         out.data_ptr(), out.stride(0), out.stride(1), q.data_ptr(), q.stride(0), q.stride(1), Tq,
-        *args, Hq, Hkv, D, scale, _lib.dtype_code(q.dtype), ws, ws_bytes, err.data_ptr(),
+        *args, Hq, Hkv, D, scale, _lib.dtype_code(q.dtype),
+        None if k_page_scale is None else k_page_scale.data_ptr(), ws, ws_bytes, err.data_ptr(),
         stream_ptr(dev)),
         "paged_prefill")
+    return out
+
+
+def flash_attn_varlen_func_fp8(q, k_codes, v_codes, k_scale, v_scale, cu_seqlens_q,
+                               cu_seqlens_k, max_seqlen_q, max_seqlen_k, softmax_scale=None,
+                               causal=True, block_table=None, out=None):
+    """Prefix-cache varlen attention over an FP8 pool (block_table required).
+
+    The pages the rows read are copied into a per-device f16 page buffer of
+    rows x ceil(max_seqlen_k / block_size) pages -- K as its unscaled code
+    values (exact in f16) with its per-(block, head) scale kept aside, V as
+    code x scale in fp32 rounded to f16 -- which the paged prefill kernel then
+    attends in f16 through a fixed remapped table, multiplying each page's
+    logits by its K scale (the FP8 decode's arithmetic: S = scale_k * (q .
+    codes)).  q goes in as f16 and the output comes back in q's dtype.  The
+    buffers grow outside graph capture only: make the first call of the
+    largest geometry eagerly.  Needs an even number of query heads per KV head.
+    """
+    if block_table is None:
+        raise SlokvError("FP8 varlen attention reads the pool: block_table is required")
+    NB, bs, Hkv, D = k_codes.shape
+    if v_codes.shape != k_codes.shape or D != q.shape[-1]:
+        raise SlokvError("FP8 pool shape mismatch with q")
+    for name, c in (("k_codes", k_codes), ("v_codes", v_codes)):
+        if not is_fp8_cache(c) or c.stride(3) != 1 or c.stride(2) != D or c.stride(1) != Hkv * D:
+            raise SlokvError(f"{name} must be an FP8 pool with contiguous blocks")
+    for name, sc in (("k_scale", k_scale), ("v_scale", v_scale)):
+        if sc.dtype != torch.float32 or tuple(sc.shape) != (NB, Hkv) or not sc.is_contiguous():
+            raise SlokvError(f"{name} must be contiguous fp32 [num_blocks, num_kv_heads]")
+    if block_table.dtype != torch.int32 or block_table.stride(-1) != 1:
+        raise SlokvError("block_table must be int32 with a contiguous last dimension")
+    dev = require_cuda(q, k_codes, v_codes, k_scale, v_scale, cu_seqlens_q, cu_seqlens_k,
+                       block_table)
+    _i32_contig("cu_seqlens_k", cu_seqlens_k)
+    rows = cu_seqlens_k.numel() - 1
+    width = (int(max_seqlen_k) + bs - 1) // bs
+    if rows <= 0 or width <= 0:                 # no keys anywhere: zero output
+        o = out if out is not None else torch.empty_like(q)
+        return o.zero_()
+    if q.dim() != 3 or q.dtype not in (torch.bfloat16, torch.float16):
+        raise SlokvError("q must be bf16/f16 [tokens, heads, head_dim]")
+    page = bs * Hkv * D
+    pages = rows * width
+    nbytes = pages * page * 2
+    kbuf = buffers.workspace(dev, "fp8_prefill_k", nbytes)
+    vbuf = buffers.workspace(dev, "fp8_prefill_v", nbytes)
+    sbuf = buffers.workspace(dev, "fp8_prefill_kscale", pages * Hkv * 4)
+    kd = kbuf[:nbytes].view(torch.float16).view(pages, bs, Hkv, D)
+    vd = vbuf[:nbytes].view(torch.float16).view(pages, bs, Hkv, D)
+    ks = sbuf[:pages * Hkv * 4].view(torch.float32).view(pages, Hkv)
+    err = buffers.error_word(dev)
+    check(lib().slokv_fp8_pages_dequant(
+        k_codes.data_ptr(), v_codes.data_ptr(), k_codes.stride(0), v_codes.stride(0),
+        k_scale.data_ptr(), v_scale.data_ptr(), NB, bs, Hkv, D, block_table.data_ptr(),
+        block_table.stride(0), block_table.shape[1], cu_seqlens_k.data_ptr(), rows, width,
+        kd.data_ptr(), vd.data_ptr(), ks.data_ptr(), err.data_ptr(),
+        stream_ptr(dev)), "fp8_pages_dequant")
+    table = torch.arange(pages, dtype=torch.int32, device=q.device).view(rows, width)
+    q16 = q if q.dtype == torch.float16 else q.to(torch.float16)
+    o16 = _varlen_attention(q16, kd, vd, cu_seqlens_q, cu_seqlens_k, max_seqlen_q,
+                            softmax_scale, causal, table, None, ks)
+    if out is None:
+        return o16 if q.dtype == torch.float16 else o16.to(q.dtype)
+    out.copy_(o16)
     return out
 
 
@@ -419,9 +493,7 @@ def _prefill_workspace(dev: torch.device, rows: int, max_seqlen_q: int):
     need = lib().slokv_paged_prefill_workspace_bytes(rows, max_seqlen_q)
     if need == 0:
         return None, 0
-    idx = dev.index if dev.index is not None else torch.cuda.current_device()
-    t = buffers._ws.get((idx, "prefill"))
-    if (t is None or t.numel() < need) and torch.cuda.is_current_stream_capturing():
+    if torch.cuda.is_current_stream_capturing() and not buffers.workspace_fits(dev, "prefill", need):
         return None, 0
     t = buffers.workspace(dev, "prefill", max(need, _PREFILL_WS_MIN))
     return t.data_ptr(), t.numel()

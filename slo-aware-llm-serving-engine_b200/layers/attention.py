@@ -4,13 +4,15 @@ Same constructor, `.k_cache`/`.v_cache` attributes (bound by the model runner to
 kv_cache[0, layer] / kv_cache[1, layer]) and forward(q, k, v) dispatch as the
 reference (nanovllm/layers/attention.py:43-79): store the step's K/V, then run
 prefill varlen attention (paged when the context carries block tables), decode
-attention over the paged cache, or the mixed prefill/decode path.
+attention over the paged cache, or the mixed prefill/decode path -- over a
+bf16/f16 pool or an FP8-E4M3 one (codes plus k_scale / v_scale).
 """
 import torch
 from torch import nn
 
-from ..kvcache import (flash_attn_varlen_func, flash_attn_with_kvcache,
-                       flash_attn_with_kvcache_fp8, store_kvcache, store_kvcache_fp8)
+from ..kvcache import (flash_attn_varlen_func, flash_attn_varlen_func_fp8,
+                       flash_attn_with_kvcache, flash_attn_with_kvcache_fp8, store_kvcache,
+                       store_kvcache_fp8)
 from ..utils.context import get_context
 
 __all__ = ["Attention", "store_kvcache"]
@@ -66,18 +68,25 @@ class Attention(nn.Module):
                                        softmax_scale=self.scale, causal=True)
 
     def _forward_fp8(self, q, k, v, context):
-        cold_prefill = context.is_prefill and context.block_tables is None
-        if context.mixed is not None or (context.is_prefill and not cold_prefill):
-            raise RuntimeError("the FP8 KV pool supports decode and cold (no prefix) prefill only")
+        if context.mixed is not None:
+            from .mixed_attention import forward_mixed_fp8
+            return forward_mixed_fp8(q, k, v, self.k_cache, self.v_cache, self.k_scale,
+                                     self.v_scale, context, self.scale)
         store_kvcache_fp8(k, v, self.k_cache, self.v_cache, self.k_scale, self.v_scale,
                           context.slot_mapping)
-        if cold_prefill:     # keys are the step's own bf16 k/v; the pool only stores codes
-            return flash_attn_varlen_func(q, k, v,
-                                          max_seqlen_q=context.max_seqlen_q,
-                                          cu_seqlens_q=context.cu_seqlens_q,
-                                          max_seqlen_k=context.max_seqlen_k,
-                                          cu_seqlens_k=context.cu_seqlens_k,
-                                          softmax_scale=self.scale, causal=True)
+        if context.is_prefill:
+            if context.block_tables is None:   # cold prompt: keys are the step's own rows
+                return flash_attn_varlen_func(q, k, v,
+                                              max_seqlen_q=context.max_seqlen_q,
+                                              cu_seqlens_q=context.cu_seqlens_q,
+                                              max_seqlen_k=context.max_seqlen_k,
+                                              cu_seqlens_k=context.cu_seqlens_k,
+                                              softmax_scale=self.scale, causal=True)
+            return flash_attn_varlen_func_fp8(q, self.k_cache, self.v_cache, self.k_scale,
+                                              self.v_scale, context.cu_seqlens_q,
+                                              context.cu_seqlens_k, context.max_seqlen_q,
+                                              context.max_seqlen_k, softmax_scale=self.scale,
+                                              causal=True, block_table=context.block_tables)
         return flash_attn_with_kvcache_fp8(q.unsqueeze(1), self.k_cache, self.v_cache,
                                            self.k_scale, self.v_scale,
                                            cache_seqlens=context.context_lens,

@@ -198,3 +198,78 @@ def test_attention_module_fp8_decode(pkg):
     _assert_pool_equal(dev, ref)
     expect = O.fp8_decode(c["q"].unsqueeze(1), *ref, c["lens"], c["tables"], 128 ** -0.5)
     assert_fp8_close(out, expect)
+
+
+def _mixed_fp8_case(seed, dec_lens, pre_rows, Hq=32, Hkv=8, D=128, bs=256):
+    """Decode rows (context including the new token) and prefill rows (history,
+    new tokens) over one FP8 pool: the history slots (stored in a step before)
+    and the step's slots in the engine's decode-first layout."""
+    rows = [(L - 1, 1) for L in dec_lens] + list(pre_rows)
+    pages = [(h + n + bs - 1) // bs for h, n in rows]
+    NB = sum(pages) + 3
+    perm = det_perm(seed, NB).tolist()
+    tables, cur = [], 0
+    for n in pages:
+        tables.append(perm[cur:cur + n])
+        cur += n
+    slot = lambda r, p: tables[r][p // bs] * bs + p % bs
+    hist_slots = [slot(r, p) for r, (h, _) in enumerate(rows) for p in range(h)]
+    step_slots = [slot(r, p) for r, (h, n) in enumerate(rows) for p in range(h, h + n)]
+    W = max(pages)
+    pad = lambda ts: torch.tensor([t + [-1] * (W - len(t)) for t in ts], dtype=torch.int32)
+    d = len(dec_lens)
+    cu_q, cu_k = [0], [0]
+    for h, n in rows[d:]:
+        cu_q.append(cu_q[-1] + n)
+        cu_k.append(cu_k[-1] + h + n)
+    T = len(step_slots)
+    return dict(
+        NB=NB, Hkv=Hkv, d=d, T=T,
+        hist=(kv_values(seed + 1, (len(hist_slots), Hkv, D)),
+              kv_values(seed + 2, (len(hist_slots), Hkv, D)),
+              torch.tensor(hist_slots, dtype=torch.int32)),
+        k=kv_values(seed + 3, (T, Hkv, D)), v=kv_values(seed + 4, (T, Hkv, D)),
+        slots=torch.tensor(step_slots, dtype=torch.int32),
+        q=torch.from_numpy(det_normal(seed + 5, (T, Hq, D))).bfloat16(),
+        meta=dict(num_decode=d, num_prefill_tokens=T - d,
+                  decode_lens=torch.tensor(dec_lens, dtype=torch.int32),
+                  decode_tables=pad(tables[:d]) if d else None,
+                  prefill_cu_q=torch.tensor(cu_q, dtype=torch.int32),
+                  prefill_cu_k=torch.tensor(cu_k, dtype=torch.int32),
+                  prefill_tables=pad(tables[d:]), max_q=max(n for _, n in rows[d:]),
+                  max_k=max(h + n for h, n in rows[d:]), prefill_has_history=True))
+
+
+@pytest.mark.parametrize("dec_lens,pre_rows,seed", [
+    ([], [(1024, 300), (0, 77), (3000, 2048)], 3300),              # prefix-cache prefill only
+    ([900, 17, 4097], [(511, 129), (256, 1), (0, 600)], 3301),      # mixed step
+])
+def test_fp8_mixed_step_with_history_matches_oracle(pkg, dec_lens, pre_rows, seed):
+    """An FP8 pool in the engine's mixed step (MixedLLMEngine runs every step
+    through forward_mixed): quantising store bit-exact, FP8 decode rows and
+    prefill rows over cached pages (dequantised for the step) within the FP8
+    tolerance of the fp32 oracle on the dequantised pool."""
+    c = _mixed_fp8_case(seed, dec_lens, pre_rows)
+    ref = _pools(c["NB"], H=c["Hkv"])
+    dev = _gpu(_pools(c["NB"], H=c["Hkv"]))
+    hk, hv, hs = c["hist"]
+    O.fp8_append(hk, hv, *ref, hs)
+    pkg.store_kvcache_fp8(hk.cuda(), hv.cuda(), *dev, hs.cuda())
+    attn = pkg.Attention(32, 128, 128 ** -0.5, c["Hkv"])
+    attn.k_cache, attn.v_cache, attn.k_scale, attn.v_scale = dev
+    meta = {k: (t.cuda() if isinstance(t, torch.Tensor) else t) for k, t in c["meta"].items()}
+    pkg.set_context(False, slot_mapping=c["slots"].cuda(), mixed=pkg.MixedAttentionContext(**meta))
+    out = attn(c["q"].cuda(), c["k"].cuda(), c["v"].cuda())
+    pkg.reset_context()
+    torch.cuda.synchronize()
+    O.fp8_append(c["k"], c["v"], *ref, c["slots"])
+    _assert_pool_equal(dev, ref)
+    assert pkg.read_device_errors() == 0
+    d, m, scale = c["d"], c["meta"], 128 ** -0.5
+    if d:
+        exp_d = O.fp8_decode(c["q"][:d].unsqueeze(1), *ref, m["decode_lens"], m["decode_tables"],
+                             scale)
+        assert_fp8_close(out[:d], exp_d.squeeze(1))
+    exp_p = O.varlen(c["q"][d:], O.fp8_dequant(ref[0], ref[2]), O.fp8_dequant(ref[1], ref[3]),
+                     m["prefill_cu_q"], m["prefill_cu_k"], scale, m["prefill_tables"])
+    assert_fp8_close(out[d:], exp_p)

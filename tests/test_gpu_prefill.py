@@ -226,7 +226,7 @@ def test_longest_first_order_matches_row_major(pkg, q_lens, hist, seed):
         plain.data_ptr(), plain.stride(0), plain.stride(1), q.data_ptr(), q.stride(0), q.stride(1),
         q.shape[0], kc.data_ptr(), vc.data_ptr(), 0, 0, 0, kc.stride(0), vc.stride(0),
         cu_q.data_ptr(), cu_k.data_ptr(), rows, mq, tables.data_ptr(), tables.stride(0),
-        tables.shape[1], kc.shape[0], 256, 32, 8, 128, 128 ** -0.5, _lib.DTYPE_BF16, None, 0,
+        tables.shape[1], kc.shape[0], 256, 32, 8, 128, 128 ** -0.5, _lib.DTYPE_BF16, None, None, 0,
         err.data_ptr(), _lib.stream_ptr(q.device)), "paged_prefill")
     torch.cuda.synchronize()
     assert torch.equal(ordered, plain)
