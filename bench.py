@@ -202,6 +202,48 @@ def append_bytes(wl):
     return wl["B"] * wl["hkv"] * D * 2 * 2 * 2 + wl["B"] * 4
 
 
+def flash_attn_decode(wl, L, reps):
+    """The reference's own GPU decode dependency on this box: flash-attn's
+    flash_attn_with_kvcache (nanovllm/layers/attention.py:76-78) over the same
+    pool, tables, lengths and queries, timed with CUDA events over reps x L
+    launches (eager, as the reference calls it outside its graph).  Returns its
+    per-layer time, GB/s of the same algorithmic bytes and the largest
+    difference from our output of the same layers, or why it did not run."""
+    try:
+        import flash_attn
+        from flash_attn import flash_attn_with_kvcache
+    except Exception as e:  # noqa: BLE001 - report any import failure
+        return {"unavailable": f"import flash_attn: {type(e).__name__}: {e}"[:300]}
+    kc, vc = wl["kv"][0], wl["kv"][1]
+    tables = wl["tables"].clamp(min=0)      # padding -> a valid id: reads stay in bounds
+    def layer(l):
+        return flash_attn_with_kvcache(wl["q"][l].unsqueeze(1), kc[l], vc[l],
+                                       cache_seqlens=wl["lens"], block_table=tables,
+                                       softmax_scale=D ** -0.5, causal=True)
+    try:
+        diff = 0.0
+        for l in range(min(L, 4)):
+            o = layer(l).squeeze(1)
+            diff = max(diff, (o.float() - wl["out"][l].float()).abs().max().item())
+        torch.cuda.synchronize()
+        for l in range(L):
+            layer(l)
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(reps):
+            for l in range(L):
+                layer(l)
+        e.record()
+        torch.cuda.synchronize()
+    except Exception as e:  # noqa: BLE001 - a missing sm_100 kernel image lands here
+        return {"unavailable": f"flash_attn {flash_attn.__version__}: {type(e).__name__}: {e}"[:300]}
+    ms = s.elapsed_time(e) / (reps * L)
+    return {"version": flash_attn.__version__, "ms_per_layer": round(ms, 5),
+            "gbs": round(decode_bytes(wl) / (ms * 1e-3) / 1e9, 1),
+            "max_abs_diff_vs_ours": diff}
+
+
 # ----------------------------------------------------------------------------
 # our implementation
 # ----------------------------------------------------------------------------
@@ -372,6 +414,12 @@ def run_ours(args):
                                    "layers"}
         if n == 1 and not args.no_cpu_baseline and not wl["fp8"]:
             line["cpu_baseline"] = cpu_baseline(args, sample_seconds=args.cpu_seconds)
+        if args.against_flash_attn and n == 1 and not wl["fp8"]:
+            fa = flash_attn_decode(wl, L, reps)
+            if "ms_per_layer" in fa:
+                fa["ours_ms_per_layer"] = round(dec_ms, 5)
+                fa["speedup"] = round(fa["ms_per_layer"] / dec_ms, 3)
+            line["library_decode"] = {"flash_attn_with_kvcache": fa}
         print(json.dumps(line), flush=True)
     del graph, dgraph
     if dist is not None:
@@ -699,8 +747,11 @@ def run_model(args):
     """random-init Qwen3-4B (36 layers, N(0, 0.02) weights)
     decode step at TP = --gpus.  Prompts of random ids with context U[512, 4096]
     are prefilled through the tcgen05 varlen kernel, then the graph-captured
-    decode step (dense torch + this package's append / paged decode, NCCL
-    all-reduce after o_proj and down_proj) is timed; max over ranks."""
+    decode step (dense torch + this package's append / paged decode; o_proj and
+    down_proj with their TP all-reduce as the fused row-parallel kernel, or
+    cuBLAS + NCCL with --nccl-all-reduce) is timed; max over ranks.  At TP > 1
+    the step is then re-captured with cuBLAS + NCCL and timed again for
+    comparison (unless --nccl-all-reduce)."""
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -726,8 +777,11 @@ def run_model(args):
         prompts.append(ids[cur:cur + n])
         cur += n
     model = h.Qwen3Model(cfg, rank, world, None, seed=0, device=device,
-                         fused_qk_norm_rope=not args.unfused_qk)
-    runner = h.GreedyRunner(model, lens, args.warmup + args.steps + 2, seed=1, kv_dtype=args.kv)
+                         fused_qk_norm_rope=not args.unfused_qk,
+                         fused_all_reduce=not args.nccl_all_reduce)
+    compare = world > 1 and not args.nccl_all_reduce
+    runner = h.GreedyRunner(model, lens, (args.warmup + args.steps) * (2 if compare else 1) + 2,
+                            seed=1, kv_dtype=args.kv)
     t0 = time.time()
     tok = runner.prefill(prompts, chunk_tokens=32768)
     torch.cuda.synchronize()
@@ -750,10 +804,26 @@ def run_model(args):
             dist.barrier()
     ms = start.elapsed_time(end) / args.steps
     errs = pkg.read_device_errors()
-    t = torch.tensor([ms], device=device)
+    nccl_ms = 0.0
+    if compare:   # the same step with cuBLAS + NCCL for o_proj / down_proj
+        fused_comm, model.rowpar = model.rowpar, None
+        runner.graph = None
+        for _ in range(args.warmup):
+            tok = runner.decode(tok)
+        dist.barrier()
+        torch.cuda.synchronize()
+        start.record()
+        for _ in range(args.steps):
+            tok = runner.decode(tok)
+        end.record()
+        torch.cuda.synchronize()
+        dist.barrier()
+        nccl_ms = start.elapsed_time(end) / args.steps
+        model.rowpar = fused_comm
+    t = torch.tensor([ms, nccl_ms], device=device)
     if dist is not None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = t.item()
+    ms, nccl_ms = t.tolist()
     if rank == 0:
         # per-rank HBM bytes of one step: the KV read by attention (mean context
         # over the timed steps) + the append + this rank's weights
@@ -773,7 +843,10 @@ def run_model(args):
             "config": {"workload": "BASELINE config 5: random-init Qwen3-4B greedy decode step "
                                    f"(36 layers), batch {B}, context U[{args.ctx_lo}, "
                                    f"{args.ctx_hi}] after prefill, KV {args.kv}, q/k norm + "
-                                   f"RoPE {'torch ops' if args.unfused_qk else 'fused with the append'}",
+                                   f"RoPE {'torch ops' if args.unfused_qk else 'fused with the append'}"
+                                   + (", o_proj/down_proj + all-reduce "
+                                      + ("cuBLAS + NCCL" if args.nccl_all_reduce or world == 1
+                                         else "fused row-parallel kernel")),
                        "parallelism": f"tp{world}", "global_batch": B,
                        "prefill_seconds": round(prefill_s, 2)},
             "roofline": {"kernel": "whole decode step per rank (KV read + weights)",
@@ -781,11 +854,21 @@ def run_model(args):
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "peak_kind": peak_kind, "algorithmic_bytes": kv_bytes + w_bytes,
                          "traffic": None},
+            # per layer: the append (fused with q/k norm + RoPE, or alone), the
+            # decode's main + merge launches, and two fused row-parallel launches
+            "gpu_launches": args.steps * cfg.num_layers * (
+                3 + (2 if world > 1 and not args.nccl_all_reduce else 0)),
             "clocks": clocks.summary(),
             "device_errors": errs,
         }
+        if compare:
+            line["all_reduce_compare"] = {
+                "fused_ms_per_step": round(ms, 3), "nccl_ms_per_step": round(nccl_ms, 3),
+                "note": "same step re-captured with cuBLAS o_proj/down_proj + NCCL all-reduce, "
+                        "timed right after (contexts longer by warmup + steps tokens)"}
         print(json.dumps(line), flush=True)
     runner.release()
+    model.close()
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
@@ -851,6 +934,11 @@ def main():
     ap.add_argument("--unfused-qk", action="store_true",
                     help="model workload: q/k norm + RoPE as torch ops and the plain append")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--nccl-all-reduce", action="store_true",
+                    help="model workload: cuBLAS o_proj/down_proj + NCCL all-reduce instead of "
+                         "the fused row-parallel kernel")
+    ap.add_argument("--against-flash-attn", action="store_true",
+                    help="also time the reference's flash-attn decode on the same pool (N=1, bf16)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--cpu-batch", type=int, default=BATCH_PER_GPU)
     args = ap.parse_args()

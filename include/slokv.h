@@ -41,7 +41,7 @@ extern "C" {
 #define SLOKV_DEVERR_SLOT_RANGE   0x1u  /* slot_mapping entry < -1 or >= num_slots  */
 #define SLOKV_DEVERR_BLOCK_RANGE  0x2u  /* block_tables entry outside [0, num_blocks) */
 #define SLOKV_DEVERR_CONTEXT_LEN  0x4u  /* context length > table width * block_size */
-#define SLOKV_DEVERR_TIMEOUT      0x8u  /* a bounded wait on an mbarrier gave up      */
+#define SLOKV_DEVERR_TIMEOUT      0x8u  /* a bounded wait (mbarrier, peer flag) gave up */
 #define SLOKV_DEVERR_NONFINITE    0x10u /* FP8 encode met NaN/Inf (stored as code 0x7F) */
 
 /* ---- element types --------------------------------------------------------- */
@@ -331,6 +331,52 @@ int slokv_kv_block_copy(const void *src, int64_t src_plane_stride_bytes,
                         int32_t dst_capacity,
                         int32_t num_pages, int32_t num_planes, int64_t page_bytes,
                         uint32_t *dev_error, void *stream);
+
+/* ---- row-parallel linear + tensor-parallel all-reduce (one kernel) --------
+ *
+ * Replaces RowParallelLinear.forward (nanovllm/layers/linear.py:152-156):
+ *   y = F.linear(x, W_rank, bias if rank == 0 else None); dist.all_reduce(y)
+ * for the o_proj and down_proj of every decoder layer.  Every rank computes
+ * its partial x_r W_r^T on the tensor cores and the ranks exchange 128 x 128
+ * output tiles through each other's symmetric buffer over NVLink peer memory
+ * (owner-reduce, then broadcast of the reduced tile), all inside one launch.
+ * Result: y = round(bias + sum_r round(x_r W_r^T)) on every rank (the per-rank
+ * rounding is the reference's F.linear output; the sum is fp32 in rank order,
+ * rounded once), identical on every rank.
+ *
+ * x[i]: [tokens, k_features] (row stride x_row_stride elements), w[i]: [n_features,
+ * k_features] (nn.Linear weight of rank rank_base + i), bias[i]: [n_features] or
+ * NULL (bias may be NULL), y[i]: [tokens, n_features] output, for the
+ * `local_ranks` ranks rank_base .. rank_base + local_ranks - 1 this launch runs
+ * (1 in a one-process-per-GPU deployment; all ranks when one GPU emulates the
+ * group).  rank_buffers[r] (r < world): the symmetric buffer of rank r as mapped
+ * in this process (its own allocation, or a peer's opened with
+ * slokv_ipc_import), slokv_row_parallel_buffer_bytes(max_tokens, n_features,
+ * world) bytes each, zeroed once before first use; ignored when world == 1.
+ * state: 2 device uint32 of this process, zeroed once (the call counter the
+ * flags are compared against).  Every rank must make the same sequence of calls
+ * with the same tokens / geometry.  n_features % 128 == 0, k_features % 64 ==
+ * 0, tokens <= max_tokens, 16-bit dtype, row strides multiples of 8 elements,
+ * pointers 16-byte aligned (rank buffers 256-byte).  A peer that does not
+ * arrive within the wait limit sets SLOKV_DEVERR_TIMEOUT (the output is then
+ * undefined and the buffers must be zeroed again on every rank). */
+size_t slokv_row_parallel_buffer_bytes(int32_t max_tokens, int32_t n_features, int32_t world);
+int slokv_row_parallel_linear(const void *const *x, int64_t x_row_stride, const void *const *w,
+                              int64_t w_row_stride, const void *const *bias, void *const *y,
+                              int64_t y_row_stride, int32_t tokens, int32_t n_features,
+                              int32_t k_features, void *const *rank_buffers, int32_t world,
+                              int32_t rank_base, int32_t local_ranks, int32_t max_tokens,
+                              uint32_t *state, int32_t dtype, uint32_t *dev_error, void *stream);
+
+/* Symmetric-buffer plumbing: a zeroed device allocation owned by the library,
+ * and CUDA IPC export / import / close of it between the ranks' processes
+ * (handles are slokv_ipc_handle_size() bytes, exchanged by the host). */
+int slokv_device_alloc(size_t bytes, void **ptr);
+int slokv_device_free(void *ptr);
+int slokv_ipc_handle_size(void);
+int slokv_ipc_export(const void *ptr, void *handle_out);
+int slokv_ipc_import(const void *handle, void **ptr);
+int slokv_ipc_close(void *ptr);
 
 #ifdef __cplusplus
 }

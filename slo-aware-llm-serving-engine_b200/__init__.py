@@ -17,6 +17,7 @@ from .kvcache import (decode_workspace, e4m3_decode, e4m3_encode, flash_attn_var
                       kv_block_gather, kv_block_scatter, qk_norm_rope_append, store_kvcache,
                       store_kvcache_fp8)
 from .layers.attention import Attention
+from .layers.linear import RowParallelAllReduce, RowParallelLinear, row_parallel_buffer_bytes
 from .pool import KVPool, block_bytes, plan_num_blocks, tp_shard
 from .layers.mixed_attention import MixedAttentionContext, forward_mixed, forward_mixed_fp8
 from .utils.context import Context, get_context, reset_context, set_context
@@ -29,4 +30,5 @@ __all__ = [
     "forward_mixed_fp8", "get_context", "store_kvcache_fp8",
     "kv_block_copy", "kv_block_gather", "kv_block_scatter", "qk_norm_rope_append",
     "read_device_errors", "reset_context", "set_context", "store_kvcache",
+    "RowParallelAllReduce", "RowParallelLinear", "row_parallel_buffer_bytes",
 ]

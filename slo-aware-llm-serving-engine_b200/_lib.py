@@ -95,6 +95,19 @@ SIGNATURES = {
         _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_vp, _c_i64, _c_i32, _c_vp, _c_i32,
         _c_f32, _c_i32, _c_vp, _c_vp]),   # as slokv_paged_decode, without the workspace
     "slokv_paged_decode_noalloc_scratch_bytes": (_c_sz, []),
+    "slokv_row_parallel_buffer_bytes": (_c_sz, [_c_i32, _c_i32, _c_i32]),
+    "slokv_row_parallel_linear": (ctypes.c_int, [
+        _c_vp, _c_i64, _c_vp, _c_i64,             # x[], row stride, w[], row stride
+        _c_vp, _c_vp, _c_i64,                     # bias[] (or None), y[], row stride
+        _c_i32, _c_i32, _c_i32,                   # tokens, n_features, k_features
+        _c_vp, _c_i32, _c_i32, _c_i32, _c_i32,    # rank_buffers[], world, rank_base, local, max_tokens
+        _c_vp, _c_i32, _c_vp, _c_vp]),            # state, dtype, dev_error, stream
+    "slokv_device_alloc": (ctypes.c_int, [_c_sz, ctypes.POINTER(ctypes.c_void_p)]),
+    "slokv_device_free": (ctypes.c_int, [_c_vp]),
+    "slokv_ipc_handle_size": (ctypes.c_int, []),
+    "slokv_ipc_export": (ctypes.c_int, [_c_vp, _c_vp]),
+    "slokv_ipc_import": (ctypes.c_int, [_c_vp, ctypes.POINTER(ctypes.c_void_p)]),
+    "slokv_ipc_close": (ctypes.c_int, [_c_vp]),
     "slokv_kv_block_copy": (ctypes.c_int, [
         _c_vp, _c_i64, _c_i64, _c_vp, _c_i32,     # src, strides, ids, capacity
         _c_vp, _c_i64, _c_i64, _c_vp, _c_i32,     # dst, strides, ids, capacity

@@ -28,6 +28,7 @@ SOURCES = [
     "paged_prefill.cu",
     "qk_norm_rope.cu",
     "fp8_pages_dequant.cu",
+    "row_parallel.cu",
 ]
 HEADERS = ["common.cuh", "fp8_e4m3.cuh", "tcgen05.cuh"]
 

@@ -1,0 +1,622 @@
+// Row-parallel linear layer fused with its tensor-parallel all-reduce: the
+// o_proj / down_proj step of every decoder layer
+// (nanovllm/layers/linear.py:152-156: y = F.linear(x, W_rank) then
+// dist.all_reduce(y) over the TP group), as ONE persistent kernel per rank.
+//
+// Phase 1 (GEMM).  The rank's partial Y_r = X_r W_r^T is computed in 128 x 128
+// output tiles on the 5th-generation tensor cores: a TMA warp streams 128 x 64
+// slices of X and W (128-byte swizzle) through a 4-stage shared-memory ring, one
+// elected thread issues tcgen05.mma (kind::f16, M = N = 128, K = 16) into one of
+// two TMEM accumulators, and four epilogue warps read the finished accumulator
+// (tcgen05.ld), round it to 16 bits (the reference's per-rank F.linear output
+// is rounded the same way), stage it in shared memory and push it -- one
+// contiguous 32 KB tile, 512-byte coalesced stores -- into the symmetric buffer
+// of the tile's owner rank (tile % world) over NVLink peer memory, then publish
+// it with a system-scope release flag.  The MMA of the next tile overlaps the
+// epilogue of this one.
+//
+// Phase 2 (owner reduce).  For each tile it owns, a rank waits for the partial
+// flags of every source rank, sums the world partials in fp32 in rank order
+// (plus the bias, once), rounds once, writes its own Y rows and pushes the
+// reduced tile into every peer's result slot, again followed by a release flag.
+//
+// Phase 3.  Every rank copies the reduced tiles it does not own from its own
+// result slots (written by their owners) into Y.
+//
+// Two shots (reduce-scatter then all-gather) move 2 (world - 1) / world of Y
+// over NVLink per rank, the ring all-reduce volume, but with one hop each and
+// with the first shot overlapping the GEMM tile by tile.  Every rank ends with
+// bit-identical Y.  All loads are from this GPU's own memory (X, W, its
+// symmetric buffer); only stores cross NVLink.  No TMA multicast is used.
+//
+// Flags carry a per-call epoch (a device counter advanced by the last CTA of
+// each call), so nothing is reset between calls and the call is CUDA-graph
+// capturable.  Every wait is bounded (kWaitLimitNs); a wait that gives up sets
+// SLOKV_DEVERR_TIMEOUT and the CTA skips its remaining work.  The grid never
+// exceeds one CTA per SM and is launched cooperatively, so every CTA is
+// resident and the phase-2/3 waits (which only depend on other CTAs' phase 1/2
+// work) always end.  One launch may also run several ranks as virtual ranks
+// over buffers of this GPU (tests run the whole exchange on one GPU this way).
+#include <cstring>
+#include <mutex>
+#include <type_traits>
+
+#include "common.cuh"
+#include "tcgen05.cuh"
+
+#include <cudaTypedefs.h>
+
+namespace slokv {
+namespace rp {
+
+constexpr int kBM = 128, kBN = 128, kBK = 64;
+constexpr int kStages = 4;
+constexpr uint32_t kSlice = kBM * kBK * 2;         // 16 KB: 128 rows x 64 elements
+constexpr uint32_t kStageBytes = 2 * kSlice;       // X slice + W slice
+constexpr uint32_t kTileBytes = kBM * kBN * 2;     // 32 KB output tile
+constexpr int kChunks = kTileBytes / 16;           // 16-byte chunks per tile
+constexpr int kThreads = 192;                      // warps 0-3 epilogue, 4 TMA, 5 MMA
+constexpr int kEpiThreads = 128;
+constexpr int kMaxRanks = 8;
+constexpr uint32_t kTmemCols = 256;                // two 128-column accumulators
+constexpr uint32_t kOffStaging = kStages * kStageBytes;
+constexpr uint32_t kOffBars = kOffStaging + kTileBytes;
+constexpr int kNumBars = 2 * kStages + 4;          // full, empty, acc_full[2], acc_empty[2]
+constexpr uint32_t kSmemBytes = kOffBars + kNumBars * 8 + 16 + 1024;
+
+struct Maps {
+  CUtensorMap x[kMaxRanks];  // per local rank: X [tokens, K]
+  CUtensorMap w[kMaxRanks];  // per local rank: W [N, K]
+};
+
+struct Params {
+  int tokens, n, k;
+  int m_tiles, n_tiles, tiles, k_chunks;
+  int world, rank_base, ctas_per_rank;
+  int owned_max;                       // partial slots per source rank
+  int64_t y_stride;                    // elements
+  void *y[kMaxRanks];                  // per local rank
+  const void *bias[kMaxRanks];         // per local rank, [N] or null
+  uint8_t *buf[kMaxRanks];             // every rank's symmetric buffer, mapped here
+  int64_t off_result, off_pflag, off_rflag;
+  uint32_t *state;                     // [2]: completed calls, CTAs done in this call
+  uint32_t *err;
+};
+
+__device__ __forceinline__ void st_release_sys(uint32_t *f, uint32_t v) {
+  asm volatile("fence.acq_rel.sys;\n\tst.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(v)
+               : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *f) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+  return v;
+}
+
+// OR of `v` over the 128 epilogue threads (named barrier 1): every epilogue
+// thread gets the same answer, so they leave their loop together.
+__device__ __forceinline__ bool epi_any(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, 1, %2, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(v)), "n"(kEpiThreads)
+      : "memory");
+  return r != 0;
+}
+
+// Bounded wait until *f has reached `epoch` (modular comparison).
+__device__ __forceinline__ bool wait_flag(const uint32_t *f, uint32_t epoch) {
+  if (static_cast<int32_t>(ld_acquire_sys(f) - epoch) >= 0) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  while (true) {
+    __nanosleep(100);
+    if (static_cast<int32_t>(ld_acquire_sys(f) - epoch) >= 0) return true;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+  }
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, uint32_t bar,
+                                            int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar)
+      : "memory");
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float a, float b);
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t *>(&v);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
+  __half2 v = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t *>(&v);
+}
+template <typename T>
+__device__ __forceinline__ float2 unpack2(uint32_t u);
+template <>
+__device__ __forceinline__ float2 unpack2<__nv_bfloat16>(uint32_t u) {
+  return __bfloat1622float2(*reinterpret_cast<__nv_bfloat162 *>(&u));
+}
+template <>
+__device__ __forceinline__ float2 unpack2<__half>(uint32_t u) {
+  return __half22float2(*reinterpret_cast<__half2 *>(&u));
+}
+
+// Y row-major store of 16-byte chunk `c` (0..2047) of tile (m, nt), rows >= tokens skipped.
+__device__ __forceinline__ void store_y_chunk(const Params &p, void *y, int m, int nt, int c,
+                                              uint4 v) {
+  const int row = c >> 4;
+  const int tok = m * kBM + row;
+  if (tok >= p.tokens) return;
+  uint8_t *dst = static_cast<uint8_t *>(y) +
+                 (static_cast<int64_t>(tok) * p.y_stride + nt * kBN + (c & 15) * 8) * 2;
+  *reinterpret_cast<uint4 *>(dst) = v;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 1)
+    row_parallel_kernel(const __grid_constant__ Params p, const __grid_constant__ Maps maps) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                              ~uintptr_t(1023));
+  const uint32_t base = smem_u32(smem);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kOffBars);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + kOffBars + kNumBars * 8);
+  volatile uint32_t *abort_flag = tmem_slot + 1;
+  auto bar = [&](int i) { return smem_u32(bars + i); };
+  const int kFull = 0, kEmpty = kStages, kAccFull = 2 * kStages, kAccEmpty = 2 * kStages + 2;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int lr = blockIdx.x / p.ctas_per_rank;  // local (virtual) rank of this CTA
+  const int cta = blockIdx.x - lr * p.ctas_per_rank;
+  const int rank = p.rank_base + lr;
+  const int world = p.world;
+  const uint32_t epoch = *reinterpret_cast<volatile uint32_t *>(p.state) + 1u;
+  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+  constexpr uint32_t kIdesc = tc::idesc_f16(kBf16, false, kBM, kBN);
+
+  if (tid == 0) {
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(bar(kFull + i), 1);
+      mbar_init(bar(kEmpty + i), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar(kAccFull + i), 1);
+      mbar_init(bar(kAccEmpty + i), 4);  // one arrival per epilogue warp
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tc::tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+    tc::tmem_relinquish();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+  auto fail = [&]() {
+    record_error(p.err, SLOKV_DEVERR_TIMEOUT);
+    *abort_flag = 1;
+  };
+
+  // ---------------- phase 1: GEMM tiles -> owner partial slots ----------------
+  if (warp == 4) {
+    if (lane == 0) {  // TMA producer
+      prefetch_tensormap(&maps.x[lr]);
+      prefetch_tensormap(&maps.w[lr]);
+      int s = 0;
+      uint32_t ph = 0;
+      for (int tile = cta; tile < p.tiles && !*abort_flag; tile += p.ctas_per_rank) {
+        const int m = tile / p.n_tiles, nt = tile - (tile / p.n_tiles) * p.n_tiles;
+        for (int kc = 0; kc < p.k_chunks; ++kc) {
+          if (!mbar_wait(bar(kEmpty + s), ph ^ 1)) { fail(); break; }
+          const uint32_t dst = base + s * kStageBytes;
+          mbar_arrive_expect_tx(bar(kFull + s), kStageBytes);
+          tma_load_2d(dst, &maps.x[lr], bar(kFull + s), kc * kBK, m * kBM);
+          tma_load_2d(dst + kSlice, &maps.w[lr], bar(kFull + s), kc * kBK, nt * kBN);
+          if (++s == kStages) { s = 0; ph ^= 1; }
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 5) {
+    if (lane == 0) {  // MMA issuer
+      int s = 0;
+      uint32_t ph = 0;
+      int it = 0;
+      for (int tile = cta; tile < p.tiles && !*abort_flag; tile += p.ctas_per_rank, ++it) {
+        const int acc = it & 1;
+        if (!mbar_wait(bar(kAccEmpty + acc), ((it >> 1) & 1) ^ 1)) { fail(); break; }
+        tc::fence_after_sync();
+        const uint32_t d = tmem + acc * kBN;
+        bool ok = true;
+        for (int kc = 0; kc < p.k_chunks; ++kc) {
+          if (!mbar_wait(bar(kFull + s), ph)) { fail(); ok = false; break; }
+          tc::fence_after_sync();
+          const uint32_t a = base + s * kStageBytes, b = a + kSlice;
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            tc::mma_f16_ss(d, tc::smem_desc_sw128(a + kk * 32, 16, 1024),
+                           tc::smem_desc_sw128(b + kk * 32, 16, 1024), kIdesc, kc | kk);
+          tc::commit(bar(kEmpty + s));
+          if (++s == kStages) { s = 0; ph ^= 1; }
+        }
+        if (!ok) break;
+        tc::commit(bar(kAccFull + acc));
+      }
+    }
+    __syncwarp();
+  } else {  // epilogue warps 0-3: row 32 * warp + lane of the tile
+    const int row = warp * 32 + lane;
+    uint8_t *stage = smem + kOffStaging;
+    int it = 0;
+    for (int tile = cta; tile < p.tiles; tile += p.ctas_per_rank, ++it) {
+      const int acc = it & 1;
+      // all 128 threads take the same branch (epi_any), so none is left at bar 1
+      if (epi_any(*abort_flag != 0)) break;
+      if (epi_any(!mbar_wait(bar(kAccFull + acc), (it >> 1) & 1))) { fail(); break; }
+      tc::fence_after_sync();
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {  // 32 columns at a time
+        uint32_t r[32];
+        tc::ld32(tmem + (static_cast<uint32_t>(warp * 32) << 16) + acc * kBN + q * 32, r);
+        tc::wait_ld();
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {  // four 16-byte chunks of 8 columns
+          const int chunk = q * 4 + c;
+          uint4 v;
+          v.x = pack2<T>(__uint_as_float(r[8 * c + 0]), __uint_as_float(r[8 * c + 1]));
+          v.y = pack2<T>(__uint_as_float(r[8 * c + 2]), __uint_as_float(r[8 * c + 3]));
+          v.z = pack2<T>(__uint_as_float(r[8 * c + 4]), __uint_as_float(r[8 * c + 5]));
+          v.w = pack2<T>(__uint_as_float(r[8 * c + 6]), __uint_as_float(r[8 * c + 7]));
+          *reinterpret_cast<uint4 *>(stage + row * 256 + ((chunk ^ (row & 7)) << 4)) = v;
+        }
+      }
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(kAccEmpty + acc));  // accumulator free for tile it + 2
+      asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
+      const int m = tile / p.n_tiles, nt = tile - (tile / p.n_tiles) * p.n_tiles;
+      if (world == 1) {
+        for (int c = tid; c < kChunks; c += kEpiThreads) {
+          const int rr = c >> 4;
+          const uint4 v = *reinterpret_cast<const uint4 *>(stage + rr * 256 +
+                                                            (((c & 15) ^ (rr & 7)) << 4));
+          store_y_chunk(p, p.y[lr], m, nt, c, v);
+        }
+      } else {
+        const int owner = tile % world, slot = tile / world;
+        uint8_t *dst = p.buf[owner] +
+                       (static_cast<int64_t>(rank) * p.owned_max + slot) * kTileBytes;
+        for (int c = tid; c < kChunks; c += kEpiThreads) {
+          const int rr = c >> 4;
+          const uint4 v = *reinterpret_cast<const uint4 *>(stage + rr * 256 +
+                                                            (((c & 15) ^ (rr & 7)) << 4));
+          reinterpret_cast<uint4 *>(dst)[c] = v;
+        }
+      }
+      asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
+      if (world > 1 && tid == 0) {
+        const int owner = tile % world, slot = tile / world;
+        uint32_t *flags = reinterpret_cast<uint32_t *>(p.buf[owner] + p.off_pflag);
+        st_release_sys(flags + static_cast<int64_t>(rank) * p.owned_max + slot, epoch);
+      }
+    }
+  }
+  __syncthreads();
+
+  // ---------------- phase 2: reduce the tiles this rank owns ----------------
+  // (abort_flag is stable here: every writer has passed the barrier above, and
+  // below it only changes before a __syncthreads_or that all threads read)
+  if (world > 1 && !*abort_flag) {
+    const T *bias = static_cast<const T *>(p.bias[lr]);
+    uint8_t *own = p.buf[rank];
+    const uint32_t *pflags = reinterpret_cast<const uint32_t *>(own + p.off_pflag);
+    for (int slot = cta;; slot += p.ctas_per_rank) {
+      const int tile = slot * world + rank;
+      if (tile >= p.tiles) break;
+      const bool bad =
+          tid < world && !wait_flag(pflags + static_cast<int64_t>(tid) * p.owned_max + slot, epoch);
+      if (__syncthreads_or(bad)) {
+        if (tid == 0) fail();
+        break;
+      }
+      const int m = tile / p.n_tiles, nt = tile - (tile / p.n_tiles) * p.n_tiles;
+      for (int c = tid; c < kChunks; c += kThreads) {
+        float acc[8];
+        if (bias != nullptr) {
+          const uint4 b = __ldg(reinterpret_cast<const uint4 *>(bias + nt * kBN + (c & 15) * 8));
+          const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float2 f = unpack2<T>(bw[j]);
+            acc[2 * j] = f.x;
+            acc[2 * j + 1] = f.y;
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+        }
+        for (int src = 0; src < world; ++src) {
+          const uint4 v = __ldcg(reinterpret_cast<const uint4 *>(
+                                     own + (static_cast<int64_t>(src) * p.owned_max + slot) *
+                                               kTileBytes) +
+                                 c);
+          const uint32_t vw[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float2 f = unpack2<T>(vw[j]);
+            acc[2 * j] += f.x;
+            acc[2 * j + 1] += f.y;
+          }
+        }
+        uint4 o;
+        o.x = pack2<T>(acc[0], acc[1]);
+        o.y = pack2<T>(acc[2], acc[3]);
+        o.z = pack2<T>(acc[4], acc[5]);
+        o.w = pack2<T>(acc[6], acc[7]);
+        store_y_chunk(p, p.y[lr], m, nt, c, o);
+        for (int q = 1; q < world; ++q) {
+          const int peer = (rank + q) % world;
+          reinterpret_cast<uint4 *>(p.buf[peer] + p.off_result +
+                                    static_cast<int64_t>(tile) * kTileBytes)[c] = o;
+        }
+      }
+      __syncthreads();
+      if (tid > 0 && tid < world) {
+        const int peer = (rank + tid) % world;
+        st_release_sys(reinterpret_cast<uint32_t *>(p.buf[peer] + p.off_rflag) + tile, epoch);
+      }
+    }
+  }
+  __syncthreads();
+  if (world > 1 && !*abort_flag) {
+    // ---------------- phase 3: copy the tiles owned by peers ----------------
+    const uint8_t *results = p.buf[rank] + p.off_result;
+    const uint32_t *rflags = reinterpret_cast<const uint32_t *>(p.buf[rank] + p.off_rflag);
+    for (int i = cta;; i += p.ctas_per_rank) {
+      const int blk = i / (world - 1), r = i - blk * (world - 1);
+      const int tile = blk * world + r + (r >= rank ? 1 : 0);
+      if (blk * world >= p.tiles) break;
+      if (tile >= p.tiles) continue;
+      if (__syncthreads_or(tid == 0 && !wait_flag(rflags + tile, epoch))) {
+        if (tid == 0) fail();
+        break;
+      }
+      const int m = tile / p.n_tiles, nt = tile - (tile / p.n_tiles) * p.n_tiles;
+      for (int c = tid; c < kChunks; c += kThreads) {
+        const uint4 v = __ldcg(
+            reinterpret_cast<const uint4 *>(results + static_cast<int64_t>(tile) * kTileBytes) +
+            c);
+        store_y_chunk(p, p.y[lr], m, nt, c, v);
+      }
+    }
+  }
+
+  __syncthreads();
+  if (warp == 0) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem, kTmemCols);
+  }
+  if (tid == 0) {  // the last CTA of the call advances the epoch
+    __threadfence();
+    if (atomicAdd(p.state + 1, 1u) == gridDim.x - 1) {
+      atomicExch(p.state + 1, 0u);
+      __threadfence();
+      atomicExch(p.state, epoch);
+    }
+  }
+}
+
+// ---- host side -------------------------------------------------------------
+
+struct Layout {
+  int64_t tiles_max, owned_max, off_result, off_pflag, off_rflag, total;
+};
+
+inline int64_t align_up(int64_t v, int64_t a) { return (v + a - 1) / a * a; }
+
+Layout layout(int max_tokens, int n_features, int world) {
+  Layout l;
+  l.tiles_max = static_cast<int64_t>((max_tokens + kBM - 1) / kBM) * (n_features / kBN);
+  l.owned_max = (l.tiles_max + world - 1) / world;
+  const int64_t partial = static_cast<int64_t>(world) * l.owned_max * kTileBytes;
+  l.off_result = align_up(partial, 4096);
+  l.off_pflag = align_up(l.off_result + l.tiles_max * kTileBytes, 4096);
+  l.off_rflag = align_up(l.off_pflag + static_cast<int64_t>(world) * l.owned_max * 4, 256);
+  l.total = align_up(l.off_rflag + l.tiles_max * 4, 4096);
+  return l;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+// 2-D map {K (inner), rows} with a {64, 128} box and 128-byte swizzle; rows
+// past the end read as zeros.
+bool encode_2d(CUtensorMap *map, const void *base, CUtensorMapDataType dt, uint64_t k,
+               uint64_t rows, uint64_t row_stride_elems) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {k, rows};
+  cuuint64_t strides[1] = {row_stride_elems * 2};
+  cuuint32_t box[2] = {kBK, kBM};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(map, dt, 2, const_cast<void *>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int sm_count() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 148;
+  return n > 0 ? n : 148;
+}
+
+template <typename T>
+int launch(const Params &p, const Maps &maps, int local_ranks, cudaStream_t stream) {
+  static std::once_flag once;
+  static bool ok = false;
+  std::call_once(once, [] {
+    ok = cudaFuncSetAttribute(row_parallel_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              kSmemBytes) == cudaSuccess;
+  });
+  if (!ok) return SLOKV_ERR_CUDA;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(local_ranks * p.ctas_per_rank));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, row_parallel_kernel<T>, p, maps) == cudaSuccess ? SLOKV_OK
+                                                                                  : SLOKV_ERR_CUDA;
+}
+
+}  // namespace rp
+}  // namespace slokv
+
+extern "C" size_t slokv_row_parallel_buffer_bytes(int32_t max_tokens, int32_t n_features,
+                                                  int32_t world) {
+  using namespace slokv::rp;
+  if (max_tokens <= 0 || n_features <= 0 || n_features % kBN != 0 || world < 1 ||
+      world > kMaxRanks)
+    return 0;
+  return static_cast<size_t>(layout(max_tokens, n_features, world).total);
+}
+
+extern "C" int slokv_row_parallel_linear(
+    const void *const *x, int64_t x_row_stride, const void *const *w, int64_t w_row_stride,
+    const void *const *bias, void *const *y, int64_t y_row_stride, int32_t tokens,
+    int32_t n_features, int32_t k_features, void *const *rank_buffers, int32_t world,
+    int32_t rank_base, int32_t local_ranks, int32_t max_tokens, uint32_t *state, int32_t dtype,
+    uint32_t *dev_error, void *stream) {
+  using namespace slokv;
+  using namespace slokv::rp;
+  if (world < 1 || world > kMaxRanks || local_ranks < 1 || rank_base < 0 ||
+      rank_base + local_ranks > world || tokens < 0 || max_tokens <= 0 || tokens > max_tokens ||
+      n_features <= 0 || k_features <= 0)
+    return SLOKV_ERR_INVALID_ARG;
+  if (n_features % kBN != 0 || k_features % kBK != 0) return SLOKV_ERR_UNSUPPORTED;
+  if (dtype != SLOKV_DTYPE_BF16 && dtype != SLOKV_DTYPE_F16) return SLOKV_ERR_UNSUPPORTED;
+  if (tokens == 0) return SLOKV_OK;
+  if (!x || !w || !y || !state || (world > 1 && !rank_buffers)) return SLOKV_ERR_INVALID_ARG;
+  if (x_row_stride < k_features || w_row_stride < k_features || y_row_stride < n_features)
+    return SLOKV_ERR_INVALID_ARG;
+  if ((x_row_stride | w_row_stride | y_row_stride) & 7) return SLOKV_ERR_ALIGNMENT;
+  Params p = {};
+  Maps maps;
+  const CUtensorMapDataType dt =
+      dtype == SLOKV_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  for (int i = 0; i < local_ranks; ++i) {
+    if (!x[i] || !w[i] || !y[i]) return SLOKV_ERR_INVALID_ARG;
+    const uintptr_t a = reinterpret_cast<uintptr_t>(x[i]) | reinterpret_cast<uintptr_t>(w[i]) |
+                        reinterpret_cast<uintptr_t>(y[i]) |
+                        reinterpret_cast<uintptr_t>(bias ? bias[i] : nullptr);
+    if (a & 15) return SLOKV_ERR_ALIGNMENT;
+    if (!encode_2d(&maps.x[i], x[i], dt, k_features, tokens, x_row_stride) ||
+        !encode_2d(&maps.w[i], w[i], dt, k_features, n_features, w_row_stride))
+      return SLOKV_ERR_CUDA;
+    p.y[i] = y[i];
+    p.bias[i] = bias ? bias[i] : nullptr;
+  }
+  if (world > 1) {
+    for (int r = 0; r < world; ++r) {
+      if (!rank_buffers[r] || (reinterpret_cast<uintptr_t>(rank_buffers[r]) & 255))
+        return SLOKV_ERR_INVALID_ARG;
+      p.buf[r] = static_cast<uint8_t *>(rank_buffers[r]);
+    }
+  }
+  const Layout l = layout(max_tokens, n_features, world);
+  p.tokens = tokens;
+  p.n = n_features;
+  p.k = k_features;
+  p.m_tiles = (tokens + kBM - 1) / kBM;
+  p.n_tiles = n_features / kBN;
+  p.tiles = p.m_tiles * p.n_tiles;
+  p.k_chunks = k_features / kBK;
+  p.world = world;
+  p.rank_base = rank_base;
+  p.owned_max = static_cast<int>(l.owned_max);
+  p.off_result = l.off_result;
+  p.off_pflag = l.off_pflag;
+  p.off_rflag = l.off_rflag;
+  p.y_stride = y_row_stride;
+  p.state = state;
+  p.err = dev_error;
+  const int per_rank = sm_count() / local_ranks;
+  if (per_rank < 1) return SLOKV_ERR_UNSUPPORTED;
+  p.ctas_per_rank = p.tiles < per_rank ? p.tiles : per_rank;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return dtype == SLOKV_DTYPE_BF16 ? launch<__nv_bfloat16>(p, maps, local_ranks, st)
+                                   : launch<__half>(p, maps, local_ranks, st);
+}
+
+// ---- symmetric buffers shared between the ranks' processes (CUDA IPC) --------
+
+extern "C" int slokv_device_alloc(size_t bytes, void **ptr) {
+  if (!ptr || bytes == 0) return SLOKV_ERR_INVALID_ARG;
+  *ptr = nullptr;
+  if (cudaMalloc(ptr, bytes) != cudaSuccess) return SLOKV_ERR_CUDA;
+  if (cudaMemset(*ptr, 0, bytes) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
+    cudaFree(*ptr);
+    *ptr = nullptr;
+    return SLOKV_ERR_CUDA;
+  }
+  return SLOKV_OK;
+}
+
+extern "C" int slokv_device_free(void *ptr) {
+  if (!ptr) return SLOKV_OK;
+  return cudaFree(ptr) == cudaSuccess ? SLOKV_OK : SLOKV_ERR_CUDA;
+}
+
+extern "C" int slokv_ipc_handle_size(void) { return static_cast<int>(sizeof(cudaIpcMemHandle_t)); }
+
+extern "C" int slokv_ipc_export(const void *ptr, void *handle_out) {
+  if (!ptr || !handle_out) return SLOKV_ERR_INVALID_ARG;
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, const_cast<void *>(ptr)) != cudaSuccess) return SLOKV_ERR_CUDA;
+  memcpy(handle_out, &h, sizeof(h));
+  return SLOKV_OK;
+}
+
+extern "C" int slokv_ipc_import(const void *handle, void **ptr) {
+  if (!handle || !ptr) return SLOKV_ERR_INVALID_ARG;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  *ptr = nullptr;
+  return cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess
+             ? SLOKV_OK
+             : SLOKV_ERR_CUDA;
+}
+
+extern "C" int slokv_ipc_close(void *ptr) {
+  if (!ptr) return SLOKV_OK;
+  return cudaIpcCloseMemHandle(ptr) == cudaSuccess ? SLOKV_OK : SLOKV_ERR_CUDA;
+}

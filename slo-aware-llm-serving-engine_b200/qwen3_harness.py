@@ -12,7 +12,9 @@ not part of the path.
 
 Tensor parallelism splits query / KV heads and the MLP columns over the
 process group and all-reduces the o_proj and down_proj outputs
-(nanovllm/layers/linear.py:152-156); the embedding / LM head is replicated on
+(nanovllm/layers/linear.py:152-156) -- by default with the fused row-parallel
+kernel (GEMM + tile exchange over NVLink in one launch), else cuBLAS + NCCL;
+the embedding / LM head is replicated on
 every rank, so every rank computes the same logits and the same greedy token.
 Weights are N(0, init_std) drawn per full tensor from a seeded generator and
 then sliced, so the global model is identical for every TP size.
@@ -26,6 +28,7 @@ import torch.nn.functional as F
 
 from .kvcache import qk_norm_rope_append
 from .layers.attention import Attention
+from .layers.linear import RowParallelAllReduce
 from .pool import KVPool, tp_shard
 from .utils.context import get_context, reset_context, set_context
 
@@ -71,7 +74,8 @@ class Qwen3Model:
 
     def __init__(self, cfg: Qwen3Config, tp_rank: int = 0, tp_size: int = 1, group=None,
                  seed: int = 0, device="cuda", dtype=torch.bfloat16,
-                 fused_qk_norm_rope: bool = True):
+                 fused_qk_norm_rope: bool = True, fused_all_reduce: bool = True,
+                 row_parallel_max_tokens: int = 4096):
         self.cfg, self.tp_rank, self.tp_size, self.group = cfg, tp_rank, tp_size, group
         # q/k RMSNorm + RoPE + append in one kernel (qk_norm_rope_append) for
         # layers whose attention is this package's module on a bf16/f16 pool
@@ -110,6 +114,18 @@ class Qwen3Model:
         self.cos = freqs.cos().to(self.device)
         self.sin = freqs.sin().to(self.device)
         self.cos_sin = torch.cat((self.cos, self.sin), dim=-1).contiguous()
+        # o_proj / down_proj + TP all-reduce as one kernel per rank
+        # (slokv_row_parallel_linear); collective construction over `group`.
+        # (CPU instances exist only for the weight-sharding checks.)
+        self.rowpar = None
+        if tp_size > 1 and fused_all_reduce and self.device.type == "cuda":
+            self.rowpar = RowParallelAllReduce(row_parallel_max_tokens, H, self.device, group)
+
+    def close(self):
+        """Release the fused all-reduce buffers (collective over the TP group)."""
+        if self.rowpar is not None:
+            self.rowpar.close()
+            self.rowpar = None
 
     def _normal(self, shape, seed: int, idx: int) -> torch.Tensor:
         g = torch.Generator(device=self.device)
@@ -127,10 +143,14 @@ class Qwen3Model:
         x1, x2 = x.float().chunk(2, dim=-1)
         return torch.cat((x1 * cos - x2 * sin, x2 * cos + x1 * sin), dim=-1).to(x.dtype)
 
-    def _all_reduce(self, x):
+    def _row_parallel(self, x, w):
+        """RowParallelLinear.forward (nanovllm/layers/linear.py:152-156)."""
+        if self.rowpar is not None:
+            return self.rowpar(x, w)
+        y = F.linear(x, w)
         if self.tp_size > 1:
-            torch.distributed.all_reduce(x, group=self.group)
-        return x
+            torch.distributed.all_reduce(y, group=self.group)
+        return y
 
     def forward(self, input_ids: torch.Tensor, positions: torch.Tensor) -> torch.Tensor:
         """Final normed hidden states [T, hidden]; the Context must be set."""
@@ -162,10 +182,10 @@ class Qwen3Model:
                 v = v.view(-1, self.hkv, D)                # strided view, as the reference
                 q, k = self._rope(positions, q), self._rope(positions, k)
                 o = lw.attn(q, k, v)
-            h = self._all_reduce(F.linear(o.flatten(1, -1), lw.wo))
+            h = self._row_parallel(o.flatten(1, -1), lw.wo)
             x, res = add_rms_norm(h, res, lw.ln2, eps)
             gate, up = F.linear(x, lw.wgu).chunk(2, dim=-1)
-            h = self._all_reduce(F.linear(F.silu(gate) * up, lw.wd))
+            h = self._row_parallel(F.silu(gate) * up, lw.wd)
         h, _ = add_rms_norm(h, res, self.norm, eps)
         return h
 

@@ -81,3 +81,33 @@ def test_block_copy_argument_checks(pkg):
     assert call(n=2, cap=-1) == -1
     p = ctypes.c_void_p(16)
     assert call(src=p, sps=8, dst=p, dps=16, n=2) == -2
+
+
+def test_row_parallel_argument_checks(pkg):
+    lib = pkg._lib.lib()
+    def call(tokens=4, n=2560, k=1024, world=2, base=0, local=1, max_tokens=512, dtype=0,
+             x=None, w=None, y=None, bufs=None, state=None):
+        return lib.slokv_row_parallel_linear(x, k, w, k, None, y, n, tokens, n, k, bufs, world,
+                                             base, local, max_tokens, state, dtype, None, None)
+    assert call(tokens=0) == 0                       # nothing to do
+    assert call(tokens=-1) == -1
+    assert call(tokens=600) == -1                    # more rows than the buffers hold
+    assert call(world=9) == -1 and call(world=0) == -1
+    assert call(base=1, local=2) == -1               # ranks beyond the group
+    assert call(n=2500) == -3 and call(k=1000) == -3  # 128-wide output / 64-deep K tiles
+    assert call(dtype=2) == -3                       # 16-bit inputs only
+    assert call() == -1                              # null pointers
+
+
+def test_row_parallel_buffer_layout(pkg):
+    lib = pkg._lib.lib()
+    # partial slots [world][ceil(tiles / world)] + result slots [tiles] of 32 KB tiles + flags
+    for T, n, world in ((1, 2560, 2), (512, 2560, 4), (8192, 2560, 8), (130, 1024, 3)):
+        tiles = -(-T // 128) * (n // 128)
+        got = lib.slokv_row_parallel_buffer_bytes(T, n, world)
+        data = (world * -(-tiles // world) + tiles) * 32768
+        assert data < got <= data + 3 * 4096 + 4 * (world * -(-tiles // world) + tiles) + 8192
+        assert got % 4096 == 0
+    assert lib.slokv_row_parallel_buffer_bytes(128, 2500, 2) == 0
+    assert lib.slokv_row_parallel_buffer_bytes(0, 2560, 2) == 0
+    assert lib.slokv_row_parallel_buffer_bytes(128, 2560, 9) == 0

@@ -1,0 +1,119 @@
+"""Fused row-parallel linear + TP all-reduce (slokv_row_parallel_linear): the
+reference's RowParallelLinear.forward (nanovllm/layers/linear.py:152-156,
+y = all_reduce(F.linear(x_r, W_r))) on the tensor cores with the tile exchange
+over peer memory.
+
+On one GPU every rank of a 2/4/8-rank group runs inside one launch (emulated
+ranks, one symmetric buffer per rank on this GPU), which exercises the whole
+exchange: partial tiles pushed to their owner, owner reduce, broadcast of the
+reduced tiles, per-call epochs.  Results are checked against the fp32 product
+sum_r x_r W_r^T with the bound of the kernel's two roundings (each rank's
+partial rounded to bf16, as the reference's F.linear output is, and the sum
+rounded once), against cuBLAS per-rank partials summed the same way, and for
+bit-equality across ranks.  tests/test_gpu_row_parallel_mp.py runs the same
+check with one process per GPU."""
+import pytest
+import torch
+import torch.nn.functional as F
+
+pytestmark = pytest.mark.gpu
+
+N = 2560  # Qwen3-4B hidden size: the o_proj / down_proj output width
+
+
+def _case(seed, world, T, K, bias=False):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    xs = [torch.randn(T, K, device="cuda", generator=g).bfloat16() for _ in range(world)]
+    ws = [(torch.randn(N, K, device="cuda", generator=g) * 0.02).bfloat16() for _ in range(world)]
+    b = (torch.randn(N, device="cuda", generator=g) * 0.1).bfloat16() if bias else None
+    return xs, ws, b
+
+
+def _check(ys, xs, ws, b):
+    parts = [x.float() @ w.float().t() for x, w in zip(xs, ws)]
+    exact = sum(parts) + (b.float() if b is not None else 0)
+    # half an ulp of bf16 (2^-9 relative) per partial and for the final rounding, doubled
+    bound = 2 ** -8 * (sum(p.abs() for p in parts) + exact.abs()) + 1e-6
+    for r, y in enumerate(ys):
+        assert torch.isfinite(y.float()).all()
+        assert torch.equal(y, ys[0]), f"rank {r} differs from rank 0"
+    err = (ys[0].float() - exact).abs()
+    assert (err <= bound).all(), f"max excess {(err - bound).max().item():.3e}"
+    # the reference's arithmetic: cuBLAS bf16 partials, summed (fp32 here, rounded once)
+    ref = sum(F.linear(x, w).float() for x, w in zip(xs, ws))
+    if b is not None:
+        ref = ref + b.float()
+    d = (ys[0].float() - ref.bfloat16().float()).abs()
+    assert d.max().item() <= 2 ** -6 * max(1.0, ref.abs().max().item())
+    assert (d == 0).float().mean().item() >= 0.95
+
+
+@pytest.mark.parametrize("world,T,K,seed", [
+    (1, 77, 512, 10),        # no exchange: the GEMM alone, ragged rows
+    (2, 512, 2048, 11),      # o_proj at TP=2, decode batch 512
+    (4, 700, 1216, 12),      # down_proj at TP=8 depth, 6 row tiles, ragged
+    (8, 130, 512, 13),       # 8 ranks, 2 row tiles
+    (2, 1, 1024, 14),        # a single row
+])
+def test_row_parallel_emulated_matches_fp32(pkg, world, T, K, seed):
+    xs, ws, _ = _case(seed, world, T, K)
+    comm = pkg.RowParallelAllReduce.emulated(world, max_tokens=1024, n_features=N,
+                                             device="cuda")
+    try:
+        ys = comm.emulate(xs, ws)
+        torch.cuda.synchronize()
+        assert pkg.read_device_errors() == 0
+        _check(ys, xs, ws, None)
+    finally:
+        comm.close()
+
+
+def test_row_parallel_bias_chunks_and_repeated_calls(pkg):
+    """Bias added once; calls longer than max_tokens run in chunks; repeated
+    calls on the same buffers (epochs advance, no reset) stay correct."""
+    world = 4
+    comm = pkg.RowParallelAllReduce.emulated(world, max_tokens=256, n_features=N, device="cuda")
+    try:
+        for it, T in enumerate((600, 3, 256, 129)):
+            xs, ws, b = _case(100 + it, world, T, 512, bias=True)
+            ys = comm.emulate(xs, ws, biases=[b] * world)
+            torch.cuda.synchronize()
+            assert pkg.read_device_errors() == 0
+            _check(ys, xs, ws, b)
+        assert int(comm.state[0].item()) == 3 + 1 + 1 + 1   # one epoch per launch (600 -> 3)
+    finally:
+        comm.close()
+
+
+def test_row_parallel_graph_capture(pkg):
+    """Captured in a CUDA graph (as the decode step is) and replayed with new
+    inputs copied into the captured buffers."""
+    world, T, K = 2, 384, 1024
+    comm = pkg.RowParallelAllReduce.emulated(world, max_tokens=512, n_features=N, device="cuda")
+    try:
+        xs, ws, _ = _case(200, world, T, K)
+        outs = [torch.empty(T, N, dtype=torch.bfloat16, device="cuda") for _ in range(world)]
+        comm.emulate(xs, ws, outs=outs)          # eager warm-up
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            comm.emulate(xs, ws, outs=outs)
+        for it in range(3):
+            nx, nw, _ = _case(201 + it, world, T, K)
+            for a, b in zip(xs + ws, nx + nw):
+                a.copy_(b)
+            graph.replay()
+            torch.cuda.synchronize()
+            assert pkg.read_device_errors() == 0
+            _check(outs, xs, ws, None)
+        del graph
+    finally:
+        comm.close()
+
+
+def test_row_parallel_linear_module_single_rank(pkg):
+    """RowParallelLinear without a process group is F.linear (TP = 1)."""
+    m = pkg.RowParallelLinear(1024, N).cuda().bfloat16()
+    torch.nn.init.normal_(m.weight, std=0.02)
+    x = torch.randn(5, 1024, device="cuda").bfloat16()
+    assert torch.equal(m(x), F.linear(x, m.weight))

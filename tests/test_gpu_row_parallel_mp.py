@@ -1,0 +1,110 @@
+"""Fused row-parallel linear + all-reduce with one process per GPU (NCCL group
+for the handshake, CUDA IPC symmetric buffers, P2P stores over NVLink), against
+the reference's F.linear + dist.all_reduce and the fp32 product.  Needs >= 2
+GPUs; skipped otherwise.  The process group has a short timeout and every wait
+in the kernel is bounded, so a rank that fails ends the others with an error."""
+import datetime
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+N = 2560
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, queue):
+    import importlib
+    import sys
+
+    import torch.distributed as dist
+    import torch.nn.functional as F
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, root)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    result = {"rank": rank}
+    try:
+        pkg = importlib.import_module("slo-aware-llm-serving-engine_b200")
+        comm = pkg.RowParallelAllReduce(max_tokens=1024, n_features=N, device="cuda")
+        worst = 0.0
+        for it, (T, K) in enumerate(((512, 1024), (77, 2432), (1500, 512))):
+            g = torch.Generator(device="cuda").manual_seed(1000 * it + rank)
+            x = torch.randn(T, K, device="cuda", generator=g).bfloat16()
+            w = (torch.randn(N, K, device="cuda", generator=g) * 0.02).bfloat16()
+            y = comm(x, w)
+            ref = F.linear(x, w)
+            dist.all_reduce(ref)                      # the reference's collective
+            exact = (x.float() @ w.float().t())
+            absum = exact.abs()
+            dist.all_reduce(exact)
+            dist.all_reduce(absum)
+            torch.cuda.synchronize()
+            bound = 2 ** -8 * (absum + exact.abs()) + 1e-6
+            err = (y.float() - exact).abs()
+            worst = max(worst, (err - bound).max().item())
+            ys = [torch.empty_like(y) for _ in range(world)]
+            dist.all_gather(ys, y)
+            result[f"same_{it}"] = all(torch.equal(ys[0], t) for t in ys)
+            result[f"vs_nccl_{it}"] = (y.float() - ref.float()).abs().max().item()
+        # captured in a graph, replayed
+        x = torch.randn(256, 1024, device="cuda").bfloat16()
+        w = (torch.randn(N, 1024, device="cuda") * 0.02).bfloat16()
+        out = torch.empty(256, N, dtype=torch.bfloat16, device="cuda")
+        comm(x, w, out=out)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            comm(x, w, out=out)
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize()
+        ref = F.linear(x, w)
+        dist.all_reduce(ref)
+        result["graph_vs_nccl"] = (out.float() - ref.float()).abs().max().item()
+        del graph
+        result["worst_excess"] = worst
+        result["errors"] = pkg.read_device_errors()
+        dist.barrier()
+        comm.close()
+    except Exception as e:  # noqa: BLE001 - reported to the parent
+        result["exception"] = repr(e)
+    finally:
+        queue.put(result)
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                    reason="needs two GPUs")
+def test_row_parallel_two_processes_match_nccl():
+    world = 2
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, queue)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [queue.get(timeout=300) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+    for r in results:
+        assert "exception" not in r, r
+        assert r["errors"] == 0, r
+        assert r["worst_excess"] <= 0, r
+        assert all(r[f"same_{i}"] for i in range(3)), r
+        assert all(r[f"vs_nccl_{i}"] <= 0.0625 for i in range(3)), r
+        assert r["graph_vs_nccl"] <= 0.0625, r
+    for p in procs:
+        assert p.exitcode == 0
