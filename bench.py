@@ -740,6 +740,120 @@ def run_copy(args):
         "gpu_launches": args.steps, "clocks": clocks.summary()}), flush=True)
 
 
+ROWPAR_METRIC = "row-parallel linear + TP all-reduce, us per call (o_proj, down_proj of Qwen3-4B)"
+
+
+def run_rowpar(args):
+    """The o_proj / down_proj step of config 5 alone at TP = --gpus: x [T, K/t] @
+    W_r^T [2560, K/t] then the sum over ranks, T = --batch rows (the decode
+    batch), as the fused row-parallel kernel and as the reference's cuBLAS
+    F.linear + NCCL all-reduce (each also alone).  Every variant is captured as
+    a CUDA graph of `reps` back-to-back calls and timed with CUDA events over
+    --steps replays; max over ranks.  Roofline of the fused call: the slower of
+    its tensor-core time (FLOPs / measured bf16 peak) and its NVLink time
+    (2 (t-1)/t of y per rank over the measured 770 GB/s peer-copy rate)."""
+    import torch.nn.functional as F
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+    pkg = importlib.import_module("slo-aware-llm-serving-engine_b200")
+    T, N, reps = args.batch, 2560, 8
+    comm = pkg.RowParallelAllReduce(T, N, device)
+    g = torch.Generator(device=device).manual_seed(77 + rank)
+    peak, peak_kind = measured_tensor_peak()
+    results = {}
+    for name, K in (("o_proj", 4096 // world), ("down_proj", 9728 // world)):
+        x = torch.randn(T, K, device=device, generator=g).bfloat16()
+        w = (torch.randn(N, K, device=device, generator=g) * 0.02).bfloat16()
+        y = torch.empty(T, N, dtype=torch.bfloat16, device=device)
+        yr = torch.empty(T, N, dtype=torch.bfloat16, device=device)
+
+        def fused():
+            comm(x, w, out=y)
+
+        def gemm():
+            torch.matmul(x, w.t(), out=yr)
+
+        def allreduce():
+            if dist is not None:
+                dist.all_reduce(yr)
+
+        def reference():
+            gemm()
+            allreduce()
+
+        times = {}
+        for vname, fn in (("fused", fused), ("cublas_gemm", gemm), ("nccl_all_reduce", allreduce),
+                          ("cublas_plus_nccl", reference)):
+            if vname == "nccl_all_reduce" and dist is None:
+                continue
+            fn()
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                for _ in range(reps):
+                    fn()
+            for _ in range(args.warmup):
+                graph.replay()
+            if dist is not None:
+                dist.barrier()
+            torch.cuda.synchronize()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            for _ in range(args.steps):
+                graph.replay()
+            e.record()
+            torch.cuda.synchronize()
+            us = s.elapsed_time(e) * 1e3 / (args.steps * reps)
+            t = torch.tensor([us], device=device)
+            if dist is not None:
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            times[vname] = round(t.item(), 2)
+            del graph
+        # correctness of the fused call against the reference arithmetic
+        fused()
+        reference()
+        torch.cuda.synchronize()
+        diff = (y.float() - yr.float()).abs().max().item()
+        flops = 2.0 * T * N * K
+        link_bytes = 2.0 * (world - 1) / world * T * N * 2
+        target_us = max(flops / (peak * 1e12), link_bytes / 770e9) * 1e6
+        results[name] = dict(K_per_rank=K, us=times, max_abs_diff_vs_reference=diff,
+                             roofline={"target_us": round(target_us, 2),
+                                       "frac": round(target_us / times["fused"], 4),
+                                       "tensor_tflops": round(flops / (times["fused"] * 1e-6) / 1e12, 1),
+                                       "peak_tflops": peak, "peak_kind": peak_kind,
+                                       "nvlink_bytes_per_rank": int(link_bytes)})
+    errs = pkg.read_device_errors()
+    if rank == 0:
+        per_layer = sum(r["us"]["fused"] for r in results.values())
+        ref_layer = sum(r["us"]["cublas_plus_nccl"] for r in results.values())
+        print(json.dumps({
+            "metric": ROWPAR_METRIC, "value": round(per_layer, 2), "unit": "us/layer",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic N(0,1) activations, N(0, 0.02) weights",
+            "config": {"workload": "o_proj + down_proj of one Qwen3-4B layer with their TP "
+                                   "all-reduce (RowParallelLinear.forward)", "rows": T,
+                       "out_features": N, "parallelism": f"tp{world}",
+                       "graph": f"{reps} calls per CUDA graph"},
+            "reference_us_per_layer": round(ref_layer, 2),
+            "shapes": results, "gpu_launches": args.steps * reps * 2, "device_errors": errs,
+        }), flush=True)
+    comm.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 MODEL_METRIC = "full-model greedy decode tokens/s, random-init Qwen3-4B (config 5), TP = n_gpus"
 
 
@@ -918,9 +1032,11 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["decode", "mixed", "copy", "model"], default="decode",
+    ap.add_argument("--workload", choices=["decode", "mixed", "copy", "model", "rowpar"],
+                    default="decode",
                     help="decode: config 2/4 (the headline); mixed: config 3 prefill + decode; "
-                         "model: config 5 full random-init model at TP = --gpus")
+                         "model: config 5 full random-init model at TP = --gpus; "
+                         "rowpar: the fused row-parallel linear + all-reduce alone")
     ap.add_argument("--kv", choices=["bf16", "fp8"], default="bf16",
                     help="cache format: bf16 (config 2, the headline) or fp8 (config 4)")
     ap.add_argument("--batch", type=int, default=None, help="sequences per GPU")
@@ -950,6 +1066,8 @@ def main():
             args.batch = 512 if (args.gpus > 1 or fp8_defaults) else 256
         args.ctx_lo = args.ctx_lo or CTX_LO
         args.ctx_hi = args.ctx_hi or CTX_HI
+    if args.workload == "rowpar" and args.batch is None:
+        args.batch = 512
     if args.batch is None:
         args.batch = 128 if fp8_defaults else BATCH_PER_GPU
     if args.ctx_lo is None:
@@ -967,6 +1085,8 @@ def main():
         run_copy(args)
     elif args.workload == "model":
         run_model(args)
+    elif args.workload == "rowpar":
+        run_rowpar(args)
     else:
         run_ours(args)
 

@@ -355,7 +355,7 @@ int slokv_kv_block_copy(const void *src, int64_t src_plane_stride_bytes,
  * world) bytes each, zeroed once before first use; ignored when world == 1.
  * state: 2 device uint32 of this process, zeroed once (the call counter the
  * flags are compared against).  Every rank must make the same sequence of calls
- * with the same tokens / geometry.  n_features % 128 == 0, k_features % 64 ==
+ * with the same tokens / geometry.  world in {1, 2, 4, 8}, n_features % 128 == 0, k_features % 64 ==
  * 0, tokens <= max_tokens, 16-bit dtype, row strides multiples of 8 elements,
  * pointers 16-byte aligned (rank buffers 256-byte).  A peer that does not
  * arrive within the wait limit sets SLOKV_DEVERR_TIMEOUT (the output is then

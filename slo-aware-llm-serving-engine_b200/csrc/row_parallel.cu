@@ -4,23 +4,37 @@
 // dist.all_reduce(y) over the TP group), as ONE persistent kernel per rank.
 //
 // Phase 1 (GEMM).  The rank's partial Y_r = X_r W_r^T is computed in 128 x 128
-// output tiles on the 5th-generation tensor cores: a TMA warp streams 128 x 64
-// slices of X and W (128-byte swizzle) through a 4-stage shared-memory ring, one
-// elected thread issues tcgen05.mma (kind::f16, M = N = 128, K = 16) into one of
-// two TMEM accumulators, and four epilogue warps read the finished accumulator
-// (tcgen05.ld), round it to 16 bits (the reference's per-rank F.linear output
-// is rounded the same way), stage it in shared memory and push it -- one
-// contiguous 32 KB tile, 512-byte coalesced stores -- into the symmetric buffer
-// of the tile's owner rank (tile % world) over NVLink peer memory, then publish
-// it with a system-scope release flag.  The MMA of the next tile overlaps the
-// epilogue of this one.
+// output tiles on the 5th-generation tensor cores, stream-K: the K loops of all
+// tiles (tiles x K/64 chunk units) are split evenly over up to one CTA per SM,
+// so a decode-sized problem (a few dozen tiles) still fills all 148 SMs.  A TMA
+// warp streams 128 x 64 slices of X and W (128-byte swizzle) through a 4-stage
+// shared-memory ring, one elected thread issues tcgen05.mma (kind::f16, M = N =
+// 128, K = 16) into one of two TMEM accumulators, and four epilogue warps read
+// the finished accumulator.  A CTA whose range ends inside a tile writes that
+// segment's fp32 sum to its fix-up slot (this GPU's memory) and flags it; the
+// CTA that reaches the tile's last chunk adds its predecessors' fix-up sums in
+// CTA order (it processes that segment last, so no wait can cycle).  The
+// finished tile's epilogue then reads
+// the whole tile's fp32 sum, rounds it to 16 bits once (the reference's
+// per-rank F.linear output is rounded the same way) and stages it in shared
+// memory; one thread then
+// pushes the staged 32 KB tile with a single bulk copy (cp.async.bulk, no
+// multicast) into the symmetric buffer of the tile's owner rank (tile % world)
+// over NVLink peer memory.  The MMA of the next tile overlaps the epilogue of
+// this one.  When its last tile is out, the CTA waits for its copies, issues
+// ONE system-scope fence and sets the owners' flags with relaxed stores (a
+// system-scope fence costs microseconds here, so it is paid once per CTA and
+// phase, not per tile).
 //
-// Phase 2 (owner reduce).  For each tile it owns, a rank waits for the partial
-// flags of every source rank, sums the world partials in fp32 in rank order
-// (plus the bias, once), rounds once, writes its own Y rows and pushes the
-// reduced tile into every peer's result slot, again followed by a release flag.
+// Phase 2 (owner reduce), in 32-row quarter tiles spread over all CTAs.  For
+// each quarter it owns, a rank waits for the partial flags of every source
+// rank, loads the world partial slices at once (world x 3 16-byte loads in
+// flight per thread), sums them in fp32 in rank order (plus the bias, once),
+// rounds once, writes its own Y rows, stages the quarter and bulk-copies the
+// 8 KB into every peer's result slot; the CTA's flags follow one fence, as in
+// phase 1.
 //
-// Phase 3.  Every rank copies the reduced tiles it does not own from its own
+// Phase 3.  Every rank copies the reduced quarters it does not own from its own
 // result slots (written by their owners) into Y.
 //
 // Two shots (reduce-scatter then all-gather) move 2 (world - 1) / world of Y
@@ -28,6 +42,9 @@
 // with the first shot overlapping the GEMM tile by tile.  Every rank ends with
 // bit-identical Y.  All loads are from this GPU's own memory (X, W, its
 // symmetric buffer); only stores cross NVLink.  No TMA multicast is used.
+//
+// The world size is a template parameter (1, 2, 4 or 8: the TP sizes of the
+// 8-KV-head model), so the per-source loops unroll into independent loads.
 //
 // Flags carry a per-call epoch (a device counter advanced by the last CTA of
 // each call), so nothing is reset between calls and the call is CUDA-graph
@@ -55,9 +72,16 @@ constexpr uint32_t kSlice = kBM * kBK * 2;         // 16 KB: 128 rows x 64 eleme
 constexpr uint32_t kStageBytes = 2 * kSlice;       // X slice + W slice
 constexpr uint32_t kTileBytes = kBM * kBN * 2;     // 32 KB output tile
 constexpr int kChunks = kTileBytes / 16;           // 16-byte chunks per tile
+constexpr int kQuarters = 4;                       // exchange unit: 32 rows of a tile
+constexpr int kQRows = kBM / kQuarters;
+constexpr uint32_t kQBytes = kTileBytes / kQuarters;
+constexpr int kQChunks = kChunks / kQuarters;      // 512
 constexpr int kThreads = 192;                      // warps 0-3 epilogue, 4 TMA, 5 MMA
 constexpr int kEpiThreads = 128;
 constexpr int kMaxRanks = 8;
+constexpr int kMaxCtas = 160;                      // >= SMs per GPU (fix-up slots)
+constexpr int kMinChunks = 4;                      // K chunks per CTA at least
+constexpr uint32_t kFixBytes = kBM * kBN * 4;      // fp32 fix-up slot of one CTA
 constexpr uint32_t kTmemCols = 256;                // two 128-column accumulators
 constexpr uint32_t kOffStaging = kStages * kStageBytes;
 constexpr uint32_t kOffBars = kOffStaging + kTileBytes;
@@ -73,20 +97,16 @@ struct Params {
   int tokens, n, k;
   int m_tiles, n_tiles, tiles, k_chunks;
   int world, rank_base, ctas_per_rank;
+  int gemm_ctas;                       // CTAs 0 .. gemm_ctas - 1 of a rank run phase 1
   int owned_max;                       // partial slots per source rank
   int64_t y_stride;                    // elements
   void *y[kMaxRanks];                  // per local rank
   const void *bias[kMaxRanks];         // per local rank, [N] or null
   uint8_t *buf[kMaxRanks];             // every rank's symmetric buffer, mapped here
-  int64_t off_result, off_pflag, off_rflag;
+  int64_t off_partial, off_result, off_pflag, off_rflag, off_fix, off_fixflag;
   uint32_t *state;                     // [2]: completed calls, CTAs done in this call
   uint32_t *err;
 };
-
-__device__ __forceinline__ void st_release_sys(uint32_t *f, uint32_t v) {
-  asm volatile("fence.acq_rel.sys;\n\tst.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(v)
-               : "memory");
-}
 
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *f) {
   uint32_t v;
@@ -129,6 +149,97 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map
       : "memory");
 }
 
+// Bulk copy of `bytes` from this CTA's shared memory to global memory (here: a
+// peer's symmetric buffer), tracked by the issuing thread's bulk group.
+__device__ __forceinline__ void bulk_store(void *dst, uint32_t src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst),
+               "r"(src), "r"(bytes)
+               : "memory");
+}
+// Close the current bulk group and wait until its shared-memory source has
+// been read (the staging buffer may then be refilled; the writes may still be
+// in flight).
+__device__ __forceinline__ void bulk_commit_wait_read() {
+  asm volatile(
+      "cp.async.bulk.commit_group;\n\t"
+      "cp.async.bulk.wait_group.read 0;" ::
+          : "memory");
+}
+// Wait until every bulk copy this thread issued has completed (its writes are
+// performed), order them before this thread's later generic accesses, and
+// issue one system-scope fence: relaxed flag stores after it publish every
+// copy before it.  A system-scope fence costs microseconds on B200 across
+// NVLink, so each CTA pays it once per phase rather than once per tile.
+__device__ __forceinline__ void bulk_publish_fence() {
+  asm volatile(
+      "cp.async.bulk.wait_group 0;\n\t"
+      "fence.proxy.async;\n\t"
+      "fence.acq_rel.sys;" ::
+          : "memory");
+}
+
+__device__ __forceinline__ void st_relaxed_sys(uint32_t *f, uint32_t v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(f), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t *f) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_gpu(uint32_t *f, uint32_t v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(f), "r"(v) : "memory");
+}
+__device__ __forceinline__ bool wait_flag_gpu(const uint32_t *f, uint32_t epoch) {
+  if (static_cast<int32_t>(ld_acquire_gpu(f) - epoch) >= 0) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  while (true) {
+    __nanosleep(64);
+    if (static_cast<int32_t>(ld_acquire_gpu(f) - epoch) >= 0) return true;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+  }
+}
+
+// One CTA's stream-K range [beg, end) of chunk units (unit = tile * kc + k
+// chunk), cut into per-tile segments.  Segment j of the natural order covers
+// tile t0 + j; when the first one continues a tile begun by earlier CTAs (it
+// then also finishes it, as the range goes on), it is processed last.
+struct Seg {
+  int tile, kc0, kc1;
+};
+struct Sched {
+  int64_t beg, end;
+  int kc, n, t0;
+  bool defer;
+  __device__ __forceinline__ Seg get(int i) const {
+    const int j = defer ? (i + 1 == n ? 0 : i + 1) : i;
+    Seg s;
+    s.tile = t0 + j;
+    s.kc0 = j == 0 ? static_cast<int>(beg - static_cast<int64_t>(t0) * kc) : 0;
+    s.kc1 = j == n - 1 ? static_cast<int>(end - static_cast<int64_t>(t0 + n - 1) * kc) : kc;
+    return s;
+  }
+};
+__device__ __forceinline__ int64_t unit_begin(int cta, int ctas, int64_t units) {
+  return static_cast<int64_t>(cta) * units / ctas;
+}
+__device__ __forceinline__ Sched make_sched(int cta, int ctas, int64_t units, int kc) {
+  Sched s;
+  s.beg = unit_begin(cta, ctas, units);
+  s.end = cta < ctas ? unit_begin(cta + 1, ctas, units) : s.beg;   // CTAs past `ctas`: none
+  s.kc = kc;
+  if (s.end <= s.beg) {
+    s.n = 0;
+    s.t0 = 0;
+    s.defer = false;
+    return s;
+  }
+  s.t0 = static_cast<int>(s.beg / kc);
+  s.n = static_cast<int>((s.end - 1) / kc) - s.t0 + 1;
+  s.defer = s.n > 1 && s.beg > static_cast<int64_t>(s.t0) * kc;
+  return s;
+}
+
 template <typename T>
 __device__ __forceinline__ uint32_t pack2(float a, float b);
 template <>
@@ -163,7 +274,7 @@ __device__ __forceinline__ void store_y_chunk(const Params &p, void *y, int m, i
   *reinterpret_cast<uint4 *>(dst) = v;
 }
 
-template <typename T>
+template <typename T, int W>
 __global__ void __launch_bounds__(kThreads, 1)
     row_parallel_kernel(const __grid_constant__ Params p, const __grid_constant__ Maps maps) {
   extern __shared__ uint8_t smem_raw[];
@@ -180,7 +291,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int lr = blockIdx.x / p.ctas_per_rank;  // local (virtual) rank of this CTA
   const int cta = blockIdx.x - lr * p.ctas_per_rank;
   const int rank = p.rank_base + lr;
-  const int world = p.world;
+  constexpr int world = W;
+  // two ranks: one shot (each rank pushes its partial to both and reduces every
+  // tile itself, same NVLink volume as two shots and one flag round less)
+  constexpr bool kOneShot = W == 2;
   const uint32_t epoch = *reinterpret_cast<volatile uint32_t *>(p.state) + 1u;
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
   constexpr uint32_t kIdesc = tc::idesc_f16(kBf16, false, kBM, kBN);
@@ -210,16 +324,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     *abort_flag = 1;
   };
 
-  // ---------------- phase 1: GEMM tiles -> owner partial slots ----------------
+  // ---------------- phase 1: stream-K GEMM -> owner partial slots ----------------
+  const Sched sched = make_sched(cta < p.gemm_ctas ? cta : p.gemm_ctas, p.gemm_ctas,
+                                 static_cast<int64_t>(p.tiles) * p.k_chunks, p.k_chunks);
   if (warp == 4) {
     if (lane == 0) {  // TMA producer
       prefetch_tensormap(&maps.x[lr]);
       prefetch_tensormap(&maps.w[lr]);
       int s = 0;
       uint32_t ph = 0;
-      for (int tile = cta; tile < p.tiles && !*abort_flag; tile += p.ctas_per_rank) {
-        const int m = tile / p.n_tiles, nt = tile - (tile / p.n_tiles) * p.n_tiles;
-        for (int kc = 0; kc < p.k_chunks; ++kc) {
+      for (int i = 0; i < sched.n && !*abort_flag; ++i) {
+        const Seg sg = sched.get(i);
+        const int m = sg.tile / p.n_tiles, nt = sg.tile - m * p.n_tiles;
+        for (int kc = sg.kc0; kc < sg.kc1; ++kc) {
           if (!mbar_wait(bar(kEmpty + s), ph ^ 1)) { fail(); break; }
           const uint32_t dst = base + s * kStageBytes;
           mbar_arrive_expect_tx(bar(kFull + s), kStageBytes);
@@ -234,21 +351,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {  // MMA issuer
       int s = 0;
       uint32_t ph = 0;
-      int it = 0;
-      for (int tile = cta; tile < p.tiles && !*abort_flag; tile += p.ctas_per_rank, ++it) {
+      for (int it = 0; it < sched.n && !*abort_flag; ++it) {
+        const Seg sg = sched.get(it);
         const int acc = it & 1;
         if (!mbar_wait(bar(kAccEmpty + acc), ((it >> 1) & 1) ^ 1)) { fail(); break; }
         tc::fence_after_sync();
         const uint32_t d = tmem + acc * kBN;
         bool ok = true;
-        for (int kc = 0; kc < p.k_chunks; ++kc) {
+        for (int kc = sg.kc0; kc < sg.kc1; ++kc) {
           if (!mbar_wait(bar(kFull + s), ph)) { fail(); ok = false; break; }
           tc::fence_after_sync();
           const uint32_t a = base + s * kStageBytes, b = a + kSlice;
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk)
             tc::mma_f16_ss(d, tc::smem_desc_sw128(a + kk * 32, 16, 1024),
-                           tc::smem_desc_sw128(b + kk * 32, 16, 1024), kIdesc, kc | kk);
+                           tc::smem_desc_sw128(b + kk * 32, 16, 1024), kIdesc,
+                           (kc - sg.kc0) | kk);
           tc::commit(bar(kEmpty + s));
           if (++s == kStages) { s = 0; ph ^= 1; }
         }
@@ -260,34 +378,90 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {  // epilogue warps 0-3: row 32 * warp + lane of the tile
     const int row = warp * 32 + lane;
     uint8_t *stage = smem + kOffStaging;
-    int it = 0;
-    for (int tile = cta; tile < p.tiles; tile += p.ctas_per_rank, ++it) {
+    uint8_t *fix_base = p.buf[rank] + p.off_fix;
+    uint32_t *fix_flags = reinterpret_cast<uint32_t *>(p.buf[rank] + p.off_fixflag);
+    int pushed = 0;
+    for (int it = 0; it < sched.n; ++it) {
+      const Seg sg = sched.get(it);
       const int acc = it & 1;
+      const bool contrib = sg.kc1 < p.k_chunks;          // the tile goes on in the next CTA
+      const bool finish = !contrib && sg.kc0 > 0;         // predecessors hold its first chunks
       // all 128 threads take the same branch (epi_any), so none is left at bar 1
       if (epi_any(*abort_flag != 0)) break;
       if (epi_any(!mbar_wait(bar(kAccFull + acc), (it >> 1) & 1))) { fail(); break; }
+      // predecessors: CTAs first_pred .. cta - 1 (ascending), first_pred being the
+      // CTA whose range holds the tile's first chunk (unit_begin(0) = 0 ends the scan)
+      int first_pred = cta;
+      if (finish) {
+        const int64_t tile_beg = static_cast<int64_t>(sg.tile) * p.k_chunks;
+        const int64_t units = static_cast<int64_t>(p.tiles) * p.k_chunks;
+        first_pred = cta - 1;
+        while (unit_begin(first_pred, p.gemm_ctas, units) > tile_beg) --first_pred;
+        bool bad = false;
+        if (tid == 0)
+          for (int c = first_pred; c < cta; ++c)
+            if (!wait_flag_gpu(fix_flags + c, epoch)) { bad = true; break; }
+        if (epi_any(bad)) { fail(); break; }
+      }
       tc::fence_after_sync();
-#pragma unroll
+      float *my_fix = reinterpret_cast<float *>(fix_base + static_cast<int64_t>(cta) * kFixBytes) +
+                      row * kBN;
+#pragma unroll 1
       for (int q = 0; q < 4; ++q) {  // 32 columns at a time
         uint32_t r[32];
         tc::ld32(tmem + (static_cast<uint32_t>(warp * 32) << 16) + acc * kBN + q * 32, r);
         tc::wait_ld();
+        if (contrib) {
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            reinterpret_cast<float4 *>(my_fix + q * 32)[c] =
+                make_float4(__uint_as_float(r[4 * c]), __uint_as_float(r[4 * c + 1]),
+                            __uint_as_float(r[4 * c + 2]), __uint_as_float(r[4 * c + 3]));
+          continue;
+        }
+        float v[32];
+#pragma unroll
+        for (int c = 0; c < 32; ++c) v[c] = __uint_as_float(r[c]);
+        if (finish) {
+          for (int c = first_pred; c < cta; ++c) {
+            const float4 *src = reinterpret_cast<const float4 *>(
+                reinterpret_cast<const float *>(fix_base + static_cast<int64_t>(c) * kFixBytes) +
+                row * kBN + q * 32);
+            float4 f[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) f[j] = __ldcg(src + j);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              v[4 * j] += f[j].x;
+              v[4 * j + 1] += f[j].y;
+              v[4 * j + 2] += f[j].z;
+              v[4 * j + 3] += f[j].w;
+            }
+          }
+        }
 #pragma unroll
         for (int c = 0; c < 4; ++c) {  // four 16-byte chunks of 8 columns
           const int chunk = q * 4 + c;
-          uint4 v;
-          v.x = pack2<T>(__uint_as_float(r[8 * c + 0]), __uint_as_float(r[8 * c + 1]));
-          v.y = pack2<T>(__uint_as_float(r[8 * c + 2]), __uint_as_float(r[8 * c + 3]));
-          v.z = pack2<T>(__uint_as_float(r[8 * c + 4]), __uint_as_float(r[8 * c + 5]));
-          v.w = pack2<T>(__uint_as_float(r[8 * c + 6]), __uint_as_float(r[8 * c + 7]));
-          *reinterpret_cast<uint4 *>(stage + row * 256 + ((chunk ^ (row & 7)) << 4)) = v;
+          uint4 o;
+          o.x = pack2<T>(v[8 * c + 0], v[8 * c + 1]);
+          o.y = pack2<T>(v[8 * c + 2], v[8 * c + 3]);
+          o.z = pack2<T>(v[8 * c + 4], v[8 * c + 5]);
+          o.w = pack2<T>(v[8 * c + 6], v[8 * c + 7]);
+          *reinterpret_cast<uint4 *>(stage + row * 256 + ((chunk ^ (row & 7)) << 4)) = o;
         }
       }
       tc::fence_before_sync();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar(kAccEmpty + acc));  // accumulator free for tile it + 2
+      if (lane == 0) mbar_arrive(bar(kAccEmpty + acc));  // accumulator free for segment it + 2
       asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
-      const int m = tile / p.n_tiles, nt = tile - (tile / p.n_tiles) * p.n_tiles;
+      if (contrib) {  // publish the fp32 segment sum to the finishing CTA (same GPU)
+        if (tid == 0) {
+          __threadfence();
+          st_release_gpu(fix_flags + cta, epoch);
+        }
+        continue;
+      }
+      const int m = sg.tile / p.n_tiles, nt = sg.tile - m * p.n_tiles;
       if (world == 1) {
         for (int c = tid; c < kChunks; c += kEpiThreads) {
           const int rr = c >> 4;
@@ -295,49 +469,98 @@ __global__ void __launch_bounds__(kThreads, 1)
                                                             (((c & 15) ^ (rr & 7)) << 4));
           store_y_chunk(p, p.y[lr], m, nt, c, v);
         }
-      } else {
-        const int owner = tile % world, slot = tile / world;
-        uint8_t *dst = p.buf[owner] +
-                       (static_cast<int64_t>(rank) * p.owned_max + slot) * kTileBytes;
-        for (int c = tid; c < kChunks; c += kEpiThreads) {
-          const int rr = c >> 4;
-          const uint4 v = *reinterpret_cast<const uint4 *>(stage + rr * 256 +
-                                                            (((c & 15) ^ (rr & 7)) << 4));
-          reinterpret_cast<uint4 *>(dst)[c] = v;
+      } else if (tid == 0) {
+        // the staged tile (kept in its swizzled layout, which the owner reads
+        // back) goes to the owner's partial slot [rank][tile / world] in one copy
+        // (one shot: to slot [rank][tile] of every rank)
+        fence_proxy_async_smem();
+        if (kOneShot) {
+#pragma unroll
+          for (int d = 0; d < W; ++d)
+            bulk_store(p.buf[d] + p.off_partial +
+                           (static_cast<int64_t>(rank) * p.owned_max + sg.tile) * kTileBytes,
+                       smem_u32(stage), kTileBytes);
+        } else {
+          const int owner = sg.tile % world, slot = sg.tile / world;
+          bulk_store(p.buf[owner] + p.off_partial +
+                         (static_cast<int64_t>(rank) * p.owned_max + slot) * kTileBytes,
+                     smem_u32(stage), kTileBytes);
         }
+        bulk_commit_wait_read();
       }
+      ++pushed;
       asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
-      if (world > 1 && tid == 0) {
-        const int owner = tile % world, slot = tile / world;
-        uint32_t *flags = reinterpret_cast<uint32_t *>(p.buf[owner] + p.off_pflag);
-        st_release_sys(flags + static_cast<int64_t>(rank) * p.owned_max + slot, epoch);
+    }
+    if (world > 1 && tid == 0 && pushed > 0) {  // publish this CTA's partial tiles
+      bulk_publish_fence();
+      int k = 0;
+      for (int it = 0; it < sched.n && k < pushed; ++it) {
+        const Seg sg = sched.get(it);
+        if (sg.kc1 < p.k_chunks) continue;
+        ++k;
+        if (kOneShot) {
+#pragma unroll
+          for (int d = 0; d < W; ++d)
+            st_relaxed_sys(reinterpret_cast<uint32_t *>(p.buf[d] + p.off_pflag) +
+                               static_cast<int64_t>(rank) * p.owned_max + sg.tile,
+                           epoch);
+        } else {
+          const int owner = sg.tile % world, slot = sg.tile / world;
+          st_relaxed_sys(reinterpret_cast<uint32_t *>(p.buf[owner] + p.off_pflag) +
+                             static_cast<int64_t>(rank) * p.owned_max + slot,
+                         epoch);
+        }
       }
     }
   }
   __syncthreads();
 
-  // ---------------- phase 2: reduce the tiles this rank owns ----------------
+  // ---------------- phase 2: reduce the quarters this rank owns ----------------
   // (abort_flag is stable here: every writer has passed the barrier above, and
   // below it only changes before a __syncthreads_or that all threads read)
   if (world > 1 && !*abort_flag) {
     const T *bias = static_cast<const T *>(p.bias[lr]);
     uint8_t *own = p.buf[rank];
+    uint8_t *stage = smem + kOffStaging;
     const uint32_t *pflags = reinterpret_cast<const uint32_t *>(own + p.off_pflag);
-    for (int slot = cta;; slot += p.ctas_per_rank) {
-      const int tile = slot * world + rank;
+    int done = 0;
+    for (int u = cta;; u += p.ctas_per_rank) {
+      const int slot = u / kQuarters, q = u - slot * kQuarters;
+      const int tile = kOneShot ? slot : slot * world + rank;
       if (tile >= p.tiles) break;
+      const int m = tile / p.n_tiles, nt = tile - (tile / p.n_tiles) * p.n_tiles;
+      if (m * kBM + q * kQRows >= p.tokens) continue;   // all padding rows: nobody waits
       const bool bad =
           tid < world && !wait_flag(pflags + static_cast<int64_t>(tid) * p.owned_max + slot, epoch);
       if (__syncthreads_or(bad)) {
         if (tid == 0) fail();
         break;
       }
-      const int m = tile / p.n_tiles, nt = tile - (tile / p.n_tiles) * p.n_tiles;
-      for (int c = tid; c < kChunks; c += kThreads) {
+      // chunk cl (0..511) of the quarter: row q * 32 + cl / 16, 16-byte column cl % 16
+      constexpr int kPer = (kQChunks + kThreads - 1) / kThreads;   // 3
+      uint4 v[kPer][W];
+#pragma unroll
+      for (int b = 0; b < kPer; ++b) {
+        const int cl = tid + b * kThreads;
+        if (cl < kQChunks) {
+          const int row = q * kQRows + (cl >> 4), cc = cl & 15;
+          const int64_t off = row * 256 + ((cc ^ (row & 7)) << 4);
+#pragma unroll
+          for (int src = 0; src < W; ++src)
+            v[b][src] = __ldcg(reinterpret_cast<const uint4 *>(
+                own + p.off_partial + (static_cast<int64_t>(src) * p.owned_max + slot) * kTileBytes +
+                off));
+        }
+      }
+#pragma unroll
+      for (int b = 0; b < kPer; ++b) {
+        const int cl = tid + b * kThreads;
+        if (cl >= kQChunks) continue;
+        const int row = q * kQRows + (cl >> 4), cc = cl & 15;
         float acc[8];
         if (bias != nullptr) {
-          const uint4 b = __ldg(reinterpret_cast<const uint4 *>(bias + nt * kBN + (c & 15) * 8));
-          const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
+          const uint4 bv = __ldg(reinterpret_cast<const uint4 *>(bias + nt * kBN + cc * 8));
+          const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             const float2 f = unpack2<T>(bw[j]);
@@ -348,12 +571,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int j = 0; j < 8; ++j) acc[j] = 0.f;
         }
-        for (int src = 0; src < world; ++src) {
-          const uint4 v = __ldcg(reinterpret_cast<const uint4 *>(
-                                     own + (static_cast<int64_t>(src) * p.owned_max + slot) *
-                                               kTileBytes) +
-                                 c);
-          const uint32_t vw[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int src = 0; src < W; ++src) {
+          const uint32_t vw[4] = {v[b][src].x, v[b][src].y, v[b][src].z, v[b][src].w};
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             const float2 f = unpack2<T>(vw[j]);
@@ -366,40 +586,75 @@ __global__ void __launch_bounds__(kThreads, 1)
         o.y = pack2<T>(acc[2], acc[3]);
         o.z = pack2<T>(acc[4], acc[5]);
         o.w = pack2<T>(acc[6], acc[7]);
-        store_y_chunk(p, p.y[lr], m, nt, c, o);
-        for (int q = 1; q < world; ++q) {
-          const int peer = (rank + q) % world;
-          reinterpret_cast<uint4 *>(p.buf[peer] + p.off_result +
-                                    static_cast<int64_t>(tile) * kTileBytes)[c] = o;
-        }
+        store_y_chunk(p, p.y[lr], m, nt, row * 16 + cc, o);
+        if (!kOneShot) reinterpret_cast<uint4 *>(stage)[cl] = o;     // quarter, row-major
       }
+      if (kOneShot) continue;      // every rank reduced this quarter itself
       __syncthreads();
-      if (tid > 0 && tid < world) {
-        const int peer = (rank + tid) % world;
-        st_release_sys(reinterpret_cast<uint32_t *>(p.buf[peer] + p.off_rflag) + tile, epoch);
+      if (tid == 0) {
+        fence_proxy_async_smem();
+#pragma unroll
+        for (int k = 1; k < W; ++k) {
+          const int peer = (rank + k) % world;
+          bulk_store(p.buf[peer] + p.off_result + static_cast<int64_t>(tile) * kTileBytes +
+                         q * kQBytes,
+                     smem_u32(stage), kQBytes);
+        }
+        bulk_commit_wait_read();
+      }
+      ++done;
+      __syncthreads();   // the staging quarter is free again
+    }
+    if (!kOneShot && tid == 0 && done > 0) {  // publish this CTA's reduced quarters
+      bulk_publish_fence();
+      int k = 0;
+      for (int u = cta; k < done; u += p.ctas_per_rank) {
+        const int slot = u / kQuarters, q = u - slot * kQuarters;
+        const int tile = slot * world + rank;
+        const int m = tile / p.n_tiles;
+        if (m * kBM + q * kQRows >= p.tokens) continue;
+        ++k;
+#pragma unroll
+        for (int j = 1; j < W; ++j) {
+          const int peer = (rank + j) % world;
+          st_relaxed_sys(reinterpret_cast<uint32_t *>(p.buf[peer] + p.off_rflag) +
+                             tile * kQuarters + q,
+                         epoch);
+        }
       }
     }
   }
   __syncthreads();
-  if (world > 1 && !*abort_flag) {
-    // ---------------- phase 3: copy the tiles owned by peers ----------------
+  if (world > 1 && !kOneShot && !*abort_flag) {
+    // ---------------- phase 3: copy the quarters owned by peers ----------------
     const uint8_t *results = p.buf[rank] + p.off_result;
     const uint32_t *rflags = reinterpret_cast<const uint32_t *>(p.buf[rank] + p.off_rflag);
     for (int i = cta;; i += p.ctas_per_rank) {
-      const int blk = i / (world - 1), r = i - blk * (world - 1);
+      const int nb = i / kQuarters, q = i - nb * kQuarters;
+      constexpr int kPeers = W > 1 ? W - 1 : 1;      // (phase 3 only runs for W > 1)
+      const int blk = nb / kPeers, r = nb - blk * kPeers;
       const int tile = blk * world + r + (r >= rank ? 1 : 0);
       if (blk * world >= p.tiles) break;
       if (tile >= p.tiles) continue;
-      if (__syncthreads_or(tid == 0 && !wait_flag(rflags + tile, epoch))) {
+      const int m = tile / p.n_tiles, nt = tile - (tile / p.n_tiles) * p.n_tiles;
+      if (m * kBM + q * kQRows >= p.tokens) continue;
+      if (__syncthreads_or(tid == 0 && !wait_flag(rflags + tile * kQuarters + q, epoch))) {
         if (tid == 0) fail();
         break;
       }
-      const int m = tile / p.n_tiles, nt = tile - (tile / p.n_tiles) * p.n_tiles;
-      for (int c = tid; c < kChunks; c += kThreads) {
-        const uint4 v = __ldcg(
-            reinterpret_cast<const uint4 *>(results + static_cast<int64_t>(tile) * kTileBytes) +
-            c);
-        store_y_chunk(p, p.y[lr], m, nt, c, v);
+      constexpr int kPer = (kQChunks + kThreads - 1) / kThreads;
+      uint4 v[kPer];
+      const uint4 *src = reinterpret_cast<const uint4 *>(
+          results + static_cast<int64_t>(tile) * kTileBytes + q * kQBytes);
+#pragma unroll
+      for (int b = 0; b < kPer; ++b) {
+        const int cl = tid + b * kThreads;
+        if (cl < kQChunks) v[b] = __ldcg(src + cl);
+      }
+#pragma unroll
+      for (int b = 0; b < kPer; ++b) {
+        const int cl = tid + b * kThreads;
+        if (cl < kQChunks) store_y_chunk(p, p.y[lr], m, nt, q * kQChunks + cl, v[b]);
       }
     }
   }
@@ -422,20 +677,32 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ---- host side -------------------------------------------------------------
 
 struct Layout {
-  int64_t tiles_max, owned_max, off_result, off_pflag, off_rflag, total;
+  int64_t tiles_max, owned_max, off_fix, off_fixflag, off_partial, off_result, off_pflag,
+      off_rflag, total;
 };
 
 inline int64_t align_up(int64_t v, int64_t a) { return (v + a - 1) / a * a; }
 
+// One rank's buffer: stream-K fix-up slots and flags (used by this GPU only),
+// then, for world > 1, the partial slots [source rank][tile / world], the
+// result slots [tile] and their flags (written by peers).
 Layout layout(int max_tokens, int n_features, int world) {
   Layout l;
   l.tiles_max = static_cast<int64_t>((max_tokens + kBM - 1) / kBM) * (n_features / kBN);
-  l.owned_max = (l.tiles_max + world - 1) / world;
-  const int64_t partial = static_cast<int64_t>(world) * l.owned_max * kTileBytes;
-  l.off_result = align_up(partial, 4096);
-  l.off_pflag = align_up(l.off_result + l.tiles_max * kTileBytes, 4096);
-  l.off_rflag = align_up(l.off_pflag + static_cast<int64_t>(world) * l.owned_max * 4, 256);
-  l.total = align_up(l.off_rflag + l.tiles_max * 4, 4096);
+  // (two ranks exchange one shot: every rank holds a slot for every tile)
+  l.owned_max = world == 2 ? l.tiles_max : (l.tiles_max + world - 1) / world;
+  l.off_fix = 0;
+  l.off_fixflag = static_cast<int64_t>(kMaxCtas) * kFixBytes;
+  const int64_t x = align_up(l.off_fixflag + kMaxCtas * 4, 4096);
+  const bool ex = world > 1;
+  const int64_t partial = ex ? static_cast<int64_t>(world) * l.owned_max * kTileBytes : 0;
+  l.off_result = x + align_up(partial, 4096);
+  l.off_pflag = align_up(l.off_result + (ex ? l.tiles_max * kTileBytes : 0), 4096);
+  l.off_rflag = align_up(l.off_pflag + (ex ? static_cast<int64_t>(world) * l.owned_max * 4 : 0),
+                         256);
+  l.total = align_up(l.off_rflag + (ex ? l.tiles_max * kQuarters * 4 : 0), 4096);
+  // the partial slots start at the first exchange offset
+  l.off_partial = x;
   return l;
 }
 
@@ -475,13 +742,13 @@ int sm_count() {
   return n > 0 ? n : 148;
 }
 
-template <typename T>
+template <typename T, int W>
 int launch(const Params &p, const Maps &maps, int local_ranks, cudaStream_t stream) {
   static std::once_flag once;
   static bool ok = false;
   std::call_once(once, [] {
-    ok = cudaFuncSetAttribute(row_parallel_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              kSmemBytes) == cudaSuccess;
+    ok = cudaFuncSetAttribute(row_parallel_kernel<T, W>,
+                              cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) == cudaSuccess;
   });
   if (!ok) return SLOKV_ERR_CUDA;
   cudaLaunchConfig_t cfg = {};
@@ -494,8 +761,20 @@ int launch(const Params &p, const Maps &maps, int local_ranks, cudaStream_t stre
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, row_parallel_kernel<T>, p, maps) == cudaSuccess ? SLOKV_OK
-                                                                                  : SLOKV_ERR_CUDA;
+  return cudaLaunchKernelEx(&cfg, row_parallel_kernel<T, W>, p, maps) == cudaSuccess
+             ? SLOKV_OK
+             : SLOKV_ERR_CUDA;
+}
+
+template <typename T>
+int launch_world(const Params &p, const Maps &maps, int local_ranks, cudaStream_t stream) {
+  switch (p.world) {
+    case 1: return launch<T, 1>(p, maps, local_ranks, stream);
+    case 2: return launch<T, 2>(p, maps, local_ranks, stream);
+    case 4: return launch<T, 4>(p, maps, local_ranks, stream);
+    case 8: return launch<T, 8>(p, maps, local_ranks, stream);
+    default: return SLOKV_ERR_UNSUPPORTED;
+  }
 }
 
 }  // namespace rp
@@ -523,9 +802,10 @@ extern "C" int slokv_row_parallel_linear(
       n_features <= 0 || k_features <= 0)
     return SLOKV_ERR_INVALID_ARG;
   if (n_features % kBN != 0 || k_features % kBK != 0) return SLOKV_ERR_UNSUPPORTED;
+  if (world != 1 && world != 2 && world != 4 && world != 8) return SLOKV_ERR_UNSUPPORTED;
   if (dtype != SLOKV_DTYPE_BF16 && dtype != SLOKV_DTYPE_F16) return SLOKV_ERR_UNSUPPORTED;
   if (tokens == 0) return SLOKV_OK;
-  if (!x || !w || !y || !state || (world > 1 && !rank_buffers)) return SLOKV_ERR_INVALID_ARG;
+  if (!x || !w || !y || !state || !rank_buffers) return SLOKV_ERR_INVALID_ARG;
   if (x_row_stride < k_features || w_row_stride < k_features || y_row_stride < n_features)
     return SLOKV_ERR_INVALID_ARG;
   if ((x_row_stride | w_row_stride | y_row_stride) & 7) return SLOKV_ERR_ALIGNMENT;
@@ -545,12 +825,10 @@ extern "C" int slokv_row_parallel_linear(
     p.y[i] = y[i];
     p.bias[i] = bias ? bias[i] : nullptr;
   }
-  if (world > 1) {
-    for (int r = 0; r < world; ++r) {
-      if (!rank_buffers[r] || (reinterpret_cast<uintptr_t>(rank_buffers[r]) & 255))
-        return SLOKV_ERR_INVALID_ARG;
-      p.buf[r] = static_cast<uint8_t *>(rank_buffers[r]);
-    }
+  for (int r = 0; r < world; ++r) {
+    if (!rank_buffers[r] || (reinterpret_cast<uintptr_t>(rank_buffers[r]) & 255))
+      return SLOKV_ERR_INVALID_ARG;
+    p.buf[r] = static_cast<uint8_t *>(rank_buffers[r]);
   }
   const Layout l = layout(max_tokens, n_features, world);
   p.tokens = tokens;
@@ -563,18 +841,35 @@ extern "C" int slokv_row_parallel_linear(
   p.world = world;
   p.rank_base = rank_base;
   p.owned_max = static_cast<int>(l.owned_max);
+  p.off_partial = l.off_partial;
+  p.off_fix = l.off_fix;
+  p.off_fixflag = l.off_fixflag;
   p.off_result = l.off_result;
   p.off_pflag = l.off_pflag;
   p.off_rflag = l.off_rflag;
   p.y_stride = y_row_stride;
   p.state = state;
   p.err = dev_error;
-  const int per_rank = sm_count() / local_ranks;
+  int per_rank = sm_count() / local_ranks;
+  if (per_rank > kMaxCtas) per_rank = kMaxCtas;
   if (per_rank < 1) return SLOKV_ERR_UNSUPPORTED;
-  p.ctas_per_rank = p.tiles < per_rank ? p.tiles : per_rank;
+  // GEMM: one CTA per tile while that keeps at least half the SMs busy (the
+  // GEMM is bound by L2 operand traffic, which splitting does not reduce, and
+  // each split adds an fp32 fix-up); stream-K splits of the K loops over all SMs
+  // for long K or few tiles, every CTA getting at least kMinChunks K chunks.
+  // With an exchange every SM gets a CTA: the ones without GEMM work join the
+  // reduce.
+  const int64_t units = static_cast<int64_t>(p.tiles) * p.k_chunks;
+  if (p.k_chunks >= 128 || 2 * p.tiles < per_rank) {
+    const int64_t by_work = (units + kMinChunks - 1) / kMinChunks;
+    p.gemm_ctas = static_cast<int>(by_work < per_rank ? by_work : per_rank);
+  } else {
+    p.gemm_ctas = p.tiles < per_rank ? p.tiles : per_rank;
+  }
+  p.ctas_per_rank = world > 1 ? per_rank : p.gemm_ctas;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  return dtype == SLOKV_DTYPE_BF16 ? launch<__nv_bfloat16>(p, maps, local_ranks, st)
-                                   : launch<__half>(p, maps, local_ranks, st);
+  return dtype == SLOKV_DTYPE_BF16 ? launch_world<__nv_bfloat16>(p, maps, local_ranks, st)
+                                   : launch_world<__half>(p, maps, local_ranks, st);
 }
 
 // ---- symmetric buffers shared between the ranks' processes (CUDA IPC) --------

@@ -28,7 +28,6 @@ from .._lib import SlokvError, buffers, check, lib, require_cuda, stream_ptr
 
 __all__ = ["RowParallelAllReduce", "RowParallelLinear", "row_parallel_buffer_bytes"]
 
-_MAX_RANKS = 8
 _TILE_N = 128
 _TILE_K = 64
 
@@ -74,25 +73,27 @@ class RowParallelAllReduce:
             self.world, self.rank, self.local_ranks = int(_emulate_world), 0, int(_emulate_world)
         else:
             import torch.distributed as dist
-            self.world = dist.get_world_size(group)
-            self.rank = dist.get_rank(group)
+            if dist.is_available() and dist.is_initialized():
+                self.world = dist.get_world_size(group)
+                self.rank = dist.get_rank(group)
+            else:                      # no process group: one rank, the GEMM alone
+                self.world, self.rank = 1, 0
             self.local_ranks = 1
-        if not 1 <= self.world <= _MAX_RANKS:
-            raise SlokvError(f"world size {self.world} outside 1..{_MAX_RANKS}")
+        if self.world not in (1, 2, 4, 8):
+            raise SlokvError(f"the fused row-parallel linear supports TP sizes 1, 2, 4 and 8, "
+                             f"not {self.world}")
         self.buffer_bytes = row_parallel_buffer_bytes(self.max_tokens, self.n_features, self.world)
         if self.buffer_bytes == 0:
             raise SlokvError("unsupported row-parallel geometry")
         with torch.cuda.device(self.device):
             self.state = torch.zeros(2, dtype=torch.int32, device=self.device)
             self._err = buffers.error_word(self.device)
-            if self.world == 1:
-                self.rank_buffers = [None]
-            elif _emulate_world is not None:
+            if self.world == 1 or _emulate_world is not None:
                 self.rank_buffers = [self._alloc() for _ in range(self.world)]
             else:
                 own = self._alloc()
                 self.rank_buffers = self._exchange(own)
-        self._buf_arr = _ptr_array(self.rank_buffers) if self.world > 1 else None
+        self._buf_arr = _ptr_array(self.rank_buffers)
 
     @classmethod
     def emulated(cls, world: int, max_tokens: int, n_features: int, device):

@@ -96,17 +96,23 @@ def test_row_parallel_argument_checks(pkg):
     assert call(base=1, local=2) == -1               # ranks beyond the group
     assert call(n=2500) == -3 and call(k=1000) == -3  # 128-wide output / 64-deep K tiles
     assert call(dtype=2) == -3                       # 16-bit inputs only
+    assert call(world=3) == -3                       # TP sizes 1, 2, 4, 8
     assert call() == -1                              # null pointers
 
 
 def test_row_parallel_buffer_layout(pkg):
     lib = pkg._lib.lib()
-    # partial slots [world][ceil(tiles / world)] + result slots [tiles] of 32 KB tiles + flags
-    for T, n, world in ((1, 2560, 2), (512, 2560, 4), (8192, 2560, 8), (130, 1024, 3)):
+    # stream-K fix-up slots (160 CTAs x 128 x 128 fp32) + flags, then for world > 1
+    # partial slots [world][ceil(tiles / world)] (two ranks: [2][tiles]) + result
+    # slots [tiles] of 32 KB tiles + their flags
+    fix = 160 * 128 * 128 * 4 + 160 * 4
+    for T, n, world in ((1, 2560, 2), (512, 2560, 4), (8192, 2560, 8), (130, 1024, 1)):
         tiles = -(-T // 128) * (n // 128)
         got = lib.slokv_row_parallel_buffer_bytes(T, n, world)
-        data = (world * -(-tiles // world) + tiles) * 32768
-        assert data < got <= data + 3 * 4096 + 4 * (world * -(-tiles // world) + tiles) + 8192
+        owned = tiles if world == 2 else -(-tiles // world)   # two ranks: one shot
+        data = fix + ((world * owned + tiles) * 32768 if world > 1 else 0)
+        flags = 4 * (world * owned + 4 * tiles) if world > 1 else 0
+        assert data < got <= data + flags + 5 * 4096
         assert got % 4096 == 0
     assert lib.slokv_row_parallel_buffer_bytes(128, 2500, 2) == 0
     assert lib.slokv_row_parallel_buffer_bytes(0, 2560, 2) == 0
