@@ -21,11 +21,11 @@ pytestmark = pytest.mark.gpu
 N = 2560  # Qwen3-4B hidden size: the o_proj / down_proj output width
 
 
-def _case(seed, world, T, K, bias=False):
+def _case(seed, world, T, K, bias=False, dtype=torch.bfloat16):
     g = torch.Generator(device="cuda").manual_seed(seed)
-    xs = [torch.randn(T, K, device="cuda", generator=g).bfloat16() for _ in range(world)]
-    ws = [(torch.randn(N, K, device="cuda", generator=g) * 0.02).bfloat16() for _ in range(world)]
-    b = (torch.randn(N, device="cuda", generator=g) * 0.1).bfloat16() if bias else None
+    xs = [torch.randn(T, K, device="cuda", generator=g).to(dtype) for _ in range(world)]
+    ws = [(torch.randn(N, K, device="cuda", generator=g) * 0.02).to(dtype) for _ in range(world)]
+    b = (torch.randn(N, device="cuda", generator=g) * 0.1).to(dtype) if bias else None
     return xs, ws, b
 
 
@@ -43,7 +43,7 @@ def _check(ys, xs, ws, b):
     ref = sum(F.linear(x, w).float() for x, w in zip(xs, ws))
     if b is not None:
         ref = ref + b.float()
-    d = (ys[0].float() - ref.bfloat16().float()).abs()
+    d = (ys[0].float() - ref.to(ys[0].dtype).float()).abs()
     assert d.max().item() <= 2 ** -6 * max(1.0, ref.abs().max().item())
     assert (d == 0).float().mean().item() >= 0.95
 
@@ -54,6 +54,7 @@ def _check(ys, xs, ws, b):
     (4, 700, 1216, 12),      # down_proj at TP=8 depth, 6 row tiles, ragged
     (8, 130, 512, 13),       # 8 ranks, 2 row tiles
     (2, 1, 1024, 14),        # a single row
+    (4, 64, 8192, 15),       # long K: stream-K split with fp32 fix-ups, two-shot exchange
 ])
 def test_row_parallel_emulated_matches_fp32(pkg, world, T, K, seed):
     xs, ws, _ = _case(seed, world, T, K)
@@ -64,6 +65,19 @@ def test_row_parallel_emulated_matches_fp32(pkg, world, T, K, seed):
         torch.cuda.synchronize()
         assert pkg.read_device_errors() == 0
         _check(ys, xs, ws, None)
+    finally:
+        comm.close()
+
+
+def test_row_parallel_f16(pkg):
+    """16-bit float inputs (the f16 instantiation), two ranks."""
+    xs, ws, b = _case(20, 2, 200, 1024, bias=True, dtype=torch.float16)
+    comm = pkg.RowParallelAllReduce.emulated(2, max_tokens=256, n_features=N, device="cuda")
+    try:
+        ys = comm.emulate(xs, ws, biases=[b, b])
+        torch.cuda.synchronize()
+        assert pkg.read_device_errors() == 0
+        _check(ys, xs, ws, b)
     finally:
         comm.close()
 
