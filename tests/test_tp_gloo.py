@@ -75,3 +75,52 @@ def test_block_bytes_counts_fp8_scales():
         pkg.tp_shard(32, 8, 3, 0)
     with pytest.raises(RuntimeError):
         pkg.plan_num_blocks(10, 10, 0, 0, 1)
+
+
+def _rowpar_worker(rank, world, port, queue):
+    import importlib
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, root)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        pkg = importlib.import_module("slo-aware-llm-serving-engine_b200")
+        full = torch.arange(2560 * 1024, dtype=torch.float32).view(2560, 1024)
+        m = pkg.RowParallelLinear(1024, 2560)           # input dim sharded over the group
+        m.weight.weight_loader(m.weight, full)
+        shards = [torch.empty_like(m.weight.data) for _ in range(world)]
+        dist.all_gather(shards, m.weight.data)
+        reassembled = torch.equal(torch.cat(shards, dim=1), full)
+        try:                                            # no CPU fallback for the fused op
+            m(torch.zeros(3, 1024 // world))
+            cpu_forward = "ran"
+        except pkg.SlokvError:
+            cpu_forward = "raised"
+        # the buffer a rank would share over IPC for this group geometry
+        nbytes = pkg.row_parallel_buffer_bytes(512, 2560, world)
+        queue.put((rank, tuple(m.weight.shape), m.tp_size, reassembled, cpu_forward, nbytes))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_row_parallel_linear_two_ranks_shard_like_the_reference():
+    """RowParallelLinear over a world-2 gloo group: each rank holds columns
+    [r * K/2, (r + 1) * K/2) of the weight (nanovllm/layers/linear.py:141-149),
+    the shards reassemble the full weight, both ranks size the same symmetric
+    buffer, and a CPU forward at TP > 1 raises instead of falling back."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rowpar_worker, args=(r, world, port, queue)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = sorted(queue.get(timeout=240) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, shape, tp, reassembled, cpu_forward, nbytes in results:
+        assert shape == (2560, 512) and tp == 2 and reassembled
+        assert cpu_forward == "raised"
+        assert nbytes == results[0][5] > 0
