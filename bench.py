@@ -155,23 +155,20 @@ def build_gpu_workload(args, rank, n, device):
     g = torch.Generator(device=device).manual_seed(1234 + rank)
     scales = None
     if fp8:
-        # finite E4M3 codes (magnitude codes 0..125, random sign) and per-block
-        # scales as if amax 112 had been seen, so appends rarely re-encode
-        kv = torch.empty(2, args.layers, NB, BS, hkv, D, dtype=torch.uint8, device=device)
-        for i in range(2):
-            for l in range(args.layers):
-                kv[i, l].random_(0, 126, generator=g)
-                kv[i, l].bitwise_or_(torch.randint(0, 2, kv[i, l].shape, dtype=torch.uint8,
-                                                   device=device, generator=g) << 7)
-        scales = torch.full((2, args.layers, NB, hkv), 0.25, dtype=torch.float32, device=device)
+        # N(0, 1) bf16 with 1 % x20 outliers, quantised per
+        # (block, kv head) with scale amax / 448, in the blocks the batch reads
+        kv = torch.zeros(2, args.layers, NB, BS, hkv, D, dtype=torch.uint8, device=device)
+        scales = torch.zeros((2, args.layers, NB, hkv), dtype=torch.float32, device=device)
+        fill_fp8_pool(kv, scales, perm.tolist(), g, 1.0, True)
     else:
         kv = torch.empty(2, args.layers, NB, BS, hkv, D, dtype=torch.bfloat16, device=device)
         for i in range(2):
             for l in range(args.layers):
                 kv[i, l].normal_(0.0, 0.5, generator=g)
     q = torch.randn(args.layers, B, hq, D, device=device, generator=g).to(torch.bfloat16)
-    knew = torch.randn(args.layers, B, hkv, D, device=device, generator=g) * 0.5
-    vnew = torch.randn(args.layers, B, hkv, D, device=device, generator=g) * 0.5
+    std = 1.0 if fp8 else 0.5        # config 4: N(0, 1) (+ outliers); config 2: 0.5 N(0, 1)
+    knew = torch.randn(args.layers, B, hkv, D, device=device, generator=g) * std
+    vnew = torch.randn(args.layers, B, hkv, D, device=device, generator=g) * std
     if fp8:  # 1% outliers x20
         knew = torch.where(torch.rand(knew.shape, device=device, generator=g) < 0.01, knew * 20, knew)
         vnew = torch.where(torch.rand(vnew.shape, device=device, generator=g) < 0.01, vnew * 20, vnew)
@@ -181,6 +178,31 @@ def build_gpu_workload(args, rank, n, device):
                 slots_cpu=slots, lens=lens.to(device), tables=tables.to(device),
                 slots=slots.to(device), kv=kv, q=q, knew=knew, vnew=vnew, out=out,
                 block_bytes=block_bytes, fp8=fp8, scales=scales)
+
+
+def fill_fp8_pool(kv, scales, blocks, gen, std, outliers):
+    """FP8 pool contents as BASELINE config 4 specifies them: per layer plane,
+    bf16 values N(0, std^2) (1 % of elements x20 when `outliers`) for the blocks
+    the batch reads, stored as E4M3 codes with per-(block, kv-head) scale
+    amax / 448 (round to nearest, saturating; unused blocks keep zeros)."""
+    ids = torch.as_tensor(sorted(set(int(b) for b in blocks)), dtype=torch.long,
+                          device=kv.device)
+    n, hkv = ids.numel(), kv.shape[-2]
+    for i in range(kv.shape[0]):
+        for l in range(kv.shape[1]):
+            for c in range(0, n, 1024):                      # bounded temporaries
+                sel = ids[c:c + 1024]
+                x = torch.randn((sel.numel(),) + tuple(kv.shape[3:]), device=kv.device,
+                                generator=gen) * std
+                if outliers:
+                    x = torch.where(torch.rand(x.shape, device=kv.device, generator=gen) < 0.01,
+                                    x * 20, x)
+                x = x.bfloat16().float()
+                s = x.abs().amax(dim=(1, 3)) / 448.0                 # [blocks, hkv]
+                q = (x / s.clamp_min(1e-30)[:, None, :, None]).clamp(-448, 448)
+                kv[i, l, sel] = q.to(torch.float8_e4m3fn).view(torch.uint8)
+                scales[i, l, sel] = s
+                del x, q
 
 
 def decode_bytes(wl):
@@ -374,7 +396,9 @@ def run_ours(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "fp8_e4m3 KV, f16 MMA, bf16 q/out" if wl["fp8"] else "bf16",
-            "data": f"synthetic: K/V ~ 0.5*N(0,1), Q ~ N(0,1), context ~ U[{args.ctx_lo},"
+            "data": ("synthetic: K/V ~ N(0,1) with 1% x20 outliers, quantised per (block, kv head) "
+                     "with scale amax/448" if wl["fp8"] else "synthetic: K/V ~ 0.5*N(0,1)")
+                    + f", Q ~ N(0,1), context ~ U[{args.ctx_lo},"
                     f"{args.ctx_hi}], random block assignment (seeded)",
             "config": {
                 "workload": ("BASELINE config 4: FP8-E4M3 KV decode step, 36 layers of "
@@ -574,7 +598,9 @@ def measured_tensor_peak():
 
 
 def run_mixed(args):
-    """36 layers of forward_mixed over 64 decode rows + 3 prefill chunks."""
+    """36 layers of forward_mixed over 64 decode rows + 3 prefill chunks (with
+    --kv fp8: forward_mixed_fp8 over an FP8-E4M3 pool -- quantising append, FP8
+    decode, and the prefill rows attended through their pages copied to f16)."""
     torch.cuda.set_device(0)
     device = torch.device("cuda", 0)
     pkg = importlib.import_module("slo-aware-llm-serving-engine_b200")
@@ -584,7 +610,8 @@ def run_mixed(args):
     rows = [(int(n) - 1, 1) for n in dec_lens] + [(h, MIXED_CHUNK) for h in MIXED_PREFIX]
     pages = [(h + n + BS - 1) // BS for h, n in rows]
     W = max(pages)
-    block_bytes = 2 * L * BS * HKV * D * 2
+    fp8 = args.kv == "fp8"
+    block_bytes = 2 * L * (BS * HKV * D + HKV * 4) if fp8 else 2 * L * BS * HKV * D * 2
     free, total = torch.cuda.mem_get_info(device)
     NB = args.pool_blocks or min(int(POOL_FRAC * total) // block_bytes,
                                  int((free - (8 << 30)) // block_bytes))
@@ -596,11 +623,17 @@ def run_mixed(args):
     slots = [t[pos // BS] * BS + pos % BS for t, (h, n) in zip(tables, rows)
              for pos in range(h, h + n)]
     T = len(slots)
-    kv = torch.empty(2, L, NB, BS, HKV, D, dtype=torch.bfloat16, device=device)
     g = torch.Generator(device=device).manual_seed(77)
-    for i in range(2):
-        for l in range(L):
-            kv[i, l].normal_(0.0, 0.5, generator=g)
+    sc = None
+    if fp8:  # the bf16 pool's values (0.5 N(0, 1)) quantised per (block, head), amax / 448
+        kv = torch.zeros(2, L, NB, BS, HKV, D, dtype=torch.uint8, device=device)
+        sc = torch.zeros((2, L, NB, HKV), dtype=torch.float32, device=device)
+        fill_fp8_pool(kv, sc, perm, g, 0.5, False)
+    else:
+        kv = torch.empty(2, L, NB, BS, HKV, D, dtype=torch.bfloat16, device=device)
+        for i in range(2):
+            for l in range(L):
+                kv[i, l].normal_(0.0, 0.5, generator=g)
     q = torch.randn(L, T, HQ, D, device=device, generator=g).bfloat16()
     k = (torch.randn(L, T, HKV, D, device=device, generator=g) * 0.5).bfloat16()
     v = (torch.randn(L, T, HKV, D, device=device, generator=g) * 0.5).bfloat16()
@@ -618,15 +651,28 @@ def run_mixed(args):
 
     def step():
         for l in range(L):
-            pkg.forward_mixed(q[l], k[l], v[l], kv[0, l], kv[1, l], ctx, scale, pkg.store_kvcache)
+            if fp8:
+                pkg.forward_mixed_fp8(q[l], k[l], v[l], kv[0, l], kv[1, l], sc[0, l], sc[1, l],
+                                      ctx, scale)
+            else:
+                pkg.forward_mixed(q[l], k[l], v[l], kv[0, l], kv[1, l], ctx, scale,
+                                  pkg.store_kvcache)
 
     def prefill_only():
         for l in range(L):
-            pkg.flash_attn_varlen_func(q[l, MIXED_DECODE:], kv[0, l], kv[1, l], meta.prefill_cu_q,
-                                       meta.prefill_cu_k, meta.max_q, meta.max_k,
-                                       softmax_scale=scale, block_table=meta.prefill_tables)
+            if fp8:
+                pkg.flash_attn_varlen_func_fp8(q[l, MIXED_DECODE:], kv[0, l], kv[1, l], sc[0, l],
+                                               sc[1, l], meta.prefill_cu_q, meta.prefill_cu_k,
+                                               meta.max_q, meta.max_k, softmax_scale=scale,
+                                               block_table=meta.prefill_tables)
+            else:
+                pkg.flash_attn_varlen_func(q[l, MIXED_DECODE:], kv[0, l], kv[1, l],
+                                           meta.prefill_cu_q, meta.prefill_cu_k, meta.max_q,
+                                           meta.max_k, softmax_scale=scale,
+                                           block_table=meta.prefill_tables)
 
     step()
+    prefill_only()                  # eager: sizes the per-device buffers before capture
     torch.cuda.synchronize()
     graph, pgraph = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph):
@@ -658,26 +704,32 @@ def run_mixed(args):
     achieved = flops / (pre_ms * 1e-3) / 1e12
     traffic = None
     try:
-        with open(os.path.join(ROOT, "profiles", "paged_prefill_traffic.json")) as f:
-            traffic = json.load(f).get("dram_bytes_per_launch")
+        if not fp8:
+            with open(os.path.join(ROOT, "profiles", "paged_prefill_traffic.json")) as f:
+                traffic = json.load(f).get("dram_bytes_per_launch")
     except Exception:
         pass
     line = {
         "metric": "mixed prefill/decode step tokens/s (config 3) and prefill tensor TFLOP/s",
         "value": round(T / (ms * 1e-3), 1), "unit": "tok/s", "n_gpus": 1, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seed 1)",
+        "scaling": "weak", "vs_baseline": None,
+        "dtype": "fp8_e4m3 KV (f16 MMA on codes), bf16 q/out" if fp8 else "bf16",
+        "data": "synthetic (seed 1)",
         "config": {"workload": "BASELINE config 3: 64 decode rows (context U[256,4096]) + 3 "
                                "prefill chunks of 2048 over cached prefixes 0/1024/3072, 36 layers "
-                               "of forward_mixed (store + paged decode + paged varlen)",
+                               "of forward_mixed (store + paged decode + paged varlen)"
+                               + (" over an FP8-E4M3 pool (forward_mixed_fp8)" if fp8 else ""),
                    "tokens_per_step": T, "layers": L, "pool_blocks": NB},
-        "roofline": {"kernel": "paged_prefill (tcgen05, one layer)", "bound": "tensor",
+        "roofline": {"kernel": "paged_prefill (tcgen05, one layer"
+                               + (", incl. the f16 page copy)" if fp8 else ")"),
+                     "bound": "tensor",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind_str(kind),
                      "algorithmic_flops": flops, "launch_ms": round(pre_ms, 4),
                      "traffic": traffic},
-        # per layer: append, decode + merge, prefill work order + prefill
-        "gpu_launches": args.steps * L * 5,
+        # per layer: append, decode + merge, prefill work order + prefill (+ FP8 page copy)
+        "gpu_launches": args.steps * L * (6 if fp8 else 5),
         "clocks": clocks.summary(),
         "device_errors": pkg.read_device_errors(),
     }

@@ -56,7 +56,7 @@ __device__ __forceinline__ uint32_t encode4(float4 v, float div, bool &bad) {
 }
 
 template <typename T>
-__global__ void __launch_bounds__(256) kv_append_fp8_kernel(
+__global__ void __launch_bounds__(256, 2) kv_append_fp8_kernel(
     const T *__restrict__ key, int64_t key_stride, const T *__restrict__ value,
     int64_t value_stride, uint8_t *__restrict__ k_codes, uint8_t *__restrict__ v_codes,
     float *__restrict__ k_scale, float *__restrict__ v_scale, const int32_t *__restrict__ slots,
@@ -94,11 +94,23 @@ __global__ void __launch_bounds__(256) kv_append_fp8_kernel(
   const int64_t row = static_cast<int64_t>(hkv) * kHeadDim;  // codes per token
   const int d0 = lane * 4;
 
+  // Runs of prefill tokens are up to a block long: the loops below keep
+  // kUnroll independent loads in flight per lane instead of one.
+  constexpr int kUnroll = 8;
+  auto absmax4 = [](float4 v) {
+    return fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+  };
+  const T *hsrc = src + h * kHeadDim + d0;
   float amax = 0.f;
-  for (int t = i; t < j; ++t) {
-    const float4 v = load4<T>(src + t * sstride + h * kHeadDim + d0);
-    amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+  int t = i;
+  for (; t + kUnroll <= j; t += kUnroll) {
+    float4 v[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) v[u] = load4<T>(hsrc + (t + u) * sstride);
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) amax = fmaxf(amax, absmax4(v[u]));
   }
+  for (; t < j; ++t) amax = fmaxf(amax, absmax4(load4<T>(hsrc + t * sstride)));
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
 
@@ -108,22 +120,41 @@ __global__ void __launch_bounds__(256) kv_append_fp8_kernel(
   bool bad = false;
   uint8_t *base = codes + static_cast<int64_t>(blk) * block_size * row + h * kHeadDim + d0;
   if (s_new > s_old && s_old > 0.f) {
-    for (int p = 0; p < off; ++p) {
-      uint32_t *cp = reinterpret_cast<uint32_t *>(base + p * row);
-      const uint32_t c = *cp;
+    auto reencode = [&](uint32_t c) {
       float4 v;
       v.x = __fmul_rn(e4m3_decode(c & 0xffu), s_old);
       v.y = __fmul_rn(e4m3_decode((c >> 8) & 0xffu), s_old);
       v.z = __fmul_rn(e4m3_decode((c >> 16) & 0xffu), s_old);
       v.w = __fmul_rn(e4m3_decode(c >> 24), s_old);
-      *cp = encode4(v, s_new, bad);
+      return encode4(v, s_new, bad);
+    };
+    int p = 0;
+    for (; p + kUnroll <= off; p += kUnroll) {
+      uint32_t c[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) c[u] = *reinterpret_cast<const uint32_t *>(base + (p + u) * row);
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u)
+        *reinterpret_cast<uint32_t *>(base + (p + u) * row) = reencode(c[u]);
+    }
+    for (; p < off; ++p) {
+      uint32_t *cp = reinterpret_cast<uint32_t *>(base + p * row);
+      *cp = reencode(*cp);
     }
   }
   const float div = s_new > 0.f ? s_new : 1.0f;
-  for (int t = i; t < j; ++t) {
-    const float4 v = load4<T>(src + t * sstride + h * kHeadDim + d0);
-    *reinterpret_cast<uint32_t *>(base + (off + (t - i)) * row) = encode4(v, div, bad);
+  uint8_t *dst = base + off * row;
+  t = i;
+  for (; t + kUnroll <= j; t += kUnroll) {
+    float4 v[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) v[u] = load4<T>(hsrc + (t + u) * sstride);
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u)
+      *reinterpret_cast<uint32_t *>(dst + (t - i + u) * row) = encode4(v[u], div, bad);
   }
+  for (; t < j; ++t)
+    *reinterpret_cast<uint32_t *>(dst + (t - i) * row) = encode4(load4<T>(hsrc + t * sstride), div, bad);
   __syncwarp();
   if (lane == 0) *sp = s_new;
   if (__any_sync(0xffffffffu, bad) && lane == 0) record_error(err, SLOKV_DEVERR_NONFINITE);

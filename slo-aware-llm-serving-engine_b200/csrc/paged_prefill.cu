@@ -502,6 +502,10 @@ constexpr int kOffV = 4 * kTile;
 constexpr int kTilesBytes = 6 * kTile;
 enum Bar { kQ = 0, kK = 1, kV = 3, kFreeK = 5, kFreeV = 7, kS = 9, kP = 11, kPV = 13, kNum = 15 };
 constexpr int kSmem = 1024 + kTilesBytes + kNum * 8 + 16;
+// FP8 pools: the row's per-page K scales (one float per page of the row, for
+// the CTA's KV head) follow, so the tile loop reads them from shared memory.
+constexpr int kOffScale = kTilesBytes + kNum * 8 + 16;
+constexpr int kSmemMax = 232448;   // per-block opt-in limit of sm_100
 constexpr int kThreads = 384;
 // Register split (setmaxnreg): the block launches with 168 registers a thread
 // (384 threads x 168 = 64512); warps 8-11 drop to kRegsIssue and the two softmax
@@ -513,7 +517,11 @@ static_assert(2 * 128 * kRegsSoftmax + 128 * kRegsIssue <= kThreads * kRegsLaunc
 constexpr uint32_t kColS = 0, kColO = 256;
 }  // namespace ws
 
-template <typename T>
+// kPageScale: the K pages hold unscaled FP8 code values and every tile's logits
+// take the page's K scale (FP8 pools).  A separate instantiation, so the plain
+// bf16/f16 kernel keeps its register allocation (the scale bookkeeping costs
+// the softmax warps a few spilled registers).
+template <typename T, bool kPageScale>
 __global__ void __launch_bounds__(ws::kThreads, 1)
     paged_prefill_ws_kernel(const __grid_constant__ CUtensorMap qmap,
                             const __grid_constant__ CUtensorMap kmap,
@@ -568,6 +576,18 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
       reinterpret_cast<volatile uint32_t *>(base_ptr + ws::kTilesBytes + ws::kNum * 8);
   volatile uint32_t *abort_flag = tmem_slot + 1;
   auto bar = [&](int i) { return bars + i * 8; };
+  float *s_ks = reinterpret_cast<float *>(base_ptr + ws::kOffScale);
+  if constexpr (kPageScale) {  // the row's page scales, read after the barrier below
+    // (the table holds max_blocks entries: pages past the block table, i.e.
+    // contexts longer than the table, are neither written nor read)
+    const int npg = min((need + p.block_size - 1) / p.block_size, p.max_blocks);
+    for (int pg = tid; pg < npg; pg += ws::kThreads) {
+      const int32_t pid = __ldg(p.block_tables + static_cast<int64_t>(r) * p.bt_stride + pg);
+      s_ks[pg] = pid >= 0 && pid < p.num_blocks
+                     ? __ldg(p.k_page_scale + static_cast<int64_t>(pid) * p.hkv + hk)
+                     : 0.f;
+    }
+  }
 
   if (tid == 0) {
     prefetch_tensormap(&qmap);
@@ -747,18 +767,12 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
       tc::fence_after_sync();
       const int key0 = j * kBN;
       const bool full = key0 + kBN - 1 <= kmax;   // no key of the tile is masked
-      float sl = p.scale_log2;
-      if (p.k_page_scale != nullptr) {
-        // a zero scale (page of zero codes) must keep masked -inf keys at -inf
-        const int page = key0 / p.block_size;
-        const int32_t pid = page < p.max_blocks
-                                ? __ldg(p.block_tables + static_cast<int64_t>(r) * p.bt_stride + page)
-                                : -1;
-        const float ks = pid >= 0 && pid < p.num_blocks
-                             ? __ldg(p.k_page_scale + static_cast<int64_t>(pid) * p.hkv + hk)
-                             : 0.f;
-        sl *= fmaxf(ks, 1e-30f);
-      }
+      // K page scale of the tile (FP8 pools); a zero scale, a page of zero
+      // codes, must keep masked -inf keys at -inf
+      const int kpage = key0 / p.block_size;
+      const float sl =
+          kPageScale ? p.scale_log2 * fmaxf(kpage < p.max_blocks ? s_ks[kpage] : 0.f, 1e-30f)
+                     : p.scale_log2;
 #pragma unroll
       for (int i = 0; i < 4; ++i) tc::ld32(s_addr + 32 * i, s[i]);
       tc::wait_ld();
@@ -878,30 +892,44 @@ template <typename T>
 int launch(const Params &p, const CUtensorMap &qm, const CUtensorMap &km, const CUtensorMap &vm,
            int rows, int max_q, cudaStream_t stream) {
   static std::once_flag once;
-  static bool ok = false, ws_ok = false;
+  static bool ok = false, ws_ok = false, ws_scaled_ok = false;
   std::call_once(once, [] {
     ok = cudaFuncSetAttribute(paged_prefill_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                               kSmemBytes) == cudaSuccess &&
-         cudaFuncSetAttribute(paged_prefill_ws_kernel<T>,
-                              cudaFuncAttributeMaxDynamicSharedMemorySize, ws::kSmem) == cudaSuccess;
+         cudaFuncSetAttribute(paged_prefill_ws_kernel<T, false>,
+                              cudaFuncAttributeMaxDynamicSharedMemorySize, ws::kSmem) == cudaSuccess &&
+         cudaFuncSetAttribute(paged_prefill_ws_kernel<T, true>,
+                              cudaFuncAttributeMaxDynamicSharedMemorySize, ws::kSmemMax) ==
+             cudaSuccess;
     // The register split in the two-head kernel hands out exactly the launch
     // allocation; with any other per-thread count setmaxnreg.inc could not be
     // satisfied, so that kernel is used only when the build matches.
     cudaFuncAttributes fa;
-    ws_ok = ok && cudaFuncGetAttributes(&fa, paged_prefill_ws_kernel<T>) == cudaSuccess &&
+    ws_ok = ok && cudaFuncGetAttributes(&fa, paged_prefill_ws_kernel<T, false>) == cudaSuccess &&
             fa.numRegs == ws::kRegsLaunch;
+    ws_scaled_ok = ok &&
+                   cudaFuncGetAttributes(&fa, paged_prefill_ws_kernel<T, true>) == cudaSuccess &&
+                   fa.numRegs == ws::kRegsLaunch;
   });
   if (!ok) return SLOKV_ERR_CUDA;
-  if (p.k_page_scale != nullptr && !(p.group % 2 == 0 && ws_ok)) return SLOKV_ERR_UNSUPPORTED;
-  if (p.group % 2 == 0 && ws_ok) {  // two query heads of one KV head per CTA
+  const bool scaled = p.k_page_scale != nullptr;
+  if (scaled && !(p.group % 2 == 0 && ws_scaled_ok)) return SLOKV_ERR_UNSUPPORTED;
+  const int64_t smem_scaled = ws::kSmem + 4 * static_cast<int64_t>(p.max_blocks);
+  if (scaled && smem_scaled > ws::kSmemMax) return SLOKV_ERR_UNSUPPORTED;
+  if (p.group % 2 == 0 && (scaled || ws_ok)) {  // two query heads of one KV head per CTA
     if (p.order != nullptr) {
       prefill_schedule_kernel<<<1, kSchedThreads, 0, stream>>>(
           p.cu_q, p.cu_k, rows, p.m_tiles, const_cast<int32_t *>(p.order));
     }
     const int64_t blocks = static_cast<int64_t>(rows) * p.m_tiles * (p.hq / 2);
     if (blocks > 0x7fffffff) return SLOKV_ERR_UNSUPPORTED;
-    paged_prefill_ws_kernel<T><<<static_cast<unsigned>(blocks), ws::kThreads, ws::kSmem,
-                                 stream>>>(qm, km, vm, p);
+    if (scaled)
+      paged_prefill_ws_kernel<T, true><<<static_cast<unsigned>(blocks), ws::kThreads,
+                                         static_cast<unsigned>(smem_scaled), stream>>>(qm, km, vm,
+                                                                                        p);
+    else
+      paged_prefill_ws_kernel<T, false><<<static_cast<unsigned>(blocks), ws::kThreads, ws::kSmem,
+                                          stream>>>(qm, km, vm, p);
   } else {
     dim3 grid((max_q + kBM - 1) / kBM, p.hq, rows);
     paged_prefill_kernel<T><<<grid, 128, kSmemBytes, stream>>>(qm, km, vm, p);
