@@ -233,6 +233,25 @@ int slokv_fp8_pages_dequant(const void *k_codes, const void *v_codes, int64_t k_
                             void *dst_k, void *dst_v, float *dst_k_scale, uint32_t *dev_error,
                             void *stream);
 
+/* slokv_kv_append_fp8 for calls with long runs (prefill chunks: up to a block
+ * of new tokens per (block, kv head)), token-parallel in three launches: each
+ * (token, head, K|V) takes its row's amax into a per-(block, head, K|V) word
+ * (atomicMax on the float bits), then every token is encoded with s_new =
+ * max(s_old, amax / 448) (the run's first token re-encodes the block's earlier
+ * positions when the scale grows), then the run's first token stores s_new and
+ * clears the word.  Same arguments, codes and scales as slokv_kv_append_fp8,
+ * plus `workspace`: slokv_kv_append_fp8_runs_workspace_bytes(num_blocks,
+ * num_kv_heads) bytes, 4-byte aligned, zero before the first call (each call
+ * leaves it zero); else SLOKV_ERR_WORKSPACE. */
+size_t slokv_kv_append_fp8_runs_workspace_bytes(int32_t num_blocks, int32_t num_kv_heads);
+int slokv_kv_append_fp8_runs(const void *key, int64_t key_row_stride, const void *value,
+                             int64_t value_row_stride, void *k_codes, void *v_codes,
+                             float *k_scale, float *v_scale, const int32_t *slot_mapping,
+                             int32_t num_tokens, int32_t num_kv_heads, int32_t head_dim,
+                             int32_t block_size, int32_t num_blocks, int32_t in_dtype,
+                             void *workspace, size_t workspace_bytes, uint32_t *dev_error,
+                             void *stream);
+
 /* Workspace of slokv_paged_decode_fp8 (8 warp slots per SM), in bytes. */
 size_t slokv_paged_decode_fp8_workspace_bytes(int32_t device, int32_t num_q_heads,
                                               int32_t num_kv_heads, int32_t head_dim);

@@ -79,6 +79,11 @@ SIGNATURES = {
         _c_vp, _c_vp, _c_vp, _c_i64,                  # slot_mapping, k_cache, v_cache, slots
         _c_vp, _c_i64, _c_vp, _c_i64,                 # q_out, stride, k_out, stride
         _c_i32, _c_vp, _c_vp]),                       # dtype, dev_error, stream
+    "slokv_kv_append_fp8_runs_workspace_bytes": (_c_sz, [_c_i32, _c_i32]),
+    "slokv_kv_append_fp8_runs": (ctypes.c_int, [
+        _c_vp, _c_i64, _c_vp, _c_i64, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_i32, _c_i32,
+        _c_i32, _c_i32, _c_i32, _c_i32,           # as slokv_kv_append_fp8, then
+        _c_vp, _c_sz, _c_vp, _c_vp]),             # workspace, bytes, dev_error, stream
     "slokv_kv_append_fp8": (ctypes.c_int, [
         _c_vp, _c_i64, _c_vp, _c_i64, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_i32, _c_i32,
         _c_i32, _c_i32, _c_i32, _c_i32, _c_vp, _c_vp]),
@@ -198,7 +203,10 @@ class _PerDevice:
             self._err[idx] = t
         return t
 
-    def workspace(self, device: torch.device, key: str, nbytes: int) -> torch.Tensor:
+    def workspace(self, device: torch.device, key: str, nbytes: int,
+                  zero: bool = False) -> torch.Tensor:
+        """Buffer `key` of at least nbytes; `zero`: allocated zero-filled (for
+        buffers the kernels leave zero after every call)."""
         idx = device.index if device.index is not None else torch.cuda.current_device()
         t = self._ws.get((idx, key))
         if t is None or t.numel() < nbytes:
@@ -206,8 +214,8 @@ class _PerDevice:
                 raise SlokvError(
                     f"workspace '{key}' must be allocated before CUDA graph capture; call the op "
                     "once eagerly (warm-up) with the largest geometry first")
-            t = torch.empty(max(nbytes, 256), dtype=torch.uint8,
-                            device=torch.device("cuda", idx))
+            t = (torch.zeros if zero else torch.empty)(max(nbytes, 256), dtype=torch.uint8,
+                                                       device=torch.device("cuda", idx))
             self._ws[(idx, key)] = t
         return t
 

@@ -160,6 +160,138 @@ __global__ void __launch_bounds__(256, 2) kv_append_fp8_kernel(
   if (__any_sync(0xffffffffu, bad) && lane == 0) record_error(err, SLOKV_DEVERR_NONFINITE);
 }
 
+// ---- the same append in three launches, for calls with long runs ------------
+//
+// A prefill chunk writes runs of up to a block (256 tokens) per (block, head,
+// K|V); one warp per run walks them serially.  Here every (token, head, K|V)
+// warp works on its own token: (1) its row's amax goes into a per-(block, head,
+// K|V) word with atomicMax on the float bits (non-negative floats order like
+// their bit patterns, so the word ends as the exact run amax); (2) each warp
+// derives s_new = max(s_old, amax / 448) -- the same value for every warp of
+// the run -- and encodes its token; the run's first warp re-encodes the block's
+// earlier positions when the scale grows; (3) the run's first warp stores s_new
+// and clears the word.  Codes and scales are the one-launch kernel's, bit for
+// bit.  `amax_ws` is num_blocks * hkv * 2 words, zero between calls.
+
+struct RunToken {
+  bool valid;       // a slot inside the pool
+  bool start;       // the first token of its block's run
+  int32_t blk, off; // block and position of the token
+};
+
+__device__ __forceinline__ RunToken run_token(const int32_t *slots, int i, int32_t block_size,
+                                              int64_t num_slots) {
+  RunToken t;
+  const int32_t slot = __ldg(slots + i);
+  t.valid = slot >= 0 && slot < num_slots;
+  t.blk = t.valid ? slot / block_size : 0;
+  t.off = t.valid ? slot - t.blk * block_size : 0;
+  t.start = t.valid;
+  if (t.valid && i > 0) {
+    const int32_t prev = __ldg(slots + i - 1);
+    if (prev >= 0 && prev == slot - 1 && prev / block_size == t.blk) t.start = false;
+  }
+  return t;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) kv_append_fp8_amax_kernel(
+    const T *__restrict__ key, int64_t key_stride, const T *__restrict__ value,
+    int64_t value_stride, const int32_t *__restrict__ slots, int32_t num_tokens, int32_t hkv,
+    int32_t block_size, int32_t num_blocks, uint32_t *__restrict__ amax_ws, uint32_t *err) {
+  const int lane = threadIdx.x & 31;
+  const int64_t wid = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  if (wid >= static_cast<int64_t>(num_tokens) * hkv * 2) return;
+  const int which = static_cast<int>(wid & 1);
+  const int h = static_cast<int>((wid >> 1) % hkv);
+  const int i = static_cast<int>((wid >> 1) / hkv);
+  const int32_t slot = __ldg(slots + i);
+  if (slot < 0 || slot >= static_cast<int64_t>(num_blocks) * block_size) {
+    if (slot != -1 && lane == 0 && h == 0 && which == 0) record_error(err, SLOKV_DEVERR_SLOT_RANGE);
+    return;
+  }
+  const T *src = (which ? value + i * value_stride : key + i * key_stride) + h * kHeadDim + lane * 4;
+  const float4 v = load4<T>(src);
+  // seeded with 0 as in the one-launch kernel: NaN elements drop out of the max
+  // (fmaxf keeps the non-NaN operand), so the word never holds NaN bits
+  float a = fmaxf(fmaxf(fmaxf(0.f, fabsf(v.x)), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+  if (lane == 0)
+    atomicMax(amax_ws + (static_cast<int64_t>(slot / block_size) * hkv + h) * 2 + which,
+              __float_as_uint(a));
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256, 2) kv_append_fp8_encode_kernel(
+    const T *__restrict__ key, int64_t key_stride, const T *__restrict__ value,
+    int64_t value_stride, uint8_t *__restrict__ k_codes, uint8_t *__restrict__ v_codes,
+    const float *__restrict__ k_scale, const float *__restrict__ v_scale,
+    const int32_t *__restrict__ slots, int32_t num_tokens, int32_t hkv, int32_t block_size,
+    int32_t num_blocks, const uint32_t *__restrict__ amax_ws, uint32_t *err) {
+  const int lane = threadIdx.x & 31;
+  const int64_t wid = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  if (wid >= static_cast<int64_t>(num_tokens) * hkv * 2) return;
+  const int which = static_cast<int>(wid & 1);
+  const int h = static_cast<int>((wid >> 1) % hkv);
+  const int i = static_cast<int>((wid >> 1) / hkv);
+  const RunToken tk = run_token(slots, i, block_size, static_cast<int64_t>(num_blocks) * block_size);
+  if (!tk.valid) return;
+  const int64_t si = static_cast<int64_t>(tk.blk) * hkv + h;
+  const float s_old = (which ? v_scale : k_scale)[si];
+  const float s_new = fmaxf(s_old, __fdiv_rn(__uint_as_float(amax_ws[si * 2 + which]), 448.0f));
+  const int64_t row = static_cast<int64_t>(hkv) * kHeadDim;
+  const int d0 = lane * 4;
+  uint8_t *base = (which ? v_codes : k_codes) + static_cast<int64_t>(tk.blk) * block_size * row +
+                  h * kHeadDim + d0;
+  bool bad = false;
+  if (tk.start && s_new > s_old && s_old > 0.f) {   // earlier positions of the block
+    constexpr int kUnroll = 8;
+    auto reencode = [&](uint32_t c) {
+      float4 v;
+      v.x = __fmul_rn(e4m3_decode(c & 0xffu), s_old);
+      v.y = __fmul_rn(e4m3_decode((c >> 8) & 0xffu), s_old);
+      v.z = __fmul_rn(e4m3_decode((c >> 16) & 0xffu), s_old);
+      v.w = __fmul_rn(e4m3_decode(c >> 24), s_old);
+      return encode4(v, s_new, bad);
+    };
+    int p = 0;
+    for (; p + kUnroll <= tk.off; p += kUnroll) {
+      uint32_t c[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) c[u] = *reinterpret_cast<const uint32_t *>(base + (p + u) * row);
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u)
+        *reinterpret_cast<uint32_t *>(base + (p + u) * row) = reencode(c[u]);
+    }
+    for (; p < tk.off; ++p) {
+      uint32_t *cp = reinterpret_cast<uint32_t *>(base + p * row);
+      *cp = reencode(*cp);
+    }
+  }
+  const T *src = (which ? value + i * value_stride : key + i * key_stride) + h * kHeadDim + d0;
+  *reinterpret_cast<uint32_t *>(base + tk.off * row) =
+      encode4(load4<T>(src), s_new > 0.f ? s_new : 1.0f, bad);
+  if (__any_sync(0xffffffffu, bad) && lane == 0) record_error(err, SLOKV_DEVERR_NONFINITE);
+}
+
+__global__ void __launch_bounds__(256) kv_append_fp8_commit_kernel(
+    float *__restrict__ k_scale, float *__restrict__ v_scale, const int32_t *__restrict__ slots,
+    int32_t num_tokens, int32_t hkv, int32_t block_size, int32_t num_blocks,
+    uint32_t *__restrict__ amax_ws) {
+  const int64_t u = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (u >= static_cast<int64_t>(num_tokens) * hkv * 2) return;
+  const int which = static_cast<int>(u & 1);
+  const int h = static_cast<int>((u >> 1) % hkv);
+  const int i = static_cast<int>((u >> 1) / hkv);
+  const RunToken tk = run_token(slots, i, block_size, static_cast<int64_t>(num_blocks) * block_size);
+  if (!tk.valid || !tk.start) return;
+  const int64_t si = static_cast<int64_t>(tk.blk) * hkv + h;
+  float *sp = (which ? v_scale : k_scale) + si;
+  *sp = fmaxf(*sp, __fdiv_rn(__uint_as_float(amax_ws[si * 2 + which]), 448.0f));
+  amax_ws[si * 2 + which] = 0u;
+}
+
 __global__ void e4m3_encode_kernel(const float *__restrict__ x, uint8_t *__restrict__ codes,
                                    int64_t n, uint32_t *err) {
   bool bad = false;
@@ -246,5 +378,68 @@ extern "C" int slokv_fp8_e4m3_decode(const uint8_t *codes, float *x, int64_t n, 
   if (n == 0) return SLOKV_OK;
   if (!x || !codes) return SLOKV_ERR_INVALID_ARG;
   e4m3_decode_kernel<<<grid_for(n), 256, 0, static_cast<cudaStream_t>(stream)>>>(codes, x, n);
+  return cudaGetLastError() == cudaSuccess ? SLOKV_OK : SLOKV_ERR_CUDA;
+}
+
+extern "C" size_t slokv_kv_append_fp8_runs_workspace_bytes(int32_t num_blocks,
+                                                            int32_t num_kv_heads) {
+  if (num_blocks <= 0 || num_kv_heads <= 0) return 0;
+  return static_cast<size_t>(num_blocks) * num_kv_heads * 2 * sizeof(uint32_t);
+}
+
+extern "C" int slokv_kv_append_fp8_runs(const void *key, int64_t key_row_stride,
+                                        const void *value, int64_t value_row_stride,
+                                        void *k_codes, void *v_codes, float *k_scale,
+                                        float *v_scale, const int32_t *slot_mapping,
+                                        int32_t num_tokens, int32_t num_kv_heads,
+                                        int32_t head_dim, int32_t block_size, int32_t num_blocks,
+                                        int32_t in_dtype, void *workspace,
+                                        size_t workspace_bytes, uint32_t *dev_error,
+                                        void *stream) {
+  using namespace slokv;
+  if (num_tokens < 0 || num_kv_heads <= 0 || block_size <= 0 || num_blocks <= 0)
+    return SLOKV_ERR_INVALID_ARG;
+  if (head_dim != kHeadDim) return SLOKV_ERR_UNSUPPORTED;
+  if (num_tokens == 0) return SLOKV_OK;
+  if (!key || !value || !k_codes || !v_codes || !k_scale || !v_scale || !slot_mapping)
+    return SLOKV_ERR_INVALID_ARG;
+  if (!workspace ||
+      workspace_bytes < slokv_kv_append_fp8_runs_workspace_bytes(num_blocks, num_kv_heads) ||
+      (reinterpret_cast<uintptr_t>(workspace) & 3))
+    return SLOKV_ERR_WORKSPACE;
+  const int es = in_dtype == SLOKV_DTYPE_F32 ? 4 : 2;
+  if (in_dtype != SLOKV_DTYPE_BF16 && in_dtype != SLOKV_DTYPE_F16 && in_dtype != SLOKV_DTYPE_F32)
+    return SLOKV_ERR_UNSUPPORTED;
+  if ((reinterpret_cast<uintptr_t>(key) | reinterpret_cast<uintptr_t>(value)) % (4 * es) ||
+      ((key_row_stride | value_row_stride) & 3) ||
+      ((reinterpret_cast<uintptr_t>(k_codes) | reinterpret_cast<uintptr_t>(v_codes)) & 3))
+    return SLOKV_ERR_ALIGNMENT;
+  const int64_t units = static_cast<int64_t>(num_tokens) * num_kv_heads * 2;
+  const unsigned warp_grid = static_cast<unsigned>((units * 32 + 255) / 256);
+  const unsigned unit_grid = static_cast<unsigned>((units + 255) / 256);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  auto *kc = static_cast<uint8_t *>(k_codes);
+  auto *vc = static_cast<uint8_t *>(v_codes);
+  auto *ws = static_cast<uint32_t *>(workspace);
+  auto run = [&](auto tag) {
+    using T = decltype(tag);
+    kv_append_fp8_amax_kernel<T><<<warp_grid, 256, 0, st>>>(
+        static_cast<const T *>(key), key_row_stride, static_cast<const T *>(value),
+        value_row_stride, slot_mapping, num_tokens, num_kv_heads, block_size, num_blocks, ws,
+        dev_error);
+    kv_append_fp8_encode_kernel<T><<<warp_grid, 256, 0, st>>>(
+        static_cast<const T *>(key), key_row_stride, static_cast<const T *>(value),
+        value_row_stride, kc, vc, k_scale, v_scale, slot_mapping, num_tokens, num_kv_heads,
+        block_size, num_blocks, ws, dev_error);
+    kv_append_fp8_commit_kernel<<<unit_grid, 256, 0, st>>>(k_scale, v_scale, slot_mapping,
+                                                            num_tokens, num_kv_heads, block_size,
+                                                            num_blocks, ws);
+  };
+  if (in_dtype == SLOKV_DTYPE_BF16)
+    run(__nv_bfloat16{});
+  else if (in_dtype == SLOKV_DTYPE_F16)
+    run(__half{});
+  else
+    run(float{});
   return cudaGetLastError() == cudaSuccess ? SLOKV_OK : SLOKV_ERR_CUDA;
 }

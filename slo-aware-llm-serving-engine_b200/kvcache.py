@@ -181,15 +181,24 @@ def is_fp8_cache(cache: torch.Tensor) -> bool:
     return cache.dtype in FP8_DTYPES
 
 
+# Calls with at least this many tokens (prefill-sized: runs of up to a block
+# per (block, head)) take the three-launch append, which works token-parallel.
+_FP8_RUNS_MIN_TOKENS = 512
+
+
 def store_kvcache_fp8(key: torch.Tensor, value: torch.Tensor, k_codes: torch.Tensor,
                       v_codes: torch.Tensor, k_scale: torch.Tensor, v_scale: torch.Tensor,
-                      slot_mapping: torch.Tensor) -> None:
+                      slot_mapping: torch.Tensor, *, runs: bool | None = None) -> None:
     """Quantising store into the FP8 pool (store_kvcache's counterpart).
 
     k_codes/v_codes: [num_blocks, block_size, Hkv, D] uint8 (or float8_e4m3fn);
     k_scale/v_scale: [num_blocks, Hkv] fp32, zero for freshly assigned blocks.
     The new tokens of one block must be adjacent in slot_mapping with
     consecutive offsets (the engine's decode and prefill layouts are).
+    `runs`: force the token-parallel three-launch append (True) or the one-launch
+    kernel (False); by default calls of >= 512 tokens take the former once its
+    zeroed per-device word array exists (it is never grown during graph
+    capture).  Both write identical codes and scales.
     """
     N, num_heads, head_dim = key.shape
     assert key.stride(-1) == 1 and value.stride(-1) == 1
@@ -207,6 +216,20 @@ def store_kvcache_fp8(key: torch.Tensor, value: torch.Tensor, k_codes: torch.Ten
             raise SlokvError(f"{name} must be contiguous fp32 [num_blocks, num_kv_heads]")
     _i32_contig("slot_mapping", slot_mapping)
     err = buffers.error_word(dev)
+    use_runs = runs if runs is not None else N >= _FP8_RUNS_MIN_TOKENS
+    if use_runs:
+        nbytes = lib().slokv_kv_append_fp8_runs_workspace_bytes(NB, Hkv)
+        if (runs is None and torch.cuda.is_current_stream_capturing()
+                and not buffers.workspace_fits(dev, "fp8_append_amax", nbytes)):
+            use_runs = False
+    if use_runs:
+        ws = buffers.workspace(dev, "fp8_append_amax", nbytes, zero=True)
+        check(lib().slokv_kv_append_fp8_runs(
+            key.data_ptr(), key.stride(0), value.data_ptr(), value.stride(0),
+            k_codes.data_ptr(), v_codes.data_ptr(), k_scale.data_ptr(), v_scale.data_ptr(),
+            slot_mapping.data_ptr(), N, Hkv, D, bs, NB, _lib.dtype_code(key.dtype),
+            ws.data_ptr(), ws.numel(), err.data_ptr(), stream_ptr(dev)), "kv_append_fp8_runs")
+        return
     check(lib().slokv_kv_append_fp8(
         key.data_ptr(), key.stride(0), value.data_ptr(), value.stride(0),
         k_codes.data_ptr(), v_codes.data_ptr(), k_scale.data_ptr(), v_scale.data_ptr(),

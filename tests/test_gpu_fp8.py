@@ -78,10 +78,14 @@ def _assert_pool_equal(dev, ref):
         assert torch.equal(d.cpu(), r), "FP8 pool differs from the oracle"
 
 
-def test_prefill_runs_then_decode_appends_bit_exact(pkg):
-    """Prefill chunks that start mid-block and cross block boundaries, then
-    step-by-step decode appends (re-encoding when an outlier raises a block's
-    amax), with padding slots; codes and scales bit-exact after every call."""
+@pytest.mark.parametrize("runs", [False, True])
+def test_prefill_runs_then_decode_appends_bit_exact(pkg, runs):
+    """Prefill chunks that cross block boundaries, then step-by-step decode
+    appends (re-encoding when an outlier raises a block's amax), with padding
+    slots, then a second chunk per row that starts mid-block with outliers (a
+    long run whose first token re-encodes the block's earlier codes); codes and
+    scales bit-exact after every call -- through the one-launch kernel and
+    through the token-parallel three-launch append (runs=True)."""
     H, D, bs, NB = 8, 128, 256, 24
     ref = _pools(NB, H=H)
     dev = _gpu(ref)
@@ -93,7 +97,7 @@ def test_prefill_runs_then_decode_appends_bit_exact(pkg):
     y = kv_values(73, (len(slots), H, D))
     sl = torch.tensor(slots, dtype=torch.int32)
     O.fp8_append(x, y, *ref, sl)
-    pkg.store_kvcache_fp8(x.cuda(), y.cuda(), *dev, sl.cuda())
+    pkg.store_kvcache_fp8(x.cuda(), y.cuda(), *dev, sl.cuda(), runs=runs)
     _assert_pool_equal(dev, ref)
     # decode: one token per row per step, a padding row in between
     for step in range(40):
@@ -104,9 +108,18 @@ def test_prefill_runs_then_decode_appends_bit_exact(pkg):
         ys = kv_values(2000 + step, (3, H, D), outlier_frac=0.02)
         st = torch.tensor(s, dtype=torch.int32)
         O.fp8_append(xs, ys, *ref, st)
-        pkg.store_kvcache_fp8(xs.cuda(), ys.cuda(), *dev, st.cuda())
+        pkg.store_kvcache_fp8(xs.cuda(), ys.cuda(), *dev, st.cuda(), runs=runs)
         if step % 8 == 7:
             _assert_pool_equal(dev, ref)
+    _assert_pool_equal(dev, ref)
+    # second chunk: 300 more tokens per row from mid-block, outliers raise scales
+    start = [hist[0] + 40, hist[1] + 40]
+    slots = [tables[r][p // bs] * bs + p % bs for r in range(2) for p in range(start[r], start[r] + 300)]
+    x = kv_values(81, (len(slots), H, D), outlier_frac=0.05)
+    y = kv_values(83, (len(slots), H, D), outlier_frac=0.05)
+    sl = torch.tensor(slots, dtype=torch.int32)
+    O.fp8_append(x, y, *ref, sl)
+    pkg.store_kvcache_fp8(x.cuda(), y.cuda(), *dev, sl.cuda(), runs=runs)
     _assert_pool_equal(dev, ref)
     assert pkg.read_device_errors() == 0
 
