@@ -64,3 +64,21 @@ def test_mixed_requires_allocated_pool(pkg):
     with pytest.raises(RuntimeError, match="allocated"):
         pkg.forward_mixed(torch.zeros(1, 8, 128), torch.zeros(1, 2, 128), torch.zeros(1, 2, 128),
                           empty, empty, ctx, 0.1, pkg.store_kvcache)
+
+
+def test_bench_fp8_pool_fill_follows_the_config4_contract():
+    """bench.fill_fp8_pool (the FP8 benches' pool contents): the blocks the
+    batch reads hold E4M3 codes with per-(block, head) scale amax / 448 of
+    N(0, 1) data with 1 % x20 outliers; untouched blocks stay zero."""
+    import bench
+    kv = torch.zeros(2, 1, 6, 256, 2, 128, dtype=torch.uint8)
+    sc = torch.zeros(2, 1, 6, 2)
+    g = torch.Generator().manual_seed(0)
+    bench.fill_fp8_pool(kv, sc, [4, 1, 4], g, 1.0, True)
+    assert (sc[:, :, [0, 2, 3, 5]] == 0).all() and (kv[:, :, [0, 2, 3, 5]] == 0).all()
+    for blk in (1, 4):
+        vals = kv[0, 0, blk].view(torch.float8_e4m3fn).float() * sc[0, 0, blk][None, :, None]
+        amax = vals.abs().amax(dim=(0, 2))
+        # the largest code of each head is the saturating 448 (scale = amax / 448)
+        assert torch.allclose(amax, sc[0, 0, blk] * 448, rtol=0, atol=0)
+        assert 1.5 < vals.std().item() < 3.5            # N(0,1) with 1 % x20: std ~ 2.2
