@@ -117,3 +117,28 @@ def test_row_parallel_buffer_layout(pkg):
     assert lib.slokv_row_parallel_buffer_bytes(128, 2500, 2) == 0
     assert lib.slokv_row_parallel_buffer_bytes(0, 2560, 2) == 0
     assert lib.slokv_row_parallel_buffer_bytes(128, 2560, 9) == 0
+
+
+def test_fp8_runs_append_and_page_widen_argument_checks(pkg):
+    lib = pkg._lib.lib()
+    ws_bytes = lib.slokv_kv_append_fp8_runs_workspace_bytes(100, 8)
+    assert ws_bytes == 100 * 8 * 2 * 4
+    assert lib.slokv_kv_append_fp8_runs_workspace_bytes(0, 8) == 0
+
+    def runs(n=4, hd=128, ws=None, wsb=0, ptr=None):
+        return lib.slokv_kv_append_fp8_runs(ptr, 1024, ptr, 1024, ptr, ptr, ptr, ptr, ptr, n, 8,
+                                            hd, 256, 100, 0, ws, wsb, None, None)
+    assert runs(n=0) == 0                              # nothing to do
+    assert runs(n=-1) == -1
+    assert runs(hd=64) == -3                           # head_dim 128 only
+    assert runs() == -1                                # null pointers
+    assert runs(ptr=16, ws=None) == -5                 # workspace missing
+    assert runs(ptr=16, ws=256, wsb=ws_bytes - 4) == -5  # workspace too small
+
+    def widen(rows=2, width=3, hd=128, ptr=None):
+        return lib.slokv_fp8_pages_dequant(ptr, ptr, 0, 0, ptr, ptr, 100, 256, 8, hd, ptr, 4, 4,
+                                           ptr, rows, width, ptr, ptr, ptr, None, None)
+    assert widen(rows=0) == 0 and widen(width=0) == 0
+    assert widen(rows=-1) == -1
+    assert widen(hd=64) == -3
+    assert widen() == -1                               # null pointers
