@@ -26,7 +26,8 @@ from torch import nn
 from .. import _lib
 from .._lib import SlokvError, buffers, check, lib, require_cuda, stream_ptr
 
-__all__ = ["RowParallelAllReduce", "RowParallelLinear", "row_parallel_buffer_bytes"]
+__all__ = ["RowParallelAllReduce", "RowParallelLinear", "exchange_buffers",
+           "row_parallel_buffer_bytes"]
 
 _TILE_N = 128
 _TILE_K = 64
@@ -35,6 +36,22 @@ _TILE_K = 64
 def row_parallel_buffer_bytes(max_tokens: int, n_features: int, world: int) -> int:
     """Bytes of one rank's symmetric buffer (0 for an unsupported geometry)."""
     return int(lib().slokv_row_parallel_buffer_bytes(int(max_tokens), int(n_features), int(world)))
+
+
+def exchange_buffers(own_ptr: int, own_handle: bytes, import_handle, group=None) -> list[int]:
+    """All-gather every rank's IPC handle over `group` and map the peers'
+    buffers: returns the pointer of rank r's buffer as seen by this process at
+    index r (this rank's own `own_ptr` at its own index), then waits on a
+    barrier so no rank writes into a peer before every rank has mapped.
+    `import_handle(handle_bytes) -> int` opens one peer handle."""
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    handles = [None] * world
+    dist.all_gather_object(handles, bytes(own_handle), group=group)
+    ptrs = [own_ptr if r == rank else import_handle(h) for r, h in enumerate(handles)]
+    dist.barrier(group=group)
+    return ptrs
 
 
 def _ptr_array(values):
@@ -107,24 +124,18 @@ class RowParallelAllReduce:
         return p.value
 
     def _exchange(self, own: int) -> list[int]:
-        import torch.distributed as dist
         hsize = lib().slokv_ipc_handle_size()
         h = ctypes.create_string_buffer(hsize)
         check(lib().slokv_ipc_export(own, h), "ipc_export")
-        handles = [None] * self.world
-        dist.all_gather_object(handles, bytes(h.raw), group=self.group)
-        ptrs = []
-        for r, hb in enumerate(handles):
-            if r == self.rank:
-                ptrs.append(own)
-                continue
+
+        def import_handle(hb: bytes) -> int:
             p = ctypes.c_void_p()
             check(lib().slokv_ipc_import(ctypes.create_string_buffer(hb, hsize), ctypes.byref(p)),
                   "ipc_import")
             self._peers.append(p.value)
-            ptrs.append(p.value)
-        dist.barrier(group=self.group)
-        return ptrs
+            return p.value
+
+        return exchange_buffers(own, h.raw, import_handle, self.group)
 
     def close(self):
         """Release the peer mappings and this process's buffers.  Collective:

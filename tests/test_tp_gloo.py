@@ -124,3 +124,47 @@ def test_row_parallel_linear_two_ranks_shard_like_the_reference():
         assert shape == (2560, 512) and tp == 2 and reassembled
         assert cpu_forward == "raised"
         assert nbytes == results[0][5] > 0
+
+
+def _exchange_worker(rank, world, port, queue):
+    import importlib
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, root)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        lin = importlib.import_module("slo-aware-llm-serving-engine_b200.layers.linear")
+        own = 0x1000 * (rank + 1)
+        handle = bytes([rank]) * 64                     # stands in for a cudaIpcMemHandle_t
+        opened = []
+
+        def import_handle(h):                           # "maps" a peer: returns its tag
+            opened.append(h[0])
+            return 0xABC0000 + h[0]
+
+        ptrs = lin.exchange_buffers(own, handle, import_handle)
+        queue.put((rank, ptrs, opened))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_row_parallel_buffer_exchange_over_gloo(world):
+    """The symmetric-buffer handshake of the fused row-parallel all-reduce: every
+    rank gets rank r's buffer at index r (its own pointer at its own index, the
+    peers' opened from their handles, each peer exactly once)."""
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_exchange_worker, args=(r, world, port, queue))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    results = sorted(queue.get(timeout=240) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, ptrs, opened in results:
+        assert ptrs == [0x1000 * (r + 1) if r == rank else 0xABC0000 + r for r in range(world)]
+        assert sorted(opened) == [r for r in range(world) if r != rank]
