@@ -65,7 +65,8 @@ def install_reference_oracle():
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True,
+                    help="checkout of the reference project (read only)")
     args = ap.parse_args()
     sys.path.insert(0, os.path.abspath(args.reference))
     install_reference_oracle()

@@ -115,7 +115,7 @@ def _mixed_from_rows(name, seed, Hq, Hkv, NB, rows, poison, dtype=torch.bfloat16
 def mixed_page_reuse(round_id):
     """tests/test_v1_attention_gpu.py:42-81 geometry: decode with history 256 (+1),
     prefill with 255 cached tokens + a 3-token chunk, pages in reverse order;
-    round 1 changes the page mapping and re-poisons the pool."""
+    the second pass (round_id 1) changes the page mapping and re-poisons the pool."""
     tables = [[3, 1], [2, 0]] if round_id == 0 else [[0, 2], [1, 3]]
     rows = [(256, 1, tables[0], "decode"), (255, 3, tables[1], "prefill")]
     return _mixed_from_rows(f"mixed_page_reuse_{round_id}", 100 + 50 * round_id, 8, 2, 4, rows,
