@@ -205,6 +205,29 @@ def fill_fp8_pool(kv, scales, blocks, gen, std, outliers):
                 del x, q
 
 
+def decode_config(args, n):
+    """The `config` of the decode workload (configs 2 / 4) at N GPUs, computed
+    from the seeded metadata alone, so both arms of the bench print the same
+    dict whatever device they run on."""
+    fp8 = args.kv == "fp8"
+    B, lens, pages, _ = make_metadata(n, batch_per_gpu=args.batch, lo=args.ctx_lo,
+                                      hi=args.ctx_hi)
+    hkv = HKV // n
+    kv_bytes = int(lens.to(torch.int64).sum()) * hkv * D * (1 if fp8 else 2) * 2
+    return {
+        "workload": ("BASELINE config 4: FP8-E4M3 KV decode step, 36 layers of "
+                     "quantising append + fused-dequant GQA-4 paged decode"
+                     if fp8 else
+                     "BASELINE config 2: pure decode step, 36 layers of kv_append + "
+                     "GQA-4 paged decode, Qwen3-4B KV geometry"),
+        "batch_per_gpu": args.batch, "global_batch": B, "layers": args.layers,
+        "kv_heads_per_gpu": hkv, "q_heads_per_gpu": HQ // n, "head_dim": D,
+        "block_size": BS, "context": f"U[{args.ctx_lo},{args.ctx_hi}]",
+        "kv_cache": "fp8_e4m3" if fp8 else "bf16",
+        "parallelism": f"tp{n} over KV heads (weak: global batch {args.batch}*N)",
+        "l2": "inputs larger than L2: ~%.2f GB of K/V read per layer" % (kv_bytes / 1e9)}
+
+
 def decode_bytes(wl):
     """Algorithmic HBM bytes of one paged_decode launch (one layer)."""
     ctx = int(wl["lens_cpu"].to(torch.int64).sum())
@@ -382,8 +405,8 @@ def run_ours(args):
         step_gbs = step_bytes / (ms * 1e-3) / 1e9
         tok_s = B / (ms * 1e-3)
         traffic = None
+        name = "paged_decode_fp8_traffic.json" if wl["fp8"] else "paged_decode_traffic.json"
         try:
-            name = "paged_decode_fp8_traffic.json" if wl["fp8"] else "paged_decode_traffic.json"
             with open(os.path.join(ROOT, "profiles", name)) as f:
                 tr = json.load(f)
             # the captures were taken on the one-GPU configurations 2 and 4 only
@@ -400,20 +423,10 @@ def run_ours(args):
                      "with scale amax/448" if wl["fp8"] else "synthetic: K/V ~ 0.5*N(0,1)")
                     + f", Q ~ N(0,1), context ~ U[{args.ctx_lo},"
                     f"{args.ctx_hi}], random block assignment (seeded)",
-            "config": {
-                "workload": ("BASELINE config 4: FP8-E4M3 KV decode step, 36 layers of "
-                             "quantising append + fused-dequant GQA-4 paged decode"
-                             if wl["fp8"] else
-                             "BASELINE config 2: pure decode step, 36 layers of kv_append + "
-                             "GQA-4 paged decode, Qwen3-4B KV geometry"),
-                "batch_per_gpu": args.batch, "global_batch": B, "layers": L,
-                "kv_heads_per_gpu": wl["hkv"], "q_heads_per_gpu": wl["hq"], "head_dim": D,
-                "block_size": BS, "context": f"U[{args.ctx_lo},{args.ctx_hi}]",
-                "pool_blocks": wl["NB"],
-                "pool_gib": round(wl["NB"] * wl["block_bytes"] / 2 ** 30, 1),
-                "parallelism": f"tp{n} over KV heads (weak: global batch {args.batch}*N)",
-                "l2": "inputs larger than L2: %.2f GB of K/V read per layer" % (dbytes / 1e9),
-                "graph": "one CUDA graph per step (append + decode for every layer)"},
+            "config": decode_config(args, n),
+            "setup": {"pool_blocks": wl["NB"],
+                      "pool_gib": round(wl["NB"] * wl["block_bytes"] / 2 ** 30, 1),
+                      "graph": "one CUDA graph per step (append + decode for every layer)"},
             "hbm": {"step_gbs": round(step_gbs, 1),
                     "frac_of_8tbs": round(step_gbs / NOMINAL_HBM_GBS, 4),
                     "frac_of_measured": round(step_gbs / peak, 4),
@@ -423,7 +436,11 @@ def run_ours(args):
                          "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "peak_kind": peak_kind, "frac_of_8tbs": round(achieved / NOMINAL_HBM_GBS, 4),
                          "algorithmic_bytes": dbytes, "launch_ms": round(dec_ms, 5),
-                         "traffic": traffic},
+                         "traffic": traffic,
+                         "traffic_source": (f"profiles/{name}: dram__bytes_read.sum + "
+                                            "dram__bytes_write.sum per launch from a recorded ncu "
+                                            "capture of this kernel on this configuration (not "
+                                            "measured in this run)") if traffic else None},
             "gpu_launches": args.steps * L * 3,
             "clocks": clocks.summary(),
             "device_errors": errs,
@@ -1047,7 +1064,13 @@ def peak_kind_str(kind):
 def run_reference(args):
     """--impl reference: the reference's torch path for the hot path, as restated
     by the oracle, on the host cores (the reference has no CPU kernel of its own
-    to build).  Rank 0 only; other ranks exit without work."""
+    to build).  Rank 0 only; other ranks exit without work.
+
+    One timed step is a bounded sample of the decode step: ONE layer (append +
+    decode) of the 256-sequence batch, so `ms_per_step` is that layer's measured
+    time and `layers_timed_per_step` says so; `value` scales it to the whole
+    36-layer step (batch / (36 x layer time)).  Under weak scaling the N-GPU job
+    is N such batches, so the CPU rate is the same at every N."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
@@ -1063,17 +1086,19 @@ def run_reference(args):
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "tok/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(t * LAYERS * 1e3, 2), "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": round(t * 1e3, 2), "layers_timed_per_step": 1,
+        "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded), as the GPU arm",
-        "config": {"workload": "BASELINE config 2 decode step (append + decode per layer), "
-                               "one layer timed per step and scaled to 36 layers",
-                   "batch": B, "layers": LAYERS, "context": f"U[{CTX_LO},{CTX_HI}]",
-                   "block_size": BS},
+        "config": decode_config(args, args.gpus),
         "cpu_baseline": {"value": round(value, 3), "unit": "tok/s",
                          "cores": torch.get_num_threads(), "kind": "port",
-                         "sample": f"one layer of a {B}-sequence batch per step"},
+                         "sample": f"each step: one layer (append + decode) of a {B}-sequence "
+                                   f"batch, context U[{CTX_LO},{CTX_HI}], fp32 oracle "
+                                   f"arithmetic; value = batch / (36 x mean layer time)"},
         "e2e": {"value": round(value, 3), "unit": "tok/s", "h2d_bytes_per_step": 0,
-                "d2h_bytes_per_step": 0},
+                "d2h_bytes_per_step": 0,
+                "note": "CPU implementation: inputs and outputs stay in host memory, "
+                        "so there are no host-device copies to time"},
     }
     print(json.dumps(line), flush=True)
 

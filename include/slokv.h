@@ -188,10 +188,15 @@ int slokv_qk_norm_rope_append(const void *qkv, int64_t qkv_row_stride, int32_t n
  * Pool: codes uint8 [num_blocks, block_size, num_kv_heads, head_dim] (one tensor
  * for K, one for V, as in the bf16 layout) and fp32 scales [num_blocks,
  * num_kv_heads] for K and for V.  A scale of 0 means "nothing nonzero stored
- * yet"; zero a block's scales when the block is (re)assigned to a sequence.
+ * yet".  The scales need no reset when a block is (re)assigned: a write that
+ * starts at offset 0 of a block ignores the stored scale (a block's first
+ * token always lands at offset 0, and shared prefix blocks are full and never
+ * written), so a reused page never inherits its previous owner's amax and the
+ * block manager (nanovllm/engine/block_manager.py:43-92) stays unchanged.
  * The reference has the E4M3FN codec (benchmarks/v0/probe_quant_support.py:24-56)
  * but no quantised KV path; this is the per-(block, kv-head) contract of the
  * north star, written out in oracle/kv_oracle.py (fp8_append):
+ *   s_old = 0 if the block's new tokens start at offset 0, else the stored scale;
  *   s_new = max(s_old, amax(new tokens of the block, this head) / 448);
  *   if s_new > s_old > 0 the block/head's earlier positions are re-encoded as
  *   encode(fp32(decode(c) * s_old) / s_new); new tokens get encode(x / s_new)
@@ -298,9 +303,11 @@ int slokv_fp8_e4m3_decode(const uint8_t *codes, float *x, int64_t n, void *strea
  * freed or zeroed per call.
  *
  * Limits and rules:
- *  - a geometry whose partials exceed the scratch (on a 148-SM B200: more than
- *    8 query heads per KV head) returns SLOKV_ERR_SCRATCH_LIMIT and launches
- *    nothing;
+ *  - the partials take SMs x 3 x (2 x G x 132 x 4 + 16) bytes for G query
+ *    heads per KV head; a call that slokv_paged_decode would run but whose
+ *    partials exceed the scratch (on a 148-SM B200: G > 13) returns
+ *    SLOKV_ERR_SCRATCH_LIMIT and launches nothing; every other argument error
+ *    returns the same status as slokv_paged_decode;
  *  - the first call on a device looks up the array's device address
  *    (cudaGetSymbolAddress) with that device current, so make the first call
  *    on each device before any stream capture;

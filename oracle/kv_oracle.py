@@ -253,7 +253,12 @@ def decode_e4m3fn_array(codes: np.ndarray) -> np.ndarray:
 #   * an append call groups the new tokens of one block (they are adjacent in
 #     slot_mapping with consecutive offsets, as the engine produces them).
 #     a = max |fp32(x)| over those tokens and the head's D dims;
-#     s_new = max(s_old, fp32(a / 448)).
+#     s_new = max(s_old, fp32(a / 448)), where s_old is the stored scale, or 0
+#     when the group starts at offset 0 of the block: a block's first token is
+#     always written at offset 0 and shared prefix blocks are full and
+#     read-only (nanovllm/engine/block_manager.py:43-92 hands out blocks and
+#     never writes a shared one), so a write at offset 0 means the page was
+#     (re)assigned and whatever scale it holds belongs to its previous owner.
 #   * if s_new > s_old > 0, every existing position p < (first new offset) of
 #     that block/head is re-encoded: c' = encode(fp32(decode(c) * s_old) / s_new).
 #   * new tokens: c = encode(fp32(x) / (s_new if s_new > 0 else 1)).
@@ -288,7 +293,7 @@ def fp8_append(key, value, k_codes, v_codes, k_scale, v_scale, slot_mapping) -> 
             sb = scales[blk].numpy()                          # view [H]
             for h in range(H):
                 amax = np.float32(np.abs(run[:, h, :]).max())
-                s_old = np.float32(sb[h])
+                s_old = np.float32(0.0) if off == 0 else np.float32(sb[h])
                 s_new = np.maximum(s_old, np.float32(amax / np.float32(448.0)))
                 if s_new > s_old and s_old > 0 and off > 0:
                     old = decode_e4m3fn_array(cb[:off, h, :])

@@ -6,7 +6,12 @@
 // "amax = 0 -> scale = 1" rule of the reference manual):
 //   * the new tokens of one block in one call are adjacent in slot_mapping with
 //     consecutive offsets (how the engine lays out decode and prefill slots);
-//   * a = max |x| over those tokens and the head's dims; s_new = max(s_old, a / 448);
+//   * a = max |x| over those tokens and the head's dims; s_new = max(s_old, a / 448),
+//     where s_old is the stored scale, or 0 when the run starts at offset 0 of
+//     the block (a block's first token is always written at offset 0 and a
+//     shared prefix block is full and never written, so a write at offset 0
+//     means the page was handed to a new sequence: its stored scale is stale
+//     and no caller has to clear it);
 //   * if s_new > s_old > 0, the block/head's positions before the first new
 //     offset are re-encoded: c' = encode(fp32(decode(c) * s_old) / s_new);
 //   * new tokens: c = encode(fp32(x) / (s_new > 0 ? s_new : 1)); store s_new.
@@ -115,7 +120,7 @@ __global__ void __launch_bounds__(256, 2) kv_append_fp8_kernel(
   for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
 
   float *sp = scales + static_cast<int64_t>(blk) * hkv + h;
-  const float s_old = *sp;
+  const float s_old = off == 0 ? 0.f : *sp;   // offset 0: a freshly assigned page
   const float s_new = fmaxf(s_old, __fdiv_rn(amax, 448.0f));
   bool bad = false;
   uint8_t *base = codes + static_cast<int64_t>(blk) * block_size * row + h * kHeadDim + d0;
@@ -168,7 +173,8 @@ __global__ void __launch_bounds__(256, 2) kv_append_fp8_kernel(
 // K|V) word with atomicMax on the float bits (non-negative floats order like
 // their bit patterns, so the word ends as the exact run amax); (2) each warp
 // derives s_new = max(s_old, amax / 448) -- the same value for every warp of
-// the run -- and encodes its token; the run's first warp re-encodes the block's
+// the run, s_old being 0 for a run that starts at offset 0 -- and encodes its
+// token; the run's first warp re-encodes the block's
 // earlier positions when the scale grows; (3) the run's first warp stores s_new
 // and clears the word.  Codes and scales are the one-launch kernel's, bit for
 // bit.  `amax_ws` is num_blocks * hkv * 2 words, zero between calls.
@@ -238,7 +244,12 @@ __global__ void __launch_bounds__(256, 2) kv_append_fp8_encode_kernel(
   const RunToken tk = run_token(slots, i, block_size, static_cast<int64_t>(num_blocks) * block_size);
   if (!tk.valid) return;
   const int64_t si = static_cast<int64_t>(tk.blk) * hkv + h;
-  const float s_old = (which ? v_scale : k_scale)[si];
+  // The run starts at offset 0 (a freshly assigned page, stored scale ignored)
+  // iff the token tk.off places earlier holds offset 0 of the same block: runs
+  // are adjacent with consecutive offsets and a block has one run per call.
+  const bool fresh = i >= tk.off && __ldg(slots + i - tk.off) ==
+                                        static_cast<int64_t>(tk.blk) * block_size;
+  const float s_old = fresh ? 0.f : (which ? v_scale : k_scale)[si];
   const float s_new = fmaxf(s_old, __fdiv_rn(__uint_as_float(amax_ws[si * 2 + which]), 448.0f));
   const int64_t row = static_cast<int64_t>(hkv) * kHeadDim;
   const int d0 = lane * 4;
@@ -288,7 +299,7 @@ __global__ void __launch_bounds__(256) kv_append_fp8_commit_kernel(
   if (!tk.valid || !tk.start) return;
   const int64_t si = static_cast<int64_t>(tk.blk) * hkv + h;
   float *sp = (which ? v_scale : k_scale) + si;
-  *sp = fmaxf(*sp, __fdiv_rn(__uint_as_float(amax_ws[si * 2 + which]), 448.0f));
+  *sp = fmaxf(tk.off == 0 ? 0.f : *sp, __fdiv_rn(__uint_as_float(amax_ws[si * 2 + which]), 448.0f));
   amax_ws[si * 2 + which] = 0u;
 }
 

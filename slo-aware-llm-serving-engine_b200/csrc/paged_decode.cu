@@ -1031,14 +1031,26 @@ extern "C" int slokv_paged_decode_noalloc(void *out, int64_t out_stride_b, int64
   using namespace slokv::decode;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return SLOKV_ERR_CUDA;
-  // The scratch holds the per-warp split-K partials; reject geometries whose
-  // partials would not fit before touching anything.
+  // The scratch holds the per-warp split-K partials: SMs x 3 warp slots x
+  // (2 x group x 132 x 4 + 16) bytes, so on a 148-SM B200 up to 13 query heads
+  // per KV head fit in 6 MiB.  For a geometry that does not fit, the workspace
+  // entry point is asked with no workspace at all: it runs every argument
+  // check, launches nothing, and answers SLOKV_ERR_WORKSPACE only when the
+  // arguments are otherwise valid -- so both entry points return the same
+  // status for the same arguments, and only a call that would have run gets
+  // SLOKV_ERR_SCRATCH_LIMIT.
   if (num_kv_heads > 0 && num_q_heads > 0 && num_q_heads % num_kv_heads == 0 &&
       head_dim == kD) {
     const int sms = device_sms(dev);
     if (sms <= 0) return SLOKV_ERR_CUDA;
-    if (workspace_bytes_for(sms, num_q_heads / num_kv_heads) > kNoAllocScratchBytes)
-      return SLOKV_ERR_SCRATCH_LIMIT;
+    if (workspace_bytes_for(sms, num_q_heads / num_kv_heads) > kNoAllocScratchBytes) {
+      const int st = slokv_paged_decode(
+          out, out_stride_b, out_stride_h, q, q_stride_b, q_stride_h, k_cache, v_cache,
+          k_block_stride, v_block_stride, num_blocks, block_size, num_q_heads, num_kv_heads,
+          head_dim, block_tables, block_table_stride, max_blocks_per_seq, context_lens, batch,
+          softmax_scale, dtype, nullptr, 0, dev_error, stream);
+      return st == SLOKV_ERR_WORKSPACE ? SLOKV_ERR_SCRATCH_LIMIT : st;
+    }
   }
   void *scratch = nullptr;
   const int rc = noalloc_scratch(dev, &scratch);

@@ -18,8 +18,8 @@
 // the whole tile's fp32 sum, rounds it to 16 bits once (the reference's
 // per-rank F.linear output is rounded the same way) and stages it in shared
 // memory; one thread then
-// pushes the staged 32 KB tile with a single bulk copy (cp.async.bulk, no
-// multicast) into the symmetric buffer of the tile's owner rank (tile % world)
+// pushes the staged 32 KB tile with a single plain bulk copy (cp.async.bulk,
+// shared to global) into the symmetric buffer of the tile's owner rank (tile % world)
 // over NVLink peer memory.  The MMA of the next tile overlaps the epilogue of
 // this one.  When its last tile is out, the CTA waits for its copies, issues
 // ONE system-scope fence and sets the owners' flags with relaxed stores (a
@@ -41,7 +41,8 @@
 // over NVLink per rank, the ring all-reduce volume, but with one hop each and
 // with the first shot overlapping the GEMM tile by tile.  Every rank ends with
 // bit-identical Y.  All loads are from this GPU's own memory (X, W, its
-// symmetric buffer); only stores cross NVLink.  No TMA multicast is used.
+// symmetric buffer); only stores cross NVLink.  Every TMA load is a plain
+// single-CTA load of local memory.
 //
 // The world size is a template parameter (1, 2, 4 or 8: the TP sizes of the
 // 8-KV-head model), so the per-source loops unroll into independent loads.

@@ -11,8 +11,10 @@ kv_cache[0, l] / kv_cache[1, l].
 
 FP8-E4M3 pools keep uint8 codes in the same layout plus fp32 scales
 k_scale/v_scale [num_layers, num_blocks, Hkv_local]; block_bytes counts the
-scales, and a block's scales are zeroed when the block is handed to a new
-sequence (reset_blocks), so a reused page never inherits an old amax.
+scales.  A reused page never inherits an old amax without any call from the
+block manager: the quantising append ignores a block's stored scale when its
+write starts at offset 0, where every newly assigned block is first written
+(reset_blocks remains as an eager helper for tools that want clean scales).
 """
 from __future__ import annotations
 
@@ -108,7 +110,9 @@ class KVPool:
         return layer
 
     def reset_blocks(self, block_ids: torch.Tensor) -> None:
-        """Zero the FP8 scales of blocks handed to a new sequence (no-op for bf16)."""
+        """Zero the FP8 scales of `block_ids` (no-op for bf16).  Optional: the
+        append already treats a block whose write starts at offset 0 as fresh,
+        so the engine's block manager never has to call this."""
         if self.k_scale is not None and block_ids.numel():
             idx = block_ids.to(device=self.k_scale.device, dtype=torch.long)
             self.k_scale[:, idx] = 0

@@ -76,3 +76,27 @@ def test_separate_runs_per_block_and_skipped_slots():
     # block 2 holds tokens 4, 5 at offsets 88, 89
     amax = np.abs(x[4:6].float().numpy()).max(axis=(0, 2))
     np.testing.assert_array_equal(ks[2].numpy(), (amax / np.float32(448)).astype(np.float32))
+
+
+def test_write_at_offset_zero_ignores_a_stale_scale():
+    """A page handed to a new sequence keeps its previous owner's scale in the
+    pool (the block manager does not touch scales); the first write, which is
+    always at offset 0, must not inherit it.  A later write at offset > 0 keeps
+    the running amax of the new owner only."""
+    kc, vc, ks, vs = _pool()
+    big = kv_values(4, (256, 2, 128)).float() * 40                     # old owner: large amax
+    O.fp8_append(big.bfloat16(), big.bfloat16(), kc, vc, ks, vs, torch.arange(256, dtype=torch.int32))
+    stale = ks[0].clone()
+    small = kv_values(5, (10, 2, 128))
+    O.fp8_append(small, small, kc, vc, ks, vs, torch.arange(10, dtype=torch.int32))
+    amax = np.abs(small.float().numpy()).max(axis=(0, 2))
+    fresh = (amax / np.float32(448)).astype(np.float32)
+    np.testing.assert_array_equal(ks[0].numpy(), fresh)
+    assert (ks[0] < stale).all()
+    # codes of the new tokens are encoded against the fresh scale
+    expect = O.encode_e4m3fn_array((small.float().numpy() / fresh[None, :, None]).astype(np.float32))
+    np.testing.assert_array_equal(kc[0, :10].numpy(), expect)
+    # a decode token at offset 10 keeps the new owner's running scale
+    more = kv_values(6, (1, 2, 128)) * 0.1
+    O.fp8_append(more, more, kc, vc, ks, vs, torch.tensor([10], dtype=torch.int32))
+    np.testing.assert_array_equal(ks[0].numpy(), fresh)

@@ -286,3 +286,46 @@ def test_fp8_mixed_step_with_history_matches_oracle(pkg, dec_lens, pre_rows, see
     exp_p = O.varlen(c["q"][d:], O.fp8_dequant(ref[0], ref[2]), O.fp8_dequant(ref[1], ref[3]),
                      m["prefill_cu_q"], m["prefill_cu_k"], scale, m["prefill_tables"])
     assert_fp8_close(out[d:], exp_p)
+
+
+@pytest.mark.parametrize("runs", [False, True])
+def test_reused_block_ignores_stale_scale_without_reset(pkg, runs):
+    """Blocks freed by one sequence and handed to another keep their old codes
+    and their large scales in the pool; nothing resets them (the reference's
+    block manager has no hook for it).  The new owner's prefill starts at offset
+    0, so codes and scales must come out exactly as on a fresh page: bit-exact
+    with the oracle, scale == fresh amax / 448.  Then decode appends into the
+    same blocks keep the new owner's running scale."""
+    H, D, bs, NB = 8, 128, 256, 10
+    ref = _pools(NB, H=H)
+    dev = _gpu(ref)
+    # old owner fills blocks 3 and 7 with x40 data: large stale scales
+    old_slots = torch.tensor([3 * bs + p for p in range(bs)] + [7 * bs + p for p in range(100)],
+                             dtype=torch.int32)
+    xo = (kv_values(90, (old_slots.numel(), H, D)).float() * 40).bfloat16()
+    O.fp8_append(xo, xo, *ref, old_slots)
+    pkg.store_kvcache_fp8(xo.cuda(), xo.cuda(), *dev, old_slots.cuda(), runs=runs)
+    _assert_pool_equal(dev, ref)
+    stale = ref[2].clone()
+    # new owner: table [7, 3], a 300-token prompt (block 7 full, 44 tokens of block 3)
+    table = [7, 3]
+    slots = torch.tensor([table[p // bs] * bs + p % bs for p in range(300)], dtype=torch.int32)
+    x = kv_values(91, (300, H, D))
+    y = kv_values(92, (300, H, D))
+    O.fp8_append(x, y, *ref, slots)
+    pkg.store_kvcache_fp8(x.cuda(), y.cuda(), *dev, slots.cuda(), runs=runs)
+    _assert_pool_equal(dev, ref)
+    for blk, (a, b) in ((7, (0, 256)), (3, (256, 300))):
+        for src, sc in ((x, dev[2]), (y, dev[3])):
+            amax = np.abs(src[a:b].float().numpy()).max(axis=(0, 2))
+            np.testing.assert_array_equal(sc[blk].cpu().numpy(), (amax / np.float32(448)).astype(np.float32))
+    assert (dev[2][3].cpu() < stale[3]).all() and (dev[2][7].cpu() < stale[7]).all()
+    # decode appends at offsets 44.. of block 3 keep the running scale (no reset)
+    for step in range(5):
+        p = 300 + step
+        st = torch.tensor([table[p // bs] * bs + p % bs], dtype=torch.int32)
+        xs = kv_values(95 + step, (1, H, D), outlier_frac=0.05)
+        O.fp8_append(xs, xs, *ref, st)
+        pkg.store_kvcache_fp8(xs.cuda(), xs.cuda(), *dev, st.cuda(), runs=runs)
+    _assert_pool_equal(dev, ref)
+    assert pkg.read_device_errors() == 0

@@ -1,0 +1,172 @@
+"""Full-model greedy decode: the reference's own GPU attention against this
+package's, on the same random-init Qwen3-4B.
+
+Arm R is the reference's stock attention path, `Attention.forward`
+(nanovllm/layers/attention.py:59-79): store the step's K/V into the paged
+pool, then flash-attn's `flash_attn_varlen_func` for prefill and
+`flash_attn_with_kvcache` for decode (flash-attn 2.8.3, the reference's pinned
+third-party dependency, which runs on the B200).  The store is this package's
+`store_kvcache`, whose caches are bit-identical to the reference's Triton store
+(tests/test_gpu_append_copy.py checks them against the SHA-256 of the Triton
+kernel's output).  Arm O is this package's `Attention` bound in the same
+place: paged append, tcgen05 prefill, paged decode, decode step captured in a
+CUDA graph.
+
+Both arms run the same `qwen3_harness.Qwen3Model` weights (config-5 geometry:
+36 layers, hidden 2560, N(0, 0.02), tied LM head); its layer code is pinned to
+the reference's `Qwen3ForCausalLM` on the CPU (tests/test_model_pin_cpu.py), so
+the arms differ only in attention.  Greedy = argmax of the bf16 logits, as the
+reference's mixed runner samples (nanovllm/engine/mixed_model_runner.py:125-126).
+
+Random-init bf16 logits tie often: the top logit (~4.5) has a bf16 spacing of
+2^-5, and two candidates inside a few spacings of each other are common, so a
+token may flip wherever the reference's own top-2 margin is within the two
+attentions' rounding difference.  The bar, following the north star's 100 %
+token match: every step whose reference top-2 margin exceeds MARGIN_BOUND
+matches exactly -- teacher-forced over all steps, and free-running up to each
+sequence's first tie -- and every tie is logged.
+"""
+import importlib
+
+import pytest
+import torch
+
+from tests.golden.detgen import det_ints
+
+pytestmark = pytest.mark.gpu
+
+STEPS = 32
+BATCH = 64
+MARGIN_BOUND = 0.125       # 4 bf16 spacings of the top logit
+H = "slo-aware-llm-serving-engine_b200.qwen3_harness"
+CTX = "slo-aware-llm-serving-engine_b200.utils.context"
+
+
+class ReferenceAttention(torch.nn.Module):
+    """The reference's Attention.forward with its flash-attn calls, for the
+    bf16 prefill / decode steps the greedy runner makes."""
+
+    def __init__(self, pkg, num_heads, head_dim, scale, num_kv_heads):
+        super().__init__()
+        from flash_attn import flash_attn_varlen_func, flash_attn_with_kvcache
+        self.varlen, self.decode = flash_attn_varlen_func, flash_attn_with_kvcache
+        self.store = pkg.store_kvcache
+        self.num_heads, self.head_dim, self.scale = num_heads, head_dim, scale
+        self.num_kv_heads = num_kv_heads
+        self.k_cache = self.v_cache = torch.tensor([])
+        self.k_scale = self.v_scale = None
+
+    def forward(self, q, k, v):
+        context = importlib.import_module(CTX).get_context()
+        k_cache, v_cache = self.k_cache, self.v_cache
+        if k_cache.numel() and v_cache.numel():
+            self.store(k, v, k_cache, v_cache, context.slot_mapping)
+        if context.is_prefill:
+            if context.block_tables is not None:
+                k, v = k_cache, v_cache
+            return self.varlen(q, k, v, max_seqlen_q=context.max_seqlen_q,
+                               cu_seqlens_q=context.cu_seqlens_q,
+                               max_seqlen_k=context.max_seqlen_k,
+                               cu_seqlens_k=context.cu_seqlens_k, softmax_scale=self.scale,
+                               causal=True, block_table=context.block_tables)
+        return self.decode(q.unsqueeze(1), k_cache, v_cache, cache_seqlens=context.context_lens,
+                           block_table=context.block_tables, softmax_scale=self.scale,
+                           causal=True)
+
+
+def _prompts(vocab):
+    lens = det_ints(5150, BATCH, 512, 4096).tolist()
+    ids = det_ints(5151, sum(lens), 0, vocab - 1).tolist()
+    prompts, cur = [], 0
+    for n in lens:
+        prompts.append(ids[cur:cur + n])
+        cur += n
+    return lens, prompts
+
+
+def _run(h, model, lens, prompts, feed=None, use_graph=False, keep_logits=False):
+    """Greedy run of STEPS tokens.  feed: [B, STEPS] tokens to append instead of
+    the run's own (teacher forcing).  Returns tokens [B, STEPS] and, when asked,
+    the bf16 logits of every step (list of [B, vocab])."""
+    logits = []
+    if keep_logits:
+        def record(hid):
+            lg = h.Qwen3Model.logits(model, hid)
+            logits.append(lg)
+            return lg
+        model.logits = record
+    runner = h.GreedyRunner(model, lens, STEPS, seed=1)
+    cur = runner.prefill(prompts, chunk_tokens=32768)
+    if keep_logits:            # one logits call per prefill chunk: one entry for the step
+        logits[:] = [torch.cat(logits)]
+    toks = [cur]
+    for t in range(STEPS - 1):
+        cur = runner.decode(cur if feed is None else feed[:, t].cuda(), use_graph=use_graph)
+        toks.append(cur)
+    torch.cuda.synchronize()
+    if keep_logits:
+        del model.logits
+    runner.release()
+    del runner
+    torch.cuda.empty_cache()
+    return torch.stack(toks, dim=1).cpu(), logits
+
+
+def _margins(logits):
+    """Reference top-2 margin of every (sequence, step): [B, STEPS]."""
+    return torch.stack([(lambda v: v[:, 0] - v[:, 1])(lg.float().topk(2, dim=-1).values)
+                        for lg in logits], dim=1).cpu()
+
+
+def test_greedy_tokens_match_reference_flash_attn_model(pkg):
+    h = importlib.import_module(H)
+    cfg = h.Qwen3Config()
+    model = h.Qwen3Model(cfg, seed=21, device="cuda", fused_qk_norm_rope=False)
+    lens, prompts = _prompts(cfg.vocab_size)
+    ours = [lw.attn for lw in model.layers]
+    for lw in model.layers:
+        lw.attn = ReferenceAttention(pkg, model.hq, cfg.head_dim, cfg.head_dim ** -0.5, model.hkv)
+
+    # arm R: the reference's flash-attn path, free-running
+    ref_tok, ref_logits = _run(h, model, lens, prompts, keep_logits=True)
+    margin = _margins(ref_logits)
+    for lw, a in zip(model.layers, ours):
+        lw.attn = a
+
+    # arm O, teacher-forced on R's tokens (eager, so every step's logits are kept)
+    tf_tok, tf_logits = _run(h, model, lens, prompts, feed=ref_tok, keep_logits=True)
+    delta = torch.stack([(a.float() - b.float()).abs().amax(dim=-1)
+                         for a, b in zip(tf_logits, ref_logits)], dim=1).cpu()
+    del tf_logits, ref_logits
+    flips = tf_tok != ref_tok
+    tf_rate = 1.0 - flips.float().mean().item()
+    for b, t in flips.nonzero().tolist():
+        print(f"teacher-forced tie: seq {b} step {t}: reference margin {margin[b, t]:.4f}, "
+              f"max |logit difference| {delta[b, t]:.4f}")
+    print(f"teacher-forced agreement {tf_rate:.4f} over {flips.numel()} steps; max |logit "
+          f"difference| {delta.max().item():.4f}; reference margin <= {MARGIN_BOUND} at "
+          f"{(margin <= MARGIN_BOUND).float().mean().item():.4f} of steps")
+
+    # arm O free-running, decode step captured in a CUDA graph (the product path)
+    free_tok, _ = _run(h, model, lens, prompts, use_graph=True)
+    assert pkg.read_device_errors() == 0
+    matched, ties = 0, []
+    for b in range(BATCH):
+        diff = (free_tok[b] != ref_tok[b]).nonzero()
+        first = int(diff[0]) if diff.numel() else STEPS
+        matched += first
+        if first < STEPS:
+            ties.append((b, first, margin[b, first].item()))
+            # up to its first tie the free run saw the same history as the
+            # teacher-forced one, so it takes the same token there
+            assert free_tok[b, first] == tf_tok[b, first], (b, first)
+    for b, t, m in ties:
+        print(f"free-running tie: seq {b} leaves the reference at step {t}, margin {m:.4f}")
+    print(f"free-running: {matched} of {BATCH * STEPS} tokens ({matched / (BATCH * STEPS):.4f}) "
+          f"before each sequence's first tie; {BATCH - len(ties)} of {BATCH} sequences identical")
+
+    assert (margin[flips] <= MARGIN_BOUND).all(), (
+        f"a teacher-forced token differs at reference margin {margin[flips].max().item():.4f}")
+    assert all(m <= MARGIN_BOUND for _, _, m in ties), ties
+    assert tf_rate >= 0.9
+    model.close()

@@ -6,14 +6,16 @@ has already handed most of HBM to the KV pool -- so its split-K scratch is a
 fixed device array inside the library instead of a caller-supplied workspace.
 This test calls it through the C ABI twice in a row, on different inputs, and
 checks each result against the workspace entry point (slokv_paged_decode,
-reached through flash_attn_with_kvcache) with the decode tolerance used by every
-attention test: max |err| <= 2e-2, mean |err| <= 2e-3.  The file sorts last so
-that a run stopping at its first failure has already run every other test.
+reached through flash_attn_with_kvcache) and against the CPU oracle of the
+reference's attention, with the decode tolerance used by every attention test:
+max |err| <= 2e-2, mean |err| <= 2e-3.  The file sorts last so that a run
+stopping at its first failure has already run every other test.
 """
 import numpy as np
 import pytest
 import torch
 
+from oracle import kv_oracle as O
 from tests.golden.detgen import det_ints, det_normal, det_perm
 
 pytestmark = pytest.mark.gpu
@@ -66,15 +68,19 @@ def test_noalloc_decode_matches_workspace_entry_point(pkg):
         assert torch.isfinite(out.float()).all()
         diff = (out.float() - expect.float()).abs()
         assert diff.max().item() <= MAX_TOL and diff.mean().item() <= MEAN_TOL
+        oracle = O.decode(q.cpu(), kc.cpu(), vc.cpu(), lens.cpu(), tables.cpu(), scale)
+        odiff = (out.float().cpu() - oracle).abs()
+        assert odiff.max().item() <= MAX_TOL and odiff.mean().item() <= MEAN_TOL, (
+            f"vs oracle: max {odiff.max().item():.3e} mean {odiff.mean().item():.3e}")
         assert int(err.item()) == 0
 
 
 def test_noalloc_rejects_geometry_beyond_scratch(pkg):
     lib = pkg._lib.lib()
-    sms = torch.cuda.get_device_properties(0).multi_processor_count
-    # 16 query heads per KV head need 2 * 16 * 132 * 4 bytes per warp slot
-    # (4 warp slots per SM), beyond 6 MiB on a 148-SM part: rejected, nothing launched.
-    if sms * 4 * 2 * 16 * 132 * 4 <= (6 << 20):
+    # 16 query heads per KV head: SMs x 3 warp slots x (2 x 16 x 132 x 4 + 16)
+    # bytes of partials, beyond 6 MiB on a 148-SM part: rejected, nothing launched.
+    need = lib.slokv_paged_decode_workspace_bytes(0, 32, 2, 128)
+    if need <= lib.slokv_paged_decode_noalloc_scratch_bytes():
         pytest.skip("this device's SM count fits group 16 in the scratch")
     q, kc, vc, lens, tables = _case(4300, B=4, Hq=32, Hkv=2)
     out = torch.zeros_like(q)
@@ -84,3 +90,27 @@ def test_noalloc_rejects_geometry_beyond_scratch(pkg):
     assert b"fixed scratch" in lib.slokv_status_string(status)
     torch.cuda.synchronize()
     assert out.abs().sum().item() == 0
+
+
+def test_noalloc_status_matches_workspace_entry_point(pkg):
+    """Arguments the decode itself refuses get the decode's own status, not the
+    scratch-limit one, and an empty batch is a no-op, whatever the geometry."""
+    lib = pkg._lib.lib()
+    q, kc, vc, lens, tables = _case(4400, B=4, Hq=32, Hkv=2)
+    out = torch.zeros_like(q)
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    B, _, Hq, D = q.shape
+    NB, bs, Hkv, _ = kc.shape
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def call(batch, hq, hkv):
+        return lib.slokv_paged_decode_noalloc(
+            out.data_ptr(), out.stride(0), out.stride(2), q.data_ptr(), q.stride(0),
+            q.stride(2), kc.data_ptr(), vc.data_ptr(), kc.stride(0), vc.stride(0), NB, bs, hq,
+            hkv, D, tables.data_ptr(), tables.stride(0), tables.shape[1], lens.data_ptr(), batch,
+            0.1, 0, err.data_ptr(), stream)
+
+    assert call(0, 32, 2) == pkg._lib.OK                 # empty batch: nothing to do
+    assert call(B, 34, 2) == pkg._lib.ERR_UNSUPPORTED    # group 17: not built
+    torch.cuda.synchronize()
+    assert out.abs().sum().item() == 0 and int(err.item()) == 0
