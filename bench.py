@@ -396,6 +396,7 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms, dec_ms, e2e_ms = t.tolist()
 
+    line = None
     if rank == 0:
         peak, peak_kind = measured_hbm_peak()
         dbytes = decode_bytes(wl)
@@ -461,8 +462,34 @@ def run_ours(args):
                 fa["ours_ms_per_layer"] = round(dec_ms, 5)
                 fa["speedup"] = round(fa["ms_per_layer"] / dec_ms, 3)
             line["library_decode"] = {"flash_attn_with_kvcache": fa}
-        print(json.dumps(line), flush=True)
     del graph, dgraph
+    if not args.no_model_step and not wl["fp8"]:
+        # The decode path itself has no exchange step (attention is head-local), so
+        # the line also carries the full-model step at TP = N (config 5), whose
+        # o_proj / down_proj all-reduce is the one collective around the path:
+        # fused row-parallel kernel vs cuBLAS + NCCL, both timed on the device.
+        kv = sc = None                       # drop the decode pool (closures hold these cells)
+        wl.clear()
+        torch.cuda.empty_cache()
+        mb = 512 if n > 1 else 256          # batch 512 bf16 does not fit one B200
+        msteps = max(2, min(args.steps, 10))
+        r = measure_model_step(args, rank, n, device, dist, mb, msteps, 3)
+        if rank == 0:
+            sub = {"metric": MODEL_METRIC, "value": round(mb / (r["ms"] * 1e-3), 1),
+                   "unit": "tok/s", "ms_per_step": round(r["ms"], 3), "steps": msteps,
+                   "warmup": 3, "parallelism": f"tp{n}", "global_batch": mb,
+                   "context": f"U[{CTX_LO},{CTX_HI}] after prefill",
+                   "prefill_seconds": round(r["prefill_s"], 2),
+                   "all_reduce": ("fused row-parallel kernel (GEMM + tile exchange over NVLink "
+                                  "peer memory)" if n > 1 else "none (TP = 1)"),
+                   "gpu_launches": r["gpu_launches"], "device_errors": r["errors"],
+                   "clocks": r["clocks"]}
+            if r["nccl_ms"] is not None:
+                sub["cublas_nccl_ms_per_step"] = round(r["nccl_ms"], 3)
+                sub["cublas_nccl_value"] = round(mb / (r["nccl_ms"] * 1e-3), 1)
+            line["model_step"] = sub
+    if rank == 0:
+        print(json.dumps(line), flush=True)
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
@@ -926,15 +953,96 @@ def run_rowpar(args):
 MODEL_METRIC = "full-model greedy decode tokens/s, random-init Qwen3-4B (config 5), TP = n_gpus"
 
 
+def measure_model_step(args, rank, world, device, dist, batch, steps, warmup, kv="bf16",
+                       unfused_qk=False, nccl_all_reduce=False, ctx_lo=CTX_LO, ctx_hi=CTX_HI):
+    """Config 5 at TP = world: build the random-init Qwen3-4B shard of this rank,
+    prefill `batch` prompts of random ids (context U[ctx_lo, ctx_hi]) through the
+    tcgen05 varlen kernel, then time `steps` graph-captured greedy decode steps
+    (o_proj / down_proj + TP all-reduce as the fused row-parallel kernel, or
+    cuBLAS + NCCL); at TP > 1 the same step re-captured with cuBLAS + NCCL is
+    timed right after.  Device-timed, max over ranks.  Returns a dict (the same
+    on every rank)."""
+    h = importlib.import_module("slo-aware-llm-serving-engine_b200.qwen3_harness")
+    pkg = importlib.import_module("slo-aware-llm-serving-engine_b200")
+    cfg = h.Qwen3Config()
+    B = batch
+    gen = torch.Generator().manual_seed(5)
+    lens = torch.randint(ctx_lo, ctx_hi + 1, (B,), generator=gen).tolist()
+    ids = torch.randint(0, cfg.vocab_size, (sum(lens),), generator=gen).tolist()
+    prompts, cur = [], 0
+    for n in lens:
+        prompts.append(ids[cur:cur + n])
+        cur += n
+    model = h.Qwen3Model(cfg, rank, world, None, seed=0, device=device,
+                         fused_qk_norm_rope=not unfused_qk, fused_all_reduce=not nccl_all_reduce)
+    compare = world > 1 and not nccl_all_reduce
+    runner = h.GreedyRunner(model, lens, (warmup + steps) * (2 if compare else 1) + 2,
+                            seed=1, kv_dtype=kv)
+    t0 = time.time()
+    tok = runner.prefill(prompts, chunk_tokens=32768)
+    torch.cuda.synchronize()
+    prefill_s = time.time() - t0
+    for _ in range(warmup):
+        tok = runner.decode(tok)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = Clocks(device)
+    with clocks:
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+        start.record()
+        for _ in range(steps):
+            tok = runner.decode(tok)
+        end.record()
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+    ms = start.elapsed_time(end) / steps
+    errs = pkg.read_device_errors()
+    nccl_ms = 0.0
+    if compare:   # the same step with cuBLAS + NCCL for o_proj / down_proj
+        fused_comm, model.rowpar = model.rowpar, None
+        runner.graph = None
+        for _ in range(warmup):
+            tok = runner.decode(tok)
+        dist.barrier()
+        torch.cuda.synchronize()
+        start.record()
+        for _ in range(steps):
+            tok = runner.decode(tok)
+        end.record()
+        torch.cuda.synchronize()
+        dist.barrier()
+        nccl_ms = start.elapsed_time(end) / steps
+        model.rowpar = fused_comm
+    t = torch.tensor([ms, nccl_ms, prefill_s], device=device)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, nccl_ms, prefill_s = t.tolist()
+    # per-rank HBM bytes of one step: the KV read by attention (mean context
+    # over the timed steps) + the append + this rank's weights
+    ctx = sum(lens) + B * (warmup + steps // 2 + 1)
+    kv_bytes = 2 * cfg.num_layers * ctx * model.hkv * cfg.head_dim * (1 if kv == "fp8" else 2)
+    w_bytes = sum(t.numel() * 2 for lw in model.layers
+                  for t in (lw.wqkv, lw.wo, lw.wgu, lw.wd)) + model.embed.numel() * 2
+    fused = world > 1 and not nccl_all_reduce
+    res = dict(ms=ms, nccl_ms=nccl_ms if compare else None, prefill_s=prefill_s, B=B,
+               kv_bytes=kv_bytes, w_bytes=w_bytes, clocks=clocks.summary(), errors=errs,
+               fused_all_reduce=fused,
+               # per layer: the append (fused with q/k norm + RoPE, or alone), the
+               # decode's main + merge launches, and two fused row-parallel launches
+               gpu_launches=steps * cfg.num_layers * (3 + (2 if fused else 0)))
+    runner.release()
+    model.close()
+    del runner, model
+    torch.cuda.empty_cache()
+    return res
+
+
 def run_model(args):
     """random-init Qwen3-4B (36 layers, N(0, 0.02) weights)
-    decode step at TP = --gpus.  Prompts of random ids with context U[512, 4096]
-    are prefilled through the tcgen05 varlen kernel, then the graph-captured
-    decode step (dense torch + this package's append / paged decode; o_proj and
-    down_proj with their TP all-reduce as the fused row-parallel kernel, or
-    cuBLAS + NCCL with --nccl-all-reduce) is timed; max over ranks.  At TP > 1
-    the step is then re-captured with cuBLAS + NCCL and timed again for
-    comparison (unless --nccl-all-reduce)."""
+    decode step at TP = --gpus (measure_model_step), one JSON line."""
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -948,75 +1056,14 @@ def run_model(args):
 
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=device)
-    h = importlib.import_module("slo-aware-llm-serving-engine_b200.qwen3_harness")
-    pkg = importlib.import_module("slo-aware-llm-serving-engine_b200")
-    cfg = h.Qwen3Config()
-    B = args.batch
-    gen = torch.Generator().manual_seed(5)
-    lens = torch.randint(args.ctx_lo, args.ctx_hi + 1, (B,), generator=gen).tolist()
-    ids = torch.randint(0, cfg.vocab_size, (sum(lens),), generator=gen).tolist()
-    prompts, cur = [], 0
-    for n in lens:
-        prompts.append(ids[cur:cur + n])
-        cur += n
-    model = h.Qwen3Model(cfg, rank, world, None, seed=0, device=device,
-                         fused_qk_norm_rope=not args.unfused_qk,
-                         fused_all_reduce=not args.nccl_all_reduce)
-    compare = world > 1 and not args.nccl_all_reduce
-    runner = h.GreedyRunner(model, lens, (args.warmup + args.steps) * (2 if compare else 1) + 2,
-                            seed=1, kv_dtype=args.kv)
-    t0 = time.time()
-    tok = runner.prefill(prompts, chunk_tokens=32768)
-    torch.cuda.synchronize()
-    prefill_s = time.time() - t0
-    for _ in range(args.warmup):
-        tok = runner.decode(tok)
-    torch.cuda.synchronize()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    clocks = Clocks(device)
-    with clocks:
-        if dist is not None:
-            dist.barrier()
-        torch.cuda.synchronize()
-        start.record()
-        for _ in range(args.steps):
-            tok = runner.decode(tok)
-        end.record()
-        torch.cuda.synchronize()
-        if dist is not None:
-            dist.barrier()
-    ms = start.elapsed_time(end) / args.steps
-    errs = pkg.read_device_errors()
-    nccl_ms = 0.0
-    if compare:   # the same step with cuBLAS + NCCL for o_proj / down_proj
-        fused_comm, model.rowpar = model.rowpar, None
-        runner.graph = None
-        for _ in range(args.warmup):
-            tok = runner.decode(tok)
-        dist.barrier()
-        torch.cuda.synchronize()
-        start.record()
-        for _ in range(args.steps):
-            tok = runner.decode(tok)
-        end.record()
-        torch.cuda.synchronize()
-        dist.barrier()
-        nccl_ms = start.elapsed_time(end) / args.steps
-        model.rowpar = fused_comm
-    t = torch.tensor([ms, nccl_ms], device=device)
-    if dist is not None:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, nccl_ms = t.tolist()
+    r = measure_model_step(args, rank, world, device, dist, args.batch, args.steps, args.warmup,
+                           kv=args.kv, unfused_qk=args.unfused_qk,
+                           nccl_all_reduce=args.nccl_all_reduce, ctx_lo=args.ctx_lo,
+                           ctx_hi=args.ctx_hi)
     if rank == 0:
-        # per-rank HBM bytes of one step: the KV read by attention (mean context
-        # over the timed steps) + the append + this rank's weights
-        ctx = sum(lens) + B * (args.warmup + args.steps // 2 + 1)
-        kv_bytes = 2 * cfg.num_layers * ctx * runner.model.hkv * cfg.head_dim * (
-            1 if args.kv == "fp8" else 2)
-        w_bytes = sum(t.numel() * 2 for lw in model.layers
-                      for t in (lw.wqkv, lw.wo, lw.wgu, lw.wd)) + model.embed.numel() * 2
+        B, ms = r["B"], r["ms"]
         peak, peak_kind = measured_hbm_peak()
-        achieved = (kv_bytes + w_bytes) / (ms * 1e-3) / 1e9
+        achieved = (r["kv_bytes"] + r["w_bytes"]) / (ms * 1e-3) / 1e9
         line = {
             "metric": MODEL_METRIC, "value": round(B / (ms * 1e-3), 1), "unit": "tok/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -1031,27 +1078,22 @@ def run_model(args):
                                       + ("cuBLAS + NCCL" if args.nccl_all_reduce or world == 1
                                          else "fused row-parallel kernel")),
                        "parallelism": f"tp{world}", "global_batch": B,
-                       "prefill_seconds": round(prefill_s, 2)},
+                       "prefill_seconds": round(r["prefill_s"], 2)},
             "roofline": {"kernel": "whole decode step per rank (KV read + weights)",
                          "bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
-                         "peak_kind": peak_kind, "algorithmic_bytes": kv_bytes + w_bytes,
-                         "traffic": None},
-            # per layer: the append (fused with q/k norm + RoPE, or alone), the
-            # decode's main + merge launches, and two fused row-parallel launches
-            "gpu_launches": args.steps * cfg.num_layers * (
-                3 + (2 if world > 1 and not args.nccl_all_reduce else 0)),
-            "clocks": clocks.summary(),
-            "device_errors": errs,
+                         "peak_kind": peak_kind,
+                         "algorithmic_bytes": r["kv_bytes"] + r["w_bytes"], "traffic": None},
+            "gpu_launches": r["gpu_launches"],
+            "clocks": r["clocks"],
+            "device_errors": r["errors"],
         }
-        if compare:
+        if r["nccl_ms"] is not None:
             line["all_reduce_compare"] = {
-                "fused_ms_per_step": round(ms, 3), "nccl_ms_per_step": round(nccl_ms, 3),
+                "fused_ms_per_step": round(ms, 3), "nccl_ms_per_step": round(r["nccl_ms"], 3),
                 "note": "same step re-captured with cuBLAS o_proj/down_proj + NCCL all-reduce, "
                         "timed right after (contexts longer by warmup + steps tokens)"}
         print(json.dumps(line), flush=True)
-    runner.release()
-    model.close()
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
@@ -1127,6 +1169,8 @@ def main():
     ap.add_argument("--unfused-qk", action="store_true",
                     help="model workload: q/k norm + RoPE as torch ops and the plain append")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-model-step", action="store_true",
+                    help="decode workload: skip the config-5 model-step sub-record")
     ap.add_argument("--nccl-all-reduce", action="store_true",
                     help="model workload: cuBLAS o_proj/down_proj + NCCL all-reduce instead of "
                          "the fused row-parallel kernel")

@@ -238,6 +238,35 @@ int slokv_fp8_pages_dequant(const void *k_codes, const void *v_codes, int64_t k_
                             void *dst_k, void *dst_v, float *dst_k_scale, uint32_t *dev_error,
                             void *stream);
 
+/* Prefix-cache prefill over an FP8 pool with the dequantisation fused into the
+ * tile loads (the prefill half of flash_attn_varlen_func / forward_mixed,
+ * nanovllm/layers/attention.py:69-74, nanovllm/layers/mixed_attention.py:123-133,
+ * when the pool is FP8).  Arguments as slokv_paged_prefill with paged K/V, the
+ * pool being k_codes / v_codes (uint8 [num_blocks, block_size, Hkv, 128],
+ * block strides in bytes, 16-byte multiples) and its fp32 scales k_scale /
+ * v_scale [num_blocks, Hkv].  Each 128-key tile of codes is TMA-loaded from its
+ * page and widened in shared memory: K to its unscaled code values (exact in
+ * f16) with the logits of the page's keys multiplied by its K scale, V to
+ * f16(fp32(decode(code)) * V scale); the MMAs run in f16 (a bf16 q is
+ * converted to f16 in the kernel) and out is written in q_dtype (bf16 or
+ * f16).  The same arithmetic as slokv_fp8_pages_dequant followed by
+ * slokv_paged_prefill(f16, k_page_scale), without the page buffer.  Even GQA
+ * groups only, block_size % 128 == 0, max_blocks_per_seq <= 468 (one K scale
+ * per page in shared memory; pass the pages the longest row reaches), else
+ * SLOKV_ERR_UNSUPPORTED.  An id outside the pool loads zero codes (scale 0)
+ * and sets SLOKV_DEVERR_BLOCK_RANGE. */
+int slokv_paged_prefill_fp8(void *out, int64_t out_stride_t, int64_t out_stride_h,
+                            const void *q, int64_t q_stride_t, int64_t q_stride_h, int64_t q_rows,
+                            const void *k_codes, const void *v_codes, int64_t k_block_stride,
+                            int64_t v_block_stride, const float *k_scale, const float *v_scale,
+                            const int32_t *cu_seqlens_q, const int32_t *cu_seqlens_k,
+                            int32_t num_rows, int32_t max_seqlen_q, const int32_t *block_tables,
+                            int64_t block_table_stride, int32_t max_blocks_per_seq,
+                            int32_t num_blocks, int32_t block_size, int32_t num_q_heads,
+                            int32_t num_kv_heads, int32_t head_dim, float softmax_scale,
+                            int32_t q_dtype, void *workspace, size_t workspace_bytes,
+                            uint32_t *dev_error, void *stream);
+
 /* slokv_kv_append_fp8 for calls with long runs (prefill chunks: up to a block
  * of new tokens per (block, kv head)), token-parallel in three launches: each
  * (token, head, K|V) takes its row's amax into a per-(block, head, K|V) word

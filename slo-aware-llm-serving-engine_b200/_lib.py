@@ -67,6 +67,15 @@ SIGNATURES = {
         _c_vp,                                    # k_page_scale (FP8 pools) or None
         _c_vp, _c_sz, _c_vp, _c_vp]),             # workspace, bytes, dev_error, stream
     "slokv_paged_prefill_workspace_bytes": (_c_sz, [_c_i32, _c_i32]),
+    "slokv_paged_prefill_fp8": (ctypes.c_int, [
+        _c_vp, _c_i64, _c_i64,                    # out, token / head strides
+        _c_vp, _c_i64, _c_i64, _c_i64,            # q, strides, rows
+        _c_vp, _c_vp, _c_i64, _c_i64,             # k / v codes, block strides (bytes)
+        _c_vp, _c_vp,                             # k / v scales
+        _c_vp, _c_vp, _c_i32, _c_i32,             # cu_q, cu_k, rows, max_seqlen_q
+        _c_vp, _c_i64, _c_i32, _c_i32, _c_i32,    # tables, stride, width, num_blocks, bs
+        _c_i32, _c_i32, _c_i32, _c_f32, _c_i32,   # Hq, Hkv, D, scale, q dtype
+        _c_vp, _c_sz, _c_vp, _c_vp]),             # workspace, bytes, dev_error, stream
     "slokv_fp8_pages_dequant": (ctypes.c_int, [
         _c_vp, _c_vp, _c_i64, _c_i64, _c_vp, _c_vp,   # codes, block strides, scales
         _c_i32, _c_i32, _c_i32, _c_i32,               # num_blocks, block_size, Hkv, D

@@ -823,6 +823,185 @@ int launch(const Params &p0, const CUtensorMap &km, const CUtensorMap &vm, int s
   return cudaGetLastError() == cudaSuccess ? SLOKV_OK : SLOKV_ERR_CUDA;
 }
 
+// ---- fp32 pool: the reference's fp32 configuration --------------------------
+//
+// q, cache and out in fp32 (the reference engine's fp32 diagnostic runs its
+// whole model, pool included, in fp32).  CUDA-core arithmetic, one CTA per
+// (sequence, KV head) and its G query heads: every K/V row is read once for
+// the group.  Keys go in chunks of 256: thread t scores key t of the chunk for
+// all G heads (its 128-float K row against the group's q in shared memory),
+// each head's chunk max and exponentials update an online softmax, and thread
+// d accumulates output dim d over the chunk's V rows (coalesced 512-byte row
+// reads).  A parity path: HBM traffic is the rows' K and V once; no TMA, no
+// workspace.
+namespace f32dec {
+constexpr int kThreads = 128;
+constexpr int kChunk = 256;
+}  // namespace f32dec
+
+template <int G>
+__global__ void __launch_bounds__(f32dec::kThreads)
+    paged_decode_f32_kernel(float *__restrict__ out, int64_t out_sb, int64_t out_sh,
+                            const float *__restrict__ q, int64_t q_sb, int64_t q_sh,
+                            const float *__restrict__ k_cache, const float *__restrict__ v_cache,
+                            int64_t k_bs, int64_t v_bs, int32_t num_blocks, int32_t block_size,
+                            int32_t hkv, const int32_t *__restrict__ tables, int64_t bt_stride,
+                            int32_t max_blocks, const int32_t *__restrict__ lens, float scale,
+                            uint32_t *err) {
+  using f32dec::kChunk;
+  using f32dec::kThreads;
+  __shared__ float sq[G][kD];
+  __shared__ float ss[G][kChunk];
+  __shared__ float red[2][G][kThreads / 32];
+  const int b = blockIdx.x, hk = blockIdx.y, tid = threadIdx.x;
+  const int lane = tid & 31, warp = tid >> 5;
+  int L = __ldg(lens + b);
+  if (L > static_cast<int64_t>(max_blocks) * block_size) {
+    if (tid == 0) record_error(err, SLOKV_DEVERR_CONTEXT_LEN);
+    L = max_blocks * block_size;
+  }
+  float *orow = out + static_cast<int64_t>(b) * out_sb + static_cast<int64_t>(hk) * G * out_sh;
+  if (L <= 0) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) orow[g * out_sh + tid] = 0.f;
+    return;
+  }
+  const float *qrow = q + static_cast<int64_t>(b) * q_sb + static_cast<int64_t>(hk) * G * q_sh;
+#pragma unroll
+  for (int g = 0; g < G; ++g) sq[g][tid] = __ldg(qrow + g * q_sh + tid);
+  const int32_t *trow = tables + static_cast<int64_t>(b) * bt_stride;
+  const int64_t row_elems = static_cast<int64_t>(hkv) * kD;
+  float acc[G], m_run[G], l_run[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    acc[g] = 0.f;
+    m_run[g] = -INFINITY;
+    l_run[g] = 0.f;
+  }
+  // (block id or -1 outside the pool, offset in the block) of a key
+  auto block_of = [&](int key) {
+    const int page = key / block_size;
+    const int32_t blk = __ldg(trow + page);
+    return make_int2(blk >= 0 && blk < num_blocks ? blk : -1, key - page * block_size);
+  };
+  for (int c0 = 0; c0 < L; c0 += kChunk) {
+    const int n = min(kChunk, L - c0);
+    __syncthreads();                      // q loaded; the previous chunk's P consumed
+    for (int t = tid; t < n; t += kThreads) {
+      const int2 bo = block_of(c0 + t);
+      const int blk = bo.x, off = bo.y;
+      float dot[G];
+#pragma unroll
+      for (int g = 0; g < G; ++g) dot[g] = 0.f;
+      if (blk >= 0) {
+        const float4 *kr = reinterpret_cast<const float4 *>(
+            k_cache + static_cast<int64_t>(blk) * k_bs + off * row_elems + hk * kD);
+#pragma unroll 4
+        for (int d4 = 0; d4 < kD / 4; ++d4) {
+          const float4 kv = __ldg(kr + d4);
+#pragma unroll
+          for (int g = 0; g < G; ++g)
+            dot[g] += sq[g][4 * d4] * kv.x + sq[g][4 * d4 + 1] * kv.y + sq[g][4 * d4 + 2] * kv.z +
+                      sq[g][4 * d4 + 3] * kv.w;
+        }
+      } else {                            // a block id outside the pool reads as zeros
+        record_error(err, SLOKV_DEVERR_BLOCK_RANGE);
+      }
+#pragma unroll
+      for (int g = 0; g < G; ++g) ss[g][t] = dot[g] * scale;
+    }
+    __syncthreads();
+    // chunk max of every head
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      float mx = -INFINITY;
+      for (int t = tid; t < n; t += kThreads) mx = fmaxf(mx, ss[g][t]);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      if (lane == 0) red[0][g][warp] = mx;
+    }
+    __syncthreads();
+    float alpha[G], m_new[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      float mx = red[0][g][0];
+#pragma unroll
+      for (int w = 1; w < kThreads / 32; ++w) mx = fmaxf(mx, red[0][g][w]);
+      m_new[g] = fmaxf(m_run[g], mx);
+      alpha[g] = expf(m_run[g] - m_new[g]);           // 0 on the first chunk
+      m_run[g] = m_new[g];
+    }
+    // P = exp(s - m), its chunk sum, then O += P V (thread tid = output dim)
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      float sum = 0.f;
+      for (int t = tid; t < n; t += kThreads) {
+        const float pv = expf(ss[g][t] - m_new[g]);
+        ss[g][t] = pv;
+        sum += pv;
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      if (lane == 0) red[1][g][warp] = sum;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      float sum = 0.f;
+#pragma unroll
+      for (int w = 0; w < kThreads / 32; ++w) sum += red[1][g][w];
+      l_run[g] = l_run[g] * alpha[g] + sum;
+      acc[g] *= alpha[g];
+    }
+    for (int t = 0; t < n; ++t) {
+      const int2 bo = block_of(c0 + t);
+      const int blk = bo.x, off = bo.y;
+      const float v = blk >= 0 ? __ldg(v_cache + static_cast<int64_t>(blk) * v_bs +
+                                       off * row_elems + hk * kD + tid)
+                               : 0.f;
+#pragma unroll
+      for (int g = 0; g < G; ++g) acc[g] += ss[g][t] * v;
+    }
+  }
+#pragma unroll
+  for (int g = 0; g < G; ++g) orow[g * out_sh + tid] = acc[g] / l_run[g];
+}
+
+int run_decode_f32(void *out, int64_t out_stride_b, int64_t out_stride_h, const void *q,
+                   int64_t q_stride_b, int64_t q_stride_h, const void *k_cache,
+                   const void *v_cache, int64_t k_block_stride, int64_t v_block_stride,
+                   int32_t num_blocks, int32_t block_size, int32_t num_kv_heads, int32_t group,
+                   const int32_t *block_tables, int64_t block_table_stride,
+                   int32_t max_blocks_per_seq, const int32_t *context_lens, int32_t batch,
+                   float softmax_scale, uint32_t *dev_error, cudaStream_t st) {
+  if (!out || !q || !k_cache || !v_cache || !block_tables || !context_lens || max_blocks_per_seq <= 0)
+    return SLOKV_ERR_INVALID_ARG;
+  // float4 K rows: 16-byte cache bases and block strides
+  if ((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) & 15u)
+    return SLOKV_ERR_ALIGNMENT;
+  if ((k_block_stride | v_block_stride) & 3) return SLOKV_ERR_ALIGNMENT;
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(out)) & 3u)
+    return SLOKV_ERR_ALIGNMENT;
+  const dim3 grid(static_cast<unsigned>(batch), static_cast<unsigned>(num_kv_heads));
+  auto go = [&](auto kernel) {
+    kernel<<<grid, f32dec::kThreads, 0, st>>>(
+        static_cast<float *>(out), out_stride_b, out_stride_h, static_cast<const float *>(q),
+        q_stride_b, q_stride_h, static_cast<const float *>(k_cache),
+        static_cast<const float *>(v_cache), k_block_stride, v_block_stride, num_blocks,
+        block_size, num_kv_heads, block_tables, block_table_stride, max_blocks_per_seq,
+        context_lens, softmax_scale, dev_error);
+    return cudaGetLastError() == cudaSuccess ? SLOKV_OK : SLOKV_ERR_CUDA;
+  };
+  switch (group) {
+    case 1: return go(paged_decode_f32_kernel<1>);
+    case 2: return go(paged_decode_f32_kernel<2>);
+    case 4: return go(paged_decode_f32_kernel<4>);
+    case 8: return go(paged_decode_f32_kernel<8>);
+    case 16: return go(paged_decode_f32_kernel<16>);
+    default: return SLOKV_ERR_UNSUPPORTED;
+  }
+}
+
 // Shared argument checks and launch of both cache formats.
 int run_decode(bool fp8, void *out, int64_t out_stride_b, int64_t out_stride_h, const void *q,
                int64_t q_stride_b, int64_t q_stride_h, const void *k_cache, const void *v_cache,
@@ -838,10 +1017,17 @@ int run_decode(bool fp8, void *out, int64_t out_stride_b, int64_t out_stride_h, 
   if (batch == 0) return SLOKV_OK;
   if (batch > kMaxBatch) return SLOKV_ERR_UNSUPPORTED;
   if (head_dim != kD) return SLOKV_ERR_UNSUPPORTED;
-  if (dtype != SLOKV_DTYPE_BF16 && dtype != SLOKV_DTYPE_F16) return SLOKV_ERR_UNSUPPORTED;
+  const bool f32 = !fp8 && dtype == SLOKV_DTYPE_F32;
+  if (dtype != SLOKV_DTYPE_BF16 && dtype != SLOKV_DTYPE_F16 && !f32) return SLOKV_ERR_UNSUPPORTED;
   if (num_q_heads % num_kv_heads) return SLOKV_ERR_INVALID_ARG;
   const int group = num_q_heads / num_kv_heads;
   if (group > 16) return SLOKV_ERR_UNSUPPORTED;
+  if (f32)
+    return run_decode_f32(out, out_stride_b, out_stride_h, q, q_stride_b, q_stride_h, k_cache,
+                          v_cache, k_block_stride, v_block_stride, num_blocks, block_size,
+                          num_kv_heads, group, block_tables, block_table_stride,
+                          max_blocks_per_seq, context_lens, batch, softmax_scale, dev_error,
+                          static_cast<cudaStream_t>(stream));
   if (block_size % kTile) return SLOKV_ERR_UNSUPPORTED;
   if (!out || !q || !k_cache || !v_cache || !block_tables || !context_lens || max_blocks_per_seq <= 0)
     return SLOKV_ERR_INVALID_ARG;

@@ -30,6 +30,7 @@
 //  * V rows past k_len in the last tile are zeroed before PV so stale pool bytes
 //    (possibly NaN) never reach O; masked scores are -inf, not multiplied.
 #include "common.cuh"
+#include "fp8_e4m3.cuh"
 #include "tcgen05.cuh"
 
 #include <cudaTypedefs.h>
@@ -75,6 +76,9 @@ struct Params {
   // unscaled FP8 codes and the logits of a key tile in page `pid` are
   // S * k_page_scale[pid * hkv + kv head].  Null: 1.
   const float *k_page_scale;
+  // FP8 kernel only: the pool's V scales; V codes of page `pid` widen to
+  // f16(decode(code) * v_page_scale[pid * hkv + kv head]).
+  const float *v_page_scale;
 };
 
 __device__ __forceinline__ float fast_exp2(float x) {
@@ -857,6 +861,424 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
   }
 }
 
+
+// ---- FP8-E4M3 pool: the two-head kernel with the dequantisation in the tile load --
+//
+// Replaces the page copy of the FP8 prefix-cache path: K and V pages of E4M3
+// codes are TMA-loaded as they lie in the pool (16 KB per 128-key tile) into a
+// code staging buffer, and the two otherwise idle warps of the issue warpgroup
+// (10 and 11) widen them in shared memory into the f16 K / V stages the tensor
+// core reads -- K as its unscaled code values (every E4M3 value is exact in f16),
+// the page's K scale applied to the logits as in the FP8 decode; V as
+// f16(decode(code) * V scale) in fp32 (the f16 keeps 11 bits against V outliers,
+// where a bf16 P or V would keep 8).  MMAs run in f16 (kind::f16, A and B f16):
+// a bf16 q is converted to f16 in shared memory by the softmax warps once per
+// CTA, and the output is written in q's dtype.  The pipeline is the two-head
+// kernel's (warps 0-7 softmax, 8 MMA issue, 9 TMA), with one code buffer for K
+// and one for V: the TMA of tile j+1's codes overlaps the widening of tile j's
+// other half and the MMAs.
+namespace f8 {
+constexpr int kCodeTile = kBN * kD;                  // 16 KB of codes per 128-key tile
+constexpr int kOffQ = 0;
+constexpr int kOffK = 2 * kTile;
+constexpr int kOffV = 4 * kTile;
+constexpr int kOffKc = 6 * kTile;
+constexpr int kOffVc = kOffKc + kCodeTile;
+constexpr int kTilesBytes = kOffVc + kCodeTile;     // 224 KB
+enum Bar {
+  kQ = 0, kQ16 = 1, kKc = 2, kVc = 3, kKcFree = 4, kVcFree = 5, kK16 = 6, kV16 = 8,
+  kFreeK = 10, kFreeV = 12, kS = 14, kP = 16, kPV = 18, kNum = 20
+};
+constexpr int kOffScale = kTilesBytes + kNum * 8 + 16;
+constexpr int kSmemFixed = 1024 + kOffScale;        // + 4 bytes per page of the table row
+constexpr int kConvThreads = 64;                    // warps 10 and 11
+}  // namespace f8
+
+// Widen one 128-key tile of E4M3 codes (128-byte rows, 128-byte swizzle) into
+// the f16 operand layout (two 64-dim halves of 128-byte rows, 128-byte
+// swizzle); V tiles (kScaled) are multiplied by `sv` in fp32 and rows >= valid
+// are written as zeros.  Thread ct of the kConvThreads converters takes 16-code
+// chunks ct, ct + 64, ...
+template <bool kScaled>
+__device__ __forceinline__ void widen_tile(const uint8_t *codes, uint8_t *dst, int ct, float sv,
+                                           int valid) {
+#pragma unroll 2
+  for (int g = ct; g < kBN * 8; g += f8::kConvThreads) {
+    const int row = g >> 3, c = g & 7;
+    uint4 lo, hi;
+    if (kScaled && row >= valid) {
+      lo = hi = make_uint4(0, 0, 0, 0);
+    } else {
+      const uint4 w = *reinterpret_cast<const uint4 *>(codes + swz128(row, c));
+      const uint32_t src[4] = {w.x, w.y, w.z, w.w};
+      uint32_t out[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        uint32_t h2 = e4m3x2_to_f16x2((src[i >> 1] >> ((i & 1) * 16)) & 0xffffu);
+        if (kScaled) {
+          const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&h2));
+          const __half2 r = __floats2half2_rn(__fmul_rn(f.x, sv), __fmul_rn(f.y, sv));
+          h2 = *reinterpret_cast<const uint32_t *>(&r);
+        }
+        out[i] = h2;
+      }
+      lo = make_uint4(out[0], out[1], out[2], out[3]);
+      hi = make_uint4(out[4], out[5], out[6], out[7]);
+    }
+    uint8_t *half = dst + (c >> 2) * kHalf;
+    *reinterpret_cast<uint4 *>(half + swz128(row, 2 * (c & 3))) = lo;
+    *reinterpret_cast<uint4 *>(half + swz128(row, 2 * (c & 3) + 1)) = hi;
+  }
+}
+
+template <typename Tq>
+__global__ void __launch_bounds__(ws::kThreads, 1)
+    paged_prefill_fp8_kernel(const __grid_constant__ CUtensorMap qmap,
+                             const __grid_constant__ CUtensorMap kmap,
+                             const __grid_constant__ CUtensorMap vmap, const Params p) {
+  constexpr uint32_t kIdescS = tc::idesc_f16(false, false, 128, 128);
+  constexpr uint32_t kIdescPV = tc::idesc_f16(false, true, 128, 128);
+
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int warp = __shfl_sync(0xffffffffu, tid >> 5, 0);
+  const int pairs = p.hq >> 1;
+  const int rank = blockIdx.x / pairs;
+  const int h0 = 2 * (blockIdx.x - rank * pairs);
+  int r, m;
+  if (p.order != nullptr) {
+    const int item = __ldg(p.order + rank);
+    if (item < 0) return;
+    r = item / p.m_tiles;
+    m = item - r * p.m_tiles;
+  } else {
+    r = rank / p.m_tiles;
+    m = p.m_tiles - 1 - (rank - r * p.m_tiles);
+  }
+  const int q0 = __ldg(p.cu_q + r), q_len = __ldg(p.cu_q + r + 1) - q0;
+  const int k0 = __ldg(p.cu_k + r), k_len = __ldg(p.cu_k + r + 1) - k0;
+  if (m * kBM >= q_len) return;
+  const int hk = h0 / p.group;
+  const int qk_off = k_len - q_len;
+  const int last_q = min((m + 1) * kBM, q_len) - 1;
+  const int need = min(k_len, qk_off + last_q + 1);
+  const int nk = need > 0 ? (need + kBN - 1) / kBN : 0;
+  if (nk == 0) {
+    if (tid < 256) {
+      const int qi = m * kBM + (tid & 127);
+      if (qi < q_len) {
+        Tq *orow = static_cast<Tq *>(p.out) + static_cast<int64_t>(q0 + qi) * p.out_st +
+                   static_cast<int64_t>(h0 + (tid >> 7)) * p.out_sh;
+        for (int d = 0; d < kD; d += 8) *reinterpret_cast<uint4 *>(orow + d) = make_uint4(0, 0, 0, 0);
+      }
+    }
+    return;
+  }
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t *base_ptr = smem_raw + (base - raw);
+  const uint32_t bars = base + f8::kTilesBytes;
+  volatile uint32_t *tmem_slot =
+      reinterpret_cast<volatile uint32_t *>(base_ptr + f8::kTilesBytes + f8::kNum * 8);
+  volatile uint32_t *abort_flag = tmem_slot + 1;
+  auto bar = [&](int i) { return bars + i * 8; };
+  float *s_ks = reinterpret_cast<float *>(base_ptr + f8::kOffScale);
+  {  // the row's K page scales for this KV head (pages the tiles reach, <= table width)
+    const int npg = min((need + p.block_size - 1) / p.block_size, p.max_blocks);
+    for (int pg = tid; pg < npg; pg += ws::kThreads) {
+      const int32_t pid = __ldg(p.block_tables + static_cast<int64_t>(r) * p.bt_stride + pg);
+      s_ks[pg] = pid >= 0 && pid < p.num_blocks
+                     ? __ldg(p.k_page_scale + static_cast<int64_t>(pid) * p.hkv + hk)
+                     : 0.f;
+    }
+  }
+
+  if (tid == 0) {
+    prefetch_tensormap(&qmap);
+    prefetch_tensormap(&kmap);
+    prefetch_tensormap(&vmap);
+    for (int i = 0; i < f8::kNum; ++i) {
+      uint32_t count = 1;
+      if (i == f8::kQ16) count = 256;
+      if (i == f8::kKcFree || i == f8::kVcFree || i == f8::kK16 || i == f8::kK16 + 1 ||
+          i == f8::kV16 || i == f8::kV16 + 1)
+        count = f8::kConvThreads;
+      if (i == f8::kP || i == f8::kP + 1) count = 128;
+      mbar_init(bar(i), count);
+    }
+    fence_barrier_init();
+    *abort_flag = 0;
+  }
+  if (warp == 0) {
+    tc::tmem_alloc(smem_u32(const_cast<uint32_t *>(tmem_slot)), kTmemCols);
+    tc::tmem_relinquish();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+
+  auto wait = [&](int i, uint32_t parity) {
+    if (*abort_flag) return false;
+    if (!mbar_wait(bar(i), parity)) {
+      record_error(p.err, SLOKV_DEVERR_TIMEOUT);
+      *abort_flag = 1;
+      return false;
+    }
+    return true;
+  };
+
+  if (warp >= 8) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(ws::kRegsIssue));
+    if (warp == 9) {
+      // ---------------- TMA producer: q once, then the code tiles ----------------
+      if (lane == 0) {
+        const uint64_t policy = l2_evict_first_policy();
+        mbar_arrive_expect_tx(bar(f8::kQ), 2 * kTile);
+        for (int hh = 0; hh < 2; ++hh) {
+          const uint32_t dst = base + f8::kOffQ + hh * kTile;
+          tma_load_4d(dst, &qmap, bar(f8::kQ), 0, h0 + hh, q0 + m * kBM, 0, policy);
+          tma_load_4d(dst + kHalf, &qmap, bar(f8::kQ), 64, h0 + hh, q0 + m * kBM, 0, policy);
+        }
+        // The code buffers hold one tile each, so the tiles after the next are
+        // prefetched into L2: a load then waits on L2, not on HBM.
+        auto prefetch = [&](int jj) {
+          if (jj >= nk) return;
+          const KvCoord c = kv_coord(p, r, k0, jj);
+          tma_prefetch_4d(&kmap, 0, hk, c.c2, c.c3);
+          tma_prefetch_4d(&vmap, 0, hk, c.c2, c.c3);
+        };
+        prefetch(1);
+        for (int j = 0; j < nk; ++j) {
+          const KvCoord c = kv_coord(p, r, k0, j);
+          if (!c.ok) record_error(p.err, SLOKV_DEVERR_BLOCK_RANGE);
+          prefetch(j + 2);
+          if (j >= 1 && !wait(f8::kKcFree, (j - 1) & 1)) break;
+          mbar_arrive_expect_tx(bar(f8::kKc), f8::kCodeTile);
+          tma_load_4d(base + f8::kOffKc, &kmap, bar(f8::kKc), 0, hk, c.c2, c.c3, policy);
+          if (j >= 1 && !wait(f8::kVcFree, (j - 1) & 1)) break;
+          mbar_arrive_expect_tx(bar(f8::kVc), f8::kCodeTile);
+          tma_load_4d(base + f8::kOffVc, &vmap, bar(f8::kVc), 0, hk, c.c2, c.c3, policy);
+        }
+      }
+    } else if (warp >= 10) {
+      // ---------------- converters: codes -> f16 operand stages ----------------
+      const int ct = tid - 10 * 32;
+      for (int j = 0; j < nk; ++j) {
+        const int st = j & 1;
+        if (!wait(f8::kKc, j & 1)) break;
+        if (j >= 2 && !wait(f8::kFreeK + st, ((j - 2) >> 1) & 1)) break;
+        widen_tile<false>(base_ptr + f8::kOffKc, base_ptr + f8::kOffK + st * kTile, ct, 1.f, kBN);
+        fence_proxy_async_smem();
+        mbar_arrive(bar(f8::kKcFree));
+        mbar_arrive(bar(f8::kK16 + st));
+        const KvCoord c = kv_coord(p, r, k0, j);
+        const float sv =
+            c.ok ? __ldg(p.v_page_scale + static_cast<int64_t>(c.c3) * p.hkv + hk) : 0.f;
+        if (!wait(f8::kVc, j & 1)) break;
+        if (j >= 2 && !wait(f8::kFreeV + st, ((j - 2) >> 1) & 1)) break;
+        widen_tile<true>(base_ptr + f8::kOffVc, base_ptr + f8::kOffV + st * kTile, ct, sv,
+                         k_len - j * kBN);
+        fence_proxy_async_smem();
+        mbar_arrive(bar(f8::kVcFree));
+        mbar_arrive(bar(f8::kV16 + st));
+      }
+    } else {
+      // ---------------- tensor-core issue (lane 0) ----------------
+      auto issue_s = [&](int hh, int j) {
+        const uint32_t qa = base + f8::kOffQ + hh * kTile;
+        const uint32_t kb = base + f8::kOffK + (j & 1) * kTile;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t off = (kk >> 2) * kHalf + (kk & 3) * 32;
+          tc::mma_f16_ss(tmem + ws::kColS + hh * 128, tc::smem_desc_sw128(qa + off, 16, 1024),
+                         tc::smem_desc_sw128(kb + off, 16, 1024), kIdescS, kk > 0);
+        }
+        tc::commit(bar(f8::kS + hh));
+      };
+      bool ok = wait(f8::kQ16, 0) && wait(f8::kK16, 0);
+      if (ok && lane == 0) {
+        tc::fence_after_sync();
+        issue_s(0, 0);
+        issue_s(1, 0);
+        tc::commit(bar(f8::kFreeK));
+      }
+      __syncwarp();
+      for (int j = 0; j < nk && ok; ++j) {
+        const int st = j & 1;
+        for (int hh = 0; hh < 2 && ok; ++hh) {
+          ok = wait(f8::kP + hh, j & 1);
+          if (ok && hh == 0) ok = wait(f8::kV16 + st, (j >> 1) & 1);
+          if (ok && lane == 0) {
+            tc::fence_after_sync();
+            const uint32_t vb = base + f8::kOffV + st * kTile;
+            const uint32_t pa = tmem + ws::kColS + hh * 128;
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk)
+              tc::mma_f16_ts(tmem + ws::kColO + hh * 128, pa + kk * 8,
+                             tc::smem_desc_sw128(vb + kk * 16 * 128, kHalf, 1024), kIdescPV,
+                             (j > 0 || kk > 0) ? 1u : 0u);
+            tc::commit(bar(f8::kPV + hh));
+          }
+          if (ok && j + 1 < nk) {
+            if (hh == 0) ok = wait(f8::kK16 + ((j + 1) & 1), ((j + 1) >> 1) & 1);
+            if (ok && lane == 0) {
+              tc::fence_after_sync();
+              issue_s(hh, j + 1);
+            }
+          }
+          __syncwarp();
+        }
+        if (ok && lane == 0) {
+          tc::commit(bar(f8::kFreeV + st));
+          if (j + 1 < nk) tc::commit(bar(f8::kFreeK + ((j + 1) & 1)));
+        }
+        __syncwarp();
+      }
+    }
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(ws::kRegsSoftmax));
+    const int hh = warp >> 2;
+    const int row = tid & 127;
+    // q -> f16 in place (one row of one head per thread), then release the Q stage
+    if (wait(f8::kQ, 0) && !std::is_same<Tq, __half>::value) {
+      uint8_t *qrow = base_ptr + f8::kOffQ + hh * kTile;
+#pragma unroll 4
+      for (int c = 0; c < 16; ++c) {
+        uint4 *ptr = reinterpret_cast<uint4 *>(qrow + (c >> 3) * kHalf + swz128(row, c & 7));
+        uint4 w = *ptr;
+        uint32_t v[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const __half2 h2 = __float22half2_rn(
+              __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&v[i])));
+          v[i] = *reinterpret_cast<const uint32_t *>(&h2);
+        }
+        *ptr = make_uint4(v[0], v[1], v[2], v[3]);
+      }
+      fence_proxy_async_smem();
+    }
+    mbar_arrive(bar(f8::kQ16));
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const int qi = m * kBM + row;
+    const bool row_ok = qi < q_len;
+    const int kmax = row_ok ? min(qk_off + qi, k_len - 1) : -1;
+    const uint32_t s_addr = tmem + lane_base + ws::kColS + hh * 128;
+    const uint32_t o_addr = tmem + lane_base + ws::kColO + hh * 128;
+    constexpr float kSumLimit = 256.f;
+    float m_run = row_ok ? -INFINITY : 0.f, l_run = 0.f;
+    uint32_t s[4][32];
+    bool ok = true;
+    auto exp_store = [&](float mu, float sl) {
+      const uint64_t sl2 = f32x2(sl, sl), nmu2 = f32x2(-mu, -mu);
+      uint64_t rs2[4] = {0ull, 0ull, 0ull, 0ull};
+#pragma unroll
+      for (int hb = 0; hb < 2; ++hb) {
+        uint32_t pk[32];
+#pragma unroll
+        for (int w = 0; w < 32; ++w) {
+          const int i = 2 * hb + (w >> 4), c = (w & 15) * 2;
+          const float2 x = f32x2_split(ffma2(
+              f32x2(__uint_as_float(s[i][c]), __uint_as_float(s[i][c + 1])), sl2, nmu2));
+          const float a = fast_exp2(x.x);
+          const float b = fast_exp2(x.y);
+          rs2[w & 3] = fadd2(rs2[w & 3], f32x2(a, b));
+          pk[w] = Pack<__half>::two(a, b);
+        }
+        tc::st32(s_addr + 32 * hb, pk);
+      }
+      const float2 r01 = f32x2_split(fadd2(rs2[0], rs2[1]));
+      const float2 r23 = f32x2_split(fadd2(rs2[2], rs2[3]));
+      return (r01.x + r01.y) + (r23.x + r23.y);
+    };
+    for (int j = 0; j < nk && ok; ++j) {
+      ok = wait(f8::kS + hh, j & 1);
+      tc::fence_after_sync();
+      const int key0 = j * kBN;
+      const bool full = key0 + kBN - 1 <= kmax;
+      const int kpage = key0 / p.block_size;
+      const float sl = p.scale_log2 * fmaxf(kpage < p.max_blocks ? s_ks[kpage] : 0.f, 1e-30f);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) tc::ld32(s_addr + 32 * i, s[i]);
+      tc::wait_ld();
+      if (!full) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int c = 0; c < 32; ++c)
+            if (key0 + 32 * i + c > kmax) s[i][c] = 0xff800000u;
+      }
+      const bool fresh = __any_sync(0xffffffffu, m_run == -INFINITY);
+      float alpha = 1.f, rs = 0.f;
+      bool redo = fresh;
+      if (!fresh) {
+        rs = exp_store(m_run, sl);
+        redo = __any_sync(0xffffffffu, !(rs <= kSumLimit));
+      }
+      if (redo) {
+        float mx = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int c = 0; c < 32; ++c) mx = fmaxf(mx, __uint_as_float(s[i][c]));
+        mx *= sl;
+        if (mx > m_run) {
+          alpha = fast_exp2(m_run - mx);
+          m_run = mx;
+        }
+        if (!fresh) tc::wait_st();
+        rs = exp_store(m_run == -INFINITY ? 0.f : m_run, sl);
+      }
+      l_run = l_run * alpha + rs;
+      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) tc::ld32(o_addr + 32 * i, s[i]);
+        tc::wait_ld();
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+#pragma unroll
+          for (int c = 0; c < 32; ++c) s[i][c] = __float_as_uint(__uint_as_float(s[i][c]) * alpha);
+          tc::st32(o_addr + 32 * i, s[i]);
+        }
+      }
+      tc::wait_st();
+      tc::fence_before_sync();
+      mbar_arrive(bar(f8::kP + hh));
+    }
+    ok = ok && wait(f8::kPV + hh, (nk - 1) & 1);
+    tc::fence_after_sync();
+    if (__all_sync(0xffffffffu, ok)) {
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      Tq *orow = static_cast<Tq *>(p.out) + static_cast<int64_t>(q0 + qi) * p.out_st +
+                 static_cast<int64_t>(h0 + hh) * p.out_sh;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) tc::ld32(o_addr + 32 * i, s[i]);
+      tc::wait_ld();
+      if (row_ok) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+#pragma unroll
+          for (int c = 0; c < 32; c += 8) {
+            uint4 w;
+            w.x = Pack<Tq>::two(__uint_as_float(s[i][c]) * inv, __uint_as_float(s[i][c + 1]) * inv);
+            w.y = Pack<Tq>::two(__uint_as_float(s[i][c + 2]) * inv, __uint_as_float(s[i][c + 3]) * inv);
+            w.z = Pack<Tq>::two(__uint_as_float(s[i][c + 4]) * inv, __uint_as_float(s[i][c + 5]) * inv);
+            w.w = Pack<Tq>::two(__uint_as_float(s[i][c + 6]) * inv, __uint_as_float(s[i][c + 7]) * inv);
+            *reinterpret_cast<uint4 *>(orow + 32 * i + c) = w;
+          }
+        }
+      }
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
 // ---- host side -------------------------------------------------------------
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -886,6 +1308,49 @@ bool encode_map(CUtensorMap *map, const void *base, CUtensorMapDataType dt, uint
   return fn(map, dt, 4, const_cast<void *>(base), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// 4-D map of an E4M3 code pool {dim 128, head, row, page} (bytes) with a
+// {128, 1, 128, 1} box: one 128-key tile of one head, 128-byte rows, 128-byte
+// swizzle.
+bool encode_code_map(CUtensorMap *map, const void *base, uint64_t heads, uint64_t rows,
+                     uint64_t pages, uint64_t page_stride_bytes) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[4] = {kD, heads, rows, pages};
+  cuuint64_t strides[3] = {kD, heads * kD, page_stride_bytes};
+  cuuint32_t box[4] = {kD, 1, kBN, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void *>(base), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <typename Tq>
+int launch_fp8(const Params &p, const CUtensorMap &qm, const CUtensorMap &km,
+               const CUtensorMap &vm, int rows, cudaStream_t stream) {
+  static std::once_flag once;
+  static bool ok = false;
+  std::call_once(once, [] {
+    cudaFuncAttributes fa;
+    // the register split hands out exactly the launch allocation (see ws::kRegsLaunch)
+    ok = cudaFuncSetAttribute(paged_prefill_fp8_kernel<Tq>,
+                              cudaFuncAttributeMaxDynamicSharedMemorySize, ws::kSmemMax) ==
+             cudaSuccess &&
+         cudaFuncGetAttributes(&fa, paged_prefill_fp8_kernel<Tq>) == cudaSuccess &&
+         fa.numRegs == ws::kRegsLaunch;
+  });
+  if (!ok) return SLOKV_ERR_UNSUPPORTED;
+  const int64_t smem = f8::kSmemFixed + 4 * static_cast<int64_t>(p.max_blocks);
+  if (smem > ws::kSmemMax) return SLOKV_ERR_UNSUPPORTED;
+  if (p.order != nullptr)
+    prefill_schedule_kernel<<<1, kSchedThreads, 0, stream>>>(p.cu_q, p.cu_k, rows, p.m_tiles,
+                                                               const_cast<int32_t *>(p.order));
+  const int64_t blocks = static_cast<int64_t>(rows) * p.m_tiles * (p.hq / 2);
+  if (blocks > 0x7fffffff) return SLOKV_ERR_UNSUPPORTED;
+  paged_prefill_fp8_kernel<Tq><<<static_cast<unsigned>(blocks), ws::kThreads,
+                                 static_cast<unsigned>(smem), stream>>>(qm, km, vm, p);
+  return cudaGetLastError() == cudaSuccess ? SLOKV_OK : SLOKV_ERR_CUDA;
 }
 
 template <typename T>
@@ -1016,6 +1481,7 @@ extern "C" int slokv_paged_prefill(void *out, int64_t out_stride_t, int64_t out_
   p.err = dev_error;
   p.m_tiles = (max_seqlen_q + kBM - 1) / kBM;
   p.k_page_scale = k_page_scale;
+  p.v_page_scale = nullptr;
   // page scales are applied by the two-head kernel only (even GQA groups, paged)
   if (k_page_scale != nullptr && (p.group % 2 != 0 || !paged)) return SLOKV_ERR_UNSUPPORTED;
   // The work order needs rows x m_tiles int32 (slokv_paged_prefill_workspace_bytes);
@@ -1029,4 +1495,74 @@ extern "C" int slokv_paged_prefill(void *out, int64_t out_stride_t, int64_t out_
   return dtype == SLOKV_DTYPE_BF16
              ? launch<__nv_bfloat16>(p, qm, km, vm, num_rows, max_seqlen_q, st)
              : launch<__half>(p, qm, km, vm, num_rows, max_seqlen_q, st);
+}
+
+extern "C" int slokv_paged_prefill_fp8(void *out, int64_t out_stride_t, int64_t out_stride_h,
+                                       const void *q, int64_t q_stride_t, int64_t q_stride_h,
+                                       int64_t q_rows, const void *k_codes, const void *v_codes,
+                                       int64_t k_block_stride, int64_t v_block_stride,
+                                       const float *k_scale, const float *v_scale,
+                                       const int32_t *cu_seqlens_q, const int32_t *cu_seqlens_k,
+                                       int32_t num_rows, int32_t max_seqlen_q,
+                                       const int32_t *block_tables, int64_t block_table_stride,
+                                       int32_t max_blocks_per_seq, int32_t num_blocks,
+                                       int32_t block_size, int32_t num_q_heads,
+                                       int32_t num_kv_heads, int32_t head_dim,
+                                       float softmax_scale, int32_t q_dtype, void *workspace,
+                                       size_t workspace_bytes, uint32_t *dev_error, void *stream) {
+  using namespace slokv;
+  using namespace slokv::prefill;
+  if (num_rows < 0 || max_seqlen_q < 0 || num_q_heads <= 0 || num_kv_heads <= 0)
+    return SLOKV_ERR_INVALID_ARG;
+  if (num_rows == 0 || max_seqlen_q == 0) return SLOKV_OK;
+  if (head_dim != kD) return SLOKV_ERR_UNSUPPORTED;
+  if (q_dtype != SLOKV_DTYPE_BF16 && q_dtype != SLOKV_DTYPE_F16) return SLOKV_ERR_UNSUPPORTED;
+  if (num_q_heads % num_kv_heads) return SLOKV_ERR_INVALID_ARG;
+  if ((num_q_heads / num_kv_heads) % 2) return SLOKV_ERR_UNSUPPORTED;   // two heads per CTA
+  if (!out || !q || !k_codes || !v_codes || !k_scale || !v_scale || !cu_seqlens_q ||
+      !cu_seqlens_k || !block_tables || q_rows <= 0 || num_blocks <= 0 || max_blocks_per_seq <= 0)
+    return SLOKV_ERR_INVALID_ARG;
+  if (block_size <= 0 || block_size % kBN) return SLOKV_ERR_UNSUPPORTED;
+  const uint64_t bits = reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(out) |
+                        reinterpret_cast<uintptr_t>(k_codes) | reinterpret_cast<uintptr_t>(v_codes);
+  if (bits & 15u) return SLOKV_ERR_ALIGNMENT;
+  if (((q_stride_t | q_stride_h | out_stride_t | out_stride_h) * 2) & 15) return SLOKV_ERR_ALIGNMENT;
+  if ((k_block_stride | v_block_stride) & 15) return SLOKV_ERR_ALIGNMENT;   // bytes (codes)
+
+  const CUtensorMapDataType dt = q_dtype == SLOKV_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                             : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap qm, km, vm;
+  const uint64_t hkv = static_cast<uint64_t>(num_kv_heads);
+  if (!encode_map(&qm, q, dt, num_q_heads, q_stride_h, q_rows, q_stride_t, 1,
+                  q_rows * q_stride_t) ||
+      !encode_code_map(&km, k_codes, hkv, block_size, num_blocks, k_block_stride) ||
+      !encode_code_map(&vm, v_codes, hkv, block_size, num_blocks, v_block_stride))
+    return SLOKV_ERR_CUDA;
+  Params p;
+  p.out = out;
+  p.out_st = out_stride_t;
+  p.out_sh = out_stride_h;
+  p.cu_q = cu_seqlens_q;
+  p.cu_k = cu_seqlens_k;
+  p.block_tables = block_tables;
+  p.bt_stride = block_table_stride;
+  p.max_blocks = max_blocks_per_seq;
+  p.num_blocks = num_blocks;
+  p.block_size = block_size;
+  p.hq = num_q_heads;
+  p.hkv = num_kv_heads;
+  p.group = num_q_heads / num_kv_heads;
+  p.scale_log2 = softmax_scale * 1.4426950408889634f;
+  p.err = dev_error;
+  p.m_tiles = (max_seqlen_q + kBM - 1) / kBM;
+  p.k_page_scale = k_scale;
+  p.v_page_scale = v_scale;
+  p.order = workspace != nullptr &&
+                    workspace_bytes >= slokv_paged_prefill_workspace_bytes(num_rows, max_seqlen_q) &&
+                    (reinterpret_cast<uintptr_t>(workspace) & 3u) == 0
+                ? static_cast<const int32_t *>(workspace)
+                : nullptr;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return q_dtype == SLOKV_DTYPE_BF16 ? launch_fp8<__nv_bfloat16>(p, qm, km, vm, num_rows, st)
+                                     : launch_fp8<__half>(p, qm, km, vm, num_rows, st);
 }

@@ -443,20 +443,21 @@ def _varlen_attention(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, softmax
 def flash_attn_varlen_func_fp8(q, k_codes, v_codes, k_scale, v_scale, cu_seqlens_q,
                                cu_seqlens_k, max_seqlen_q, max_seqlen_k, softmax_scale=None,
                                causal=True, block_table=None, out=None):
-    """Prefix-cache varlen attention over an FP8 pool (block_table required).
+    """Prefix-cache varlen attention over an FP8 pool (block_table required),
+    the dequantisation fused into the prefill kernel's tile loads.
 
-    The pages the rows read are copied into a per-device f16 page buffer of
-    rows x ceil(max_seqlen_k / block_size) pages -- K as its unscaled code
-    values (exact in f16) with its per-(block, head) scale kept aside, V as
-    code x scale in fp32 rounded to f16 -- which the paged prefill kernel then
-    attends in f16 through a fixed remapped table, multiplying each page's
-    logits by its K scale (the FP8 decode's arithmetic: S = scale_k * (q .
-    codes)).  q goes in as f16 and the output comes back in q's dtype.  The
-    buffers grow outside graph capture only: make the first call of the
-    largest geometry eagerly.  Needs an even number of query heads per KV head.
+    The kernel TMA-loads each 128-key tile of E4M3 codes straight from the pool
+    pages and widens it in shared memory -- K as its unscaled code values
+    (exact in f16) with the page's K scale applied to the logits, V as
+    f16(decode(code) * V scale) -- so the tensor cores run f16 MMAs on them; a
+    bf16 q is converted to f16 inside the kernel and the output is written in
+    q's dtype.  Nothing is copied or allocated per call beyond `out`.  Needs
+    an even number of query heads per KV head and max_seqlen_k <= 468 pages.
     """
     if block_table is None:
         raise SlokvError("FP8 varlen attention reads the pool: block_table is required")
+    if not causal:
+        raise SlokvError("only causal varlen attention is implemented (the engine's only use)")
     NB, bs, Hkv, D = k_codes.shape
     if v_codes.shape != k_codes.shape or D != q.shape[-1]:
         raise SlokvError("FP8 pool shape mismatch with q")
@@ -468,39 +469,34 @@ def flash_attn_varlen_func_fp8(q, k_codes, v_codes, k_scale, v_scale, cu_seqlens
             raise SlokvError(f"{name} must be contiguous fp32 [num_blocks, num_kv_heads]")
     if block_table.dtype != torch.int32 or block_table.stride(-1) != 1:
         raise SlokvError("block_table must be int32 with a contiguous last dimension")
+    if q.dim() != 3 or q.dtype not in (torch.bfloat16, torch.float16) or q.stride(-1) != 1:
+        raise SlokvError("q must be bf16/f16 [tokens, heads, head_dim] with a contiguous last dim")
     dev = require_cuda(q, k_codes, v_codes, k_scale, v_scale, cu_seqlens_q, cu_seqlens_k,
                        block_table)
+    _i32_contig("cu_seqlens_q", cu_seqlens_q)
     _i32_contig("cu_seqlens_k", cu_seqlens_k)
-    rows = cu_seqlens_k.numel() - 1
-    width = (int(max_seqlen_k) + bs - 1) // bs
-    if rows <= 0 or width <= 0:                 # no keys anywhere: zero output
-        o = out if out is not None else torch.empty_like(q)
-        return o.zero_()
-    if q.dim() != 3 or q.dtype not in (torch.bfloat16, torch.float16):
-        raise SlokvError("q must be bf16/f16 [tokens, heads, head_dim]")
-    page = bs * Hkv * D
-    pages = rows * width
-    nbytes = pages * page * 2
-    kbuf = buffers.workspace(dev, "fp8_prefill_k", nbytes)
-    vbuf = buffers.workspace(dev, "fp8_prefill_v", nbytes)
-    sbuf = buffers.workspace(dev, "fp8_prefill_kscale", pages * Hkv * 4)
-    kd = kbuf[:nbytes].view(torch.float16).view(pages, bs, Hkv, D)
-    vd = vbuf[:nbytes].view(torch.float16).view(pages, bs, Hkv, D)
-    ks = sbuf[:pages * Hkv * 4].view(torch.float32).view(pages, Hkv)
-    err = buffers.error_word(dev)
-    check(lib().slokv_fp8_pages_dequant(
-        k_codes.data_ptr(), v_codes.data_ptr(), k_codes.stride(0), v_codes.stride(0),
-        k_scale.data_ptr(), v_scale.data_ptr(), NB, bs, Hkv, D, block_table.data_ptr(),
-        block_table.stride(0), block_table.shape[1], cu_seqlens_k.data_ptr(), rows, width,
-        kd.data_ptr(), vd.data_ptr(), ks.data_ptr(), err.data_ptr(),
-        stream_ptr(dev)), "fp8_pages_dequant")
-    table = torch.arange(pages, dtype=torch.int32, device=q.device).view(rows, width)
-    q16 = q if q.dtype == torch.float16 else q.to(torch.float16)
-    o16 = _varlen_attention(q16, kd, vd, cu_seqlens_q, cu_seqlens_k, max_seqlen_q,
-                            softmax_scale, causal, table, None, ks)
+    if cu_seqlens_k.numel() != cu_seqlens_q.numel():
+        raise SlokvError("cu_seqlens_q and cu_seqlens_k differ in length")
+    Tq, Hq, _ = q.shape
+    rows = cu_seqlens_q.numel() - 1
     if out is None:
-        return o16 if q.dtype == torch.float16 else o16.to(q.dtype)
-    out.copy_(o16)
+        out = torch.empty(Tq, Hq, D, dtype=q.dtype, device=q.device)
+    elif out.dtype != q.dtype or out.shape != q.shape or out.stride(-1) != 1:
+        raise SlokvError("out must match q's shape and dtype with a contiguous last dim")
+    if Tq == 0 or rows <= 0:
+        return out
+    # the kernel keeps one K scale per page it can reach in shared memory: no
+    # row reaches past ceil(max_seqlen_k / block_size) pages
+    width = min(block_table.shape[1], max(1, (int(max_seqlen_k) + bs - 1) // bs))
+    scale = float(softmax_scale) if softmax_scale is not None else D ** -0.5
+    ws, ws_bytes = _prefill_workspace(dev, rows, int(max_seqlen_q))
+    check(lib().slokv_paged_prefill_fp8(
+        out.data_ptr(), out.stride(0), out.stride(1), q.data_ptr(), q.stride(0), q.stride(1), Tq,
+        k_codes.data_ptr(), v_codes.data_ptr(), k_codes.stride(0), v_codes.stride(0),
+        k_scale.data_ptr(), v_scale.data_ptr(), cu_seqlens_q.data_ptr(), cu_seqlens_k.data_ptr(),
+        rows, int(max_seqlen_q), block_table.data_ptr(), block_table.stride(0), width, NB, bs,
+        Hq, Hkv, D, scale, _lib.dtype_code(q.dtype), ws, ws_bytes,
+        buffers.error_word(dev).data_ptr(), stream_ptr(dev)), "paged_prefill_fp8")
     return out
 
 

@@ -142,3 +142,22 @@ def test_fp8_runs_append_and_page_widen_argument_checks(pkg):
     assert widen(rows=-1) == -1
     assert widen(hd=64) == -3
     assert widen() == -1                               # null pointers
+
+
+def test_fused_fp8_prefill_argument_checks(pkg):
+    lib = pkg._lib.lib()
+
+    def call(rows=2, maxq=128, hq=32, hkv=8, hd=128, bs=256, qdt=0, ptr=None, align=16, kbs=1 << 20):
+        return lib.slokv_paged_prefill_fp8(
+            ptr, 32 * 128, 128, ptr, 32 * 128, 128, 256, ptr, ptr, kbs, kbs, ptr, ptr, ptr, ptr,
+            rows, maxq, ptr, 16, 16, 100, bs, hq, hkv, hd, 0.1, qdt, None, 0, None, None)
+    assert call(rows=0) == 0 and call(maxq=0) == 0     # nothing to do
+    assert call(rows=-1) == -1
+    assert call(hd=64) == -3                           # head_dim 128 only
+    assert call(qdt=2) == -3                           # q/out are bf16 or f16
+    assert call(hq=24, hkv=8) == -3                    # odd GQA group: two heads per CTA
+    assert call(hq=30, hkv=8) == -1                    # heads not divisible
+    assert call() == -1                                # null pointers
+    assert call(ptr=16, bs=200) == -3                  # block size not a multiple of 128
+    assert call(ptr=24) == -2                          # misaligned base
+    assert call(ptr=16, kbs=1000) == -2                # block stride not a 16-byte multiple

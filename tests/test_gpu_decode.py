@@ -187,3 +187,50 @@ def test_decode_is_graph_capturable(pkg):
                           128 ** -0.5)
         assert_attn_close(out, expect)
     del g
+
+
+# fp32 pools (BASELINE config 1 is the reference's fp32 case): CUDA-core fp32
+# arithmetic, so the bar is fp32 summation-order noise, not the bf16 one.
+F32_MAX_TOL, F32_MEAN_TOL = 2e-5, 2e-6
+
+
+def test_decode_config1_fp32_matches_reference_golden(pkg, golden):
+    """BASELINE config 1 exactly as specified -- fp32 q/K/V, Qwen3-4B heads, pool
+    64 x 256, batch 8, L ~ U[1, 2048] -- on the GPU: fp32 append bit-exact with
+    the reference's Triton store (SHA-256 of its caches) and fp32 decode against
+    the reference's own fp32 decode output."""
+    import hashlib
+    manifest, arrays = golden
+    sc = S.cfg1_decode()
+    assert sc["k_cache"].dtype == torch.float32
+    kc, vc = sc["k_cache"].cuda(), sc["v_cache"].cuda()
+    pkg.store_kvcache(sc["k"].cuda(), sc["v"].cuda(), kc, vc, sc["slots"].cuda())
+    sha = lambda t: hashlib.sha256(t.cpu().contiguous().view(torch.uint8).numpy().tobytes()).hexdigest()
+    assert sha(kc) == manifest["scenarios"]["cfg1_decode"]["k_cache_sha256"]
+    assert sha(vc) == manifest["scenarios"]["cfg1_decode"]["v_cache_sha256"]
+    out = pkg.flash_attn_with_kvcache(sc["q"].cuda().unsqueeze(1), kc, vc,
+                                      cache_seqlens=sc["lens"].cuda(),
+                                      block_table=sc["tables"].cuda(),
+                                      softmax_scale=sc["scale"], causal=True)
+    torch.cuda.synchronize()
+    assert out.dtype == torch.float32
+    assert_attn_close(out, torch.from_numpy(arrays["cfg1_decode/out"]), F32_MAX_TOL, F32_MEAN_TOL)
+    assert pkg.read_device_errors() == 0
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,lo,hi,seed", [
+    (8, 32, 8, 1, 2048, 1100),      # config 1 distribution, other draws
+    (5, 16, 2, 200, 3000, 1101),    # group 8, contexts over many chunks
+    (7, 8, 8, 1, 300, 1102),        # group 1
+])
+def test_decode_fp32_random_layouts(pkg, B, Hq, Hkv, lo, hi, seed):
+    lens = det_ints(seed, B, lo, hi).tolist()
+    lens[0] = 0                       # a padded row: zeros
+    q, kc, vc, lens_t, tables = make_decode_case(seed, B, Hq, Hkv, [max(L, 1) for L in lens],
+                                                 dtype=torch.float32)
+    lens_t[0] = 0
+    expect = O.decode(q.unsqueeze(1), kc, vc, lens_t, tables, 128 ** -0.5)
+    out = run_decode(pkg, q, kc, vc, lens_t, tables, 128 ** -0.5)
+    assert_attn_close(out, expect, F32_MAX_TOL, F32_MEAN_TOL)
+    assert out[0].abs().sum().item() == 0
+    assert pkg.read_device_errors() == 0

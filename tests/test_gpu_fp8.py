@@ -329,3 +329,81 @@ def test_reused_block_ignores_stale_scale_without_reset(pkg, runs):
         pkg.store_kvcache_fp8(xs.cuda(), xs.cuda(), *dev, st.cuda(), runs=runs)
     _assert_pool_equal(dev, ref)
     assert pkg.read_device_errors() == 0
+
+
+def _page_copy_prefill(pkg, q, dev, tables, cu_q, cu_k, max_q, max_k, scale):
+    """The FP8 prefill as two steps, through the C ABI: the pages the rows read
+    copied to f16 (slokv_fp8_pages_dequant: K as code values plus its page
+    scales, V as code x scale), then the f16 prefill applying the K page scales
+    to the logits.  The fused kernel must compute the same arithmetic."""
+    lib = pkg._lib.lib()
+    kc, vc, ks, vs = dev
+    NB, bs, Hkv, D = kc.shape
+    rows = cu_k.numel() - 1
+    width = (max_k + bs - 1) // bs
+    pages = rows * width
+    kd = torch.zeros(pages, bs, Hkv, D, dtype=torch.float16, device="cuda")
+    vd = torch.zeros_like(kd)
+    kps = torch.zeros(pages, Hkv, dtype=torch.float32, device="cuda")
+    err = pkg._lib.buffers.error_word(kc.device)
+    assert lib.slokv_fp8_pages_dequant(
+        kc.data_ptr(), vc.data_ptr(), kc.stride(0), vc.stride(0), ks.data_ptr(), vs.data_ptr(),
+        NB, bs, Hkv, D, tables.data_ptr(), tables.stride(0), tables.shape[1], cu_k.data_ptr(),
+        rows, width, kd.data_ptr(), vd.data_ptr(), kps.data_ptr(), err.data_ptr(),
+        torch.cuda.current_stream().cuda_stream) == 0
+    table = torch.arange(pages, dtype=torch.int32, device="cuda").view(rows, width)
+    return pkg.kvcache._varlen_attention(q.to(torch.float16), kd, vd, cu_q, cu_k, max_q, scale,
+                                         True, table, None, kps)
+
+
+@pytest.mark.parametrize("qdt", [torch.bfloat16, torch.float16])
+def test_fused_fp8_prefill_equals_page_copy_path(pkg, qdt):
+    """The fused-dequant FP8 prefill (slokv_paged_prefill_fp8) against the same
+    arithmetic done as page copy + f16 prefill: identical fp32 results, so the
+    outputs differ at most by the final rounding (f16 then bf16 vs bf16 once)."""
+    c = _mixed_fp8_case(3400, [], [(1024, 300), (0, 77), (3000, 2048), (255, 1), (4095, 129)])
+    dev = _gpu(_pools(c["NB"], H=c["Hkv"]))
+    hk, hv, hs = c["hist"]
+    pkg.store_kvcache_fp8(hk.cuda(), hv.cuda(), *dev, hs.cuda())
+    pkg.store_kvcache_fp8(c["k"].cuda(), c["v"].cuda(), *dev, c["slots"].cuda())
+    m = {k: (t.cuda() if isinstance(t, torch.Tensor) else t) for k, t in c["meta"].items()}
+    q = c["q"].cuda().to(qdt)
+    scale = 128 ** -0.5
+    fused = pkg.flash_attn_varlen_func_fp8(q, *dev, m["prefill_cu_q"], m["prefill_cu_k"],
+                                           m["max_q"], m["max_k"], softmax_scale=scale,
+                                           block_table=m["prefill_tables"])
+    two = _page_copy_prefill(pkg, q, dev, m["prefill_tables"], m["prefill_cu_q"],
+                             m["prefill_cu_k"], m["max_q"], m["max_k"], scale)
+    torch.cuda.synchronize()
+    assert pkg.read_device_errors() == 0
+    assert fused.dtype == qdt and torch.isfinite(fused.float()).all()
+    if qdt == torch.float16:
+        assert torch.equal(fused, two)
+    else:
+        ref = two.to(qdt).float()
+        d = (fused.float() - ref).abs()
+        # bf16(x) against bf16(f16(x)): at most one bf16 spacing (2^-7 relative)
+        assert (d <= 2 ** -7 * ref.abs() + 1e-30).all(), d.max().item()
+        assert (d == 0).float().mean().item() >= 0.99
+    exp = O.varlen(c["q"].to(qdt), O.fp8_dequant(dev[0].cpu(), dev[2].cpu()),
+                   O.fp8_dequant(dev[1].cpu(), dev[3].cpu()), c["meta"]["prefill_cu_q"],
+                   c["meta"]["prefill_cu_k"], scale, c["meta"]["prefill_tables"])
+    assert_fp8_close(fused, exp)
+
+
+def test_fused_fp8_prefill_flags_bad_block_id(pkg):
+    """A table entry outside the pool loads zero codes (scale 0) for that page and
+    sets SLOKV_DEVERR_BLOCK_RANGE; the output stays finite."""
+    c = _mixed_fp8_case(3500, [], [(600, 100)])
+    dev = _gpu(_pools(c["NB"], H=c["Hkv"]))
+    hk, hv, hs = c["hist"]
+    pkg.store_kvcache_fp8(hk.cuda(), hv.cuda(), *dev, hs.cuda())
+    pkg.store_kvcache_fp8(c["k"].cuda(), c["v"].cuda(), *dev, c["slots"].cuda())
+    m = {k: (t.cuda() if isinstance(t, torch.Tensor) else t) for k, t in c["meta"].items()}
+    tables = m["prefill_tables"].clone()
+    tables[0, 1] = c["NB"] + 5
+    out = pkg.flash_attn_varlen_func_fp8(c["q"].cuda(), *dev, m["prefill_cu_q"], m["prefill_cu_k"],
+                                         m["max_q"], m["max_k"], block_table=tables)
+    torch.cuda.synchronize()
+    assert pkg.read_device_errors() & pkg._lib.DEVERR_BLOCK_RANGE
+    assert torch.isfinite(out.float()).all()
