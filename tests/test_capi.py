@@ -63,7 +63,8 @@ def test_decode_argument_checks(pkg):
     assert _decode(lib, batch=0) == 0                   # empty batch: nothing to do
     assert _decode(lib, batch=-1) == -1
     assert _decode(lib, d=64) == -3                     # head_dim 128 only
-    assert _decode(lib, dtype=2) == -3                  # fp32 attention not built
+    assert _decode(lib, dtype=2) == -1                  # fp32 path: null pointers rejected
+    assert _decode(lib, dtype=3) == -3                  # FP8 codes need slokv_paged_decode_fp8
     assert _decode(lib, hq=30) == -1                    # Hq % Hkv
     assert _decode(lib, hq=8 * 17) == -3                # group > 16
     assert _decode(lib, bs=48) == -3                    # block size multiple of 32
