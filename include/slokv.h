@@ -102,7 +102,10 @@ size_t slokv_paged_decode_workspace_bytes(int32_t device, int32_t num_q_heads,
  * q/out: element (b, h, d) at base + b*stride_b + h*stride_h + d.
  * k_cache/v_cache: [num_blocks, block_size, num_kv_heads, head_dim] with the
  * given block stride (elements).
- * dtype: SLOKV_DTYPE_BF16 or SLOKV_DTYPE_F16 for q/out/cache.
+ * dtype: SLOKV_DTYPE_BF16 or SLOKV_DTYPE_F16 for q/out/cache (tensor-core
+ * path), or SLOKV_DTYPE_F32 for an fp32 pool (the reference's fp32
+ * configuration: CUDA-core fp32 arithmetic, groups of 1, 2, 4, 8 or 16 query
+ * heads per KV head, cache bases 16-byte aligned; the workspace is not used).
  * workspace: >= slokv_paged_decode_workspace_bytes(...) bytes, 256-byte aligned.
  */
 int slokv_paged_decode(void *out, int64_t out_stride_b, int64_t out_stride_h,
@@ -251,7 +254,7 @@ int slokv_fp8_pages_dequant(const void *k_codes, const void *v_codes, int64_t k_
  * converted to f16 in the kernel) and out is written in q_dtype (bf16 or
  * f16).  The same arithmetic as slokv_fp8_pages_dequant followed by
  * slokv_paged_prefill(f16, k_page_scale), without the page buffer.  Even GQA
- * groups only, block_size % 128 == 0, max_blocks_per_seq <= 468 (one K scale
+ * groups only, block_size % 128 == 0, max_blocks_per_seq <= 460 (one K scale
  * per page in shared memory; pass the pages the longest row reaches), else
  * SLOKV_ERR_UNSUPPORTED.  An id outside the pool loads zero codes (scale 0)
  * and sets SLOKV_DEVERR_BLOCK_RANGE. */

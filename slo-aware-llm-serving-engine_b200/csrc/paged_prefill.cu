@@ -866,64 +866,62 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
 //
 // Replaces the page copy of the FP8 prefix-cache path: K and V pages of E4M3
 // codes are TMA-loaded as they lie in the pool (16 KB per 128-key tile) into a
-// code staging buffer, and the two otherwise idle warps of the issue warpgroup
-// (10 and 11) widen them in shared memory into the f16 K / V stages the tensor
-// core reads -- K as its unscaled code values (every E4M3 value is exact in f16),
-// the page's K scale applied to the logits as in the FP8 decode; V as
-// f16(decode(code) * V scale) in fp32 (the f16 keeps 11 bits against V outliers,
-// where a bf16 P or V would keep 8).  MMAs run in f16 (kind::f16, A and B f16):
-// a bf16 q is converted to f16 in shared memory by the softmax warps once per
-// CTA, and the output is written in q's dtype.  The pipeline is the two-head
-// kernel's (warps 0-7 softmax, 8 MMA issue, 9 TMA), with one code buffer for K
-// and one for V: the TMA of tile j+1's codes overlaps the widening of tile j's
-// other half and the MMAs.
+// 3-slot code ring, and the two otherwise idle warps of the issue warpgroup
+// (10 and 11) widen them in shared memory into the f16 stages the tensor core
+// reads.  Both K and V are widened to their unscaled code values (every E4M3
+// value is exact in f16), so the widening is one conversion per code pair.  The
+// scales enter the softmax instead, per 128-key tile (a tile never spans two
+// 256-token pages):
+//   * K: the tile's logits are S * k_scale (as in the FP8 decode);
+//   * V: P of the tile's keys is multiplied by r = v_scale / v_ref, with v_ref
+//     the largest V scale among the row's pages, by shifting the exponent of
+//     P = 2^(s - m + log2 r) (r <= 1, so P stays <= 2^8 in f16), the row sum
+//     taking P / r, and the output O * v_ref / l.
+// P and the V codes are f16 (11 bits, one rounding on P), the MMAs run in f16
+// (kind::f16): a bf16 q is converted to f16 in shared memory by the softmax
+// warps once per CTA and the output is written in q's dtype.  The pipeline is
+// the two-head kernel's (warps 0-7 softmax, 8 MMA issue, 9 TMA) with one f16 K
+// stage (the K widening of tile j+1 overlaps the softmax of tile j) and two
+// f16 V stages; tiles two ahead are prefetched into L2.
 namespace f8 {
 constexpr int kCodeTile = kBN * kD;                  // 16 KB of codes per 128-key tile
+constexpr int kSlots = 3;                            // code ring: K(j), V(j), K(j+1), ...
 constexpr int kOffQ = 0;
-constexpr int kOffK = 2 * kTile;
-constexpr int kOffV = 4 * kTile;
-constexpr int kOffKc = 6 * kTile;
-constexpr int kOffVc = kOffKc + kCodeTile;
-constexpr int kTilesBytes = kOffVc + kCodeTile;     // 224 KB
+constexpr int kOffK = 2 * kTile;                     // one f16 K stage
+constexpr int kOffV = 3 * kTile;                     // two f16 V stages
+constexpr int kOffCodes = 5 * kTile;
+constexpr int kTilesBytes = kOffCodes + kSlots * kCodeTile;   // 208 KB
 enum Bar {
-  kQ = 0, kQ16 = 1, kKc = 2, kVc = 3, kKcFree = 4, kVcFree = 5, kK16 = 6, kV16 = 8,
-  kFreeK = 10, kFreeV = 12, kS = 14, kP = 16, kPV = 18, kNum = 20
+  kQ = 0, kQ16 = 1, kCode = 2, kCodeFree = 5, kK16 = 8, kV16 = 9, kFreeK = 11, kFreeV = 12,
+  kS = 14, kP = 16, kPV = 18, kNum = 20
 };
+// after the barriers: TMEM slot, abort flag, v_ref; then (k scale, v scale)
+// of every page of the table row
 constexpr int kOffScale = kTilesBytes + kNum * 8 + 16;
-constexpr int kSmemFixed = 1024 + kOffScale;        // + 4 bytes per page of the table row
+constexpr int kSmemFixed = 1024 + kOffScale;        // + 8 bytes per page of the table row
 constexpr int kConvThreads = 64;                    // warps 10 and 11
 }  // namespace f8
 
 // Widen one 128-key tile of E4M3 codes (128-byte rows, 128-byte swizzle) into
 // the f16 operand layout (two 64-dim halves of 128-byte rows, 128-byte
-// swizzle); V tiles (kScaled) are multiplied by `sv` in fp32 and rows >= valid
-// are written as zeros.  Thread ct of the kConvThreads converters takes 16-code
+// swizzle), rows >= valid written as zeros (stale pool bytes past a row's keys
+// may hold NaN codes).  Thread ct of the kConvThreads converters takes 16-code
 // chunks ct, ct + 64, ...
-template <bool kScaled>
-__device__ __forceinline__ void widen_tile(const uint8_t *codes, uint8_t *dst, int ct, float sv,
-                                           int valid) {
-#pragma unroll 2
+__device__ __forceinline__ void widen_tile(const uint8_t *codes, uint8_t *dst, int ct, int valid) {
+#pragma unroll 4
   for (int g = ct; g < kBN * 8; g += f8::kConvThreads) {
     const int row = g >> 3, c = g & 7;
-    uint4 lo, hi;
-    if (kScaled && row >= valid) {
-      lo = hi = make_uint4(0, 0, 0, 0);
-    } else {
+    uint4 lo = make_uint4(0, 0, 0, 0), hi = lo;
+    if (row < valid) {
       const uint4 w = *reinterpret_cast<const uint4 *>(codes + swz128(row, c));
-      const uint32_t src[4] = {w.x, w.y, w.z, w.w};
-      uint32_t out[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        uint32_t h2 = e4m3x2_to_f16x2((src[i >> 1] >> ((i & 1) * 16)) & 0xffffu);
-        if (kScaled) {
-          const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&h2));
-          const __half2 r = __floats2half2_rn(__fmul_rn(f.x, sv), __fmul_rn(f.y, sv));
-          h2 = *reinterpret_cast<const uint32_t *>(&r);
-        }
-        out[i] = h2;
-      }
-      lo = make_uint4(out[0], out[1], out[2], out[3]);
-      hi = make_uint4(out[4], out[5], out[6], out[7]);
+      lo.x = e4m3x2_to_f16x2(w.x & 0xffffu);
+      lo.y = e4m3x2_to_f16x2(w.x >> 16);
+      lo.z = e4m3x2_to_f16x2(w.y & 0xffffu);
+      lo.w = e4m3x2_to_f16x2(w.y >> 16);
+      hi.x = e4m3x2_to_f16x2(w.z & 0xffffu);
+      hi.y = e4m3x2_to_f16x2(w.z >> 16);
+      hi.z = e4m3x2_to_f16x2(w.w & 0xffffu);
+      hi.w = e4m3x2_to_f16x2(w.w >> 16);
     }
     uint8_t *half = dst + (c >> 2) * kHalf;
     *reinterpret_cast<uint4 *>(half + swz128(row, 2 * (c & 3))) = lo;
@@ -982,16 +980,23 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
   volatile uint32_t *tmem_slot =
       reinterpret_cast<volatile uint32_t *>(base_ptr + f8::kTilesBytes + f8::kNum * 8);
   volatile uint32_t *abort_flag = tmem_slot + 1;
+  uint32_t *v_ref_bits = const_cast<uint32_t *>(tmem_slot + 2);
   auto bar = [&](int i) { return bars + i * 8; };
-  float *s_ks = reinterpret_cast<float *>(base_ptr + f8::kOffScale);
-  {  // the row's K page scales for this KV head (pages the tiles reach, <= table width)
-    const int npg = min((need + p.block_size - 1) / p.block_size, p.max_blocks);
-    for (int pg = tid; pg < npg; pg += ws::kThreads) {
-      const int32_t pid = __ldg(p.block_tables + static_cast<int64_t>(r) * p.bt_stride + pg);
-      s_ks[pg] = pid >= 0 && pid < p.num_blocks
-                     ? __ldg(p.k_page_scale + static_cast<int64_t>(pid) * p.hkv + hk)
-                     : 0.f;
+  float2 *s_kv = reinterpret_cast<float2 *>(base_ptr + f8::kOffScale);
+  // the row's (K scale, V scale) per page for this KV head (pages the tiles
+  // reach, <= table width); v_ref = the largest V scale (0 when all are 0)
+  const int npg = min((need + p.block_size - 1) / p.block_size, p.max_blocks);
+  if (tid == 0) *v_ref_bits = 0u;
+  __syncthreads();
+  for (int pg = tid; pg < npg; pg += ws::kThreads) {
+    const int32_t pid = __ldg(p.block_tables + static_cast<int64_t>(r) * p.bt_stride + pg);
+    float2 kv = make_float2(0.f, 0.f);
+    if (pid >= 0 && pid < p.num_blocks) {
+      const int64_t si = static_cast<int64_t>(pid) * p.hkv + hk;
+      kv = make_float2(__ldg(p.k_page_scale + si), __ldg(p.v_page_scale + si));
     }
+    s_kv[pg] = kv;
+    if (kv.y > 0.f) atomicMax(v_ref_bits, __float_as_uint(kv.y));   // non-negative floats
   }
 
   if (tid == 0) {
@@ -1001,7 +1006,7 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
     for (int i = 0; i < f8::kNum; ++i) {
       uint32_t count = 1;
       if (i == f8::kQ16) count = 256;
-      if (i == f8::kKcFree || i == f8::kVcFree || i == f8::kK16 || i == f8::kK16 + 1 ||
+      if ((i >= f8::kCodeFree && i < f8::kCodeFree + f8::kSlots) || i == f8::kK16 ||
           i == f8::kV16 || i == f8::kV16 + 1)
         count = f8::kConvThreads;
       if (i == f8::kP || i == f8::kP + 1) count = 128;
@@ -1041,8 +1046,7 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
           tma_load_4d(dst, &qmap, bar(f8::kQ), 0, h0 + hh, q0 + m * kBM, 0, policy);
           tma_load_4d(dst + kHalf, &qmap, bar(f8::kQ), 64, h0 + hh, q0 + m * kBM, 0, policy);
         }
-        // The code buffers hold one tile each, so the tiles after the next are
-        // prefetched into L2: a load then waits on L2, not on HBM.
+        // Code items n = 2j (K of tile j) and 2j + 1 (V of tile j) go to slot n % 3.
         auto prefetch = [&](int jj) {
           if (jj >= nk) return;
           const KvCoord c = kv_coord(p, r, k0, jj);
@@ -1050,45 +1054,51 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
           tma_prefetch_4d(&vmap, 0, hk, c.c2, c.c3);
         };
         prefetch(1);
-        for (int j = 0; j < nk; ++j) {
+        bool stop = false;
+        for (int j = 0; j < nk && !stop; ++j) {
           const KvCoord c = kv_coord(p, r, k0, j);
           if (!c.ok) record_error(p.err, SLOKV_DEVERR_BLOCK_RANGE);
           prefetch(j + 2);
-          if (j >= 1 && !wait(f8::kKcFree, (j - 1) & 1)) break;
-          mbar_arrive_expect_tx(bar(f8::kKc), f8::kCodeTile);
-          tma_load_4d(base + f8::kOffKc, &kmap, bar(f8::kKc), 0, hk, c.c2, c.c3, policy);
-          if (j >= 1 && !wait(f8::kVcFree, (j - 1) & 1)) break;
-          mbar_arrive_expect_tx(bar(f8::kVc), f8::kCodeTile);
-          tma_load_4d(base + f8::kOffVc, &vmap, bar(f8::kVc), 0, hk, c.c2, c.c3, policy);
+          for (int v = 0; v < 2; ++v) {
+            const int n = 2 * j + v, slot = n % f8::kSlots;
+            if (n >= f8::kSlots &&
+                !wait(f8::kCodeFree + slot, ((n - f8::kSlots) / f8::kSlots) & 1)) {
+              stop = true;
+              break;
+            }
+            mbar_arrive_expect_tx(bar(f8::kCode + slot), f8::kCodeTile);
+            tma_load_4d(base + f8::kOffCodes + slot * f8::kCodeTile, v ? &vmap : &kmap,
+                        bar(f8::kCode + slot), 0, hk, c.c2, c.c3, policy);
+          }
         }
       }
     } else if (warp >= 10) {
-      // ---------------- converters: codes -> f16 operand stages ----------------
+      // ---------------- converters: codes -> f16 code values ----------------
       const int ct = tid - 10 * 32;
       for (int j = 0; j < nk; ++j) {
         const int st = j & 1;
-        if (!wait(f8::kKc, j & 1)) break;
-        if (j >= 2 && !wait(f8::kFreeK + st, ((j - 2) >> 1) & 1)) break;
-        widen_tile<false>(base_ptr + f8::kOffKc, base_ptr + f8::kOffK + st * kTile, ct, 1.f, kBN);
+        const int nkk = 2 * j, sk = nkk % f8::kSlots, sv = (nkk + 1) % f8::kSlots;
+        // K: one f16 stage, free once both heads' S(j-1) are done
+        if (!wait(f8::kCode + sk, (nkk / f8::kSlots) & 1)) break;
+        if (j >= 1 && !wait(f8::kFreeK, (j - 1) & 1)) break;
+        widen_tile(base_ptr + f8::kOffCodes + sk * f8::kCodeTile, base_ptr + f8::kOffK, ct, kBN);
         fence_proxy_async_smem();
-        mbar_arrive(bar(f8::kKcFree));
-        mbar_arrive(bar(f8::kK16 + st));
-        const KvCoord c = kv_coord(p, r, k0, j);
-        const float sv =
-            c.ok ? __ldg(p.v_page_scale + static_cast<int64_t>(c.c3) * p.hkv + hk) : 0.f;
-        if (!wait(f8::kVc, j & 1)) break;
+        mbar_arrive(bar(f8::kCodeFree + sk));
+        mbar_arrive(bar(f8::kK16));
+        // V: two f16 stages, stage st free once both heads' PV(j-2) are done
+        if (!wait(f8::kCode + sv, ((nkk + 1) / f8::kSlots) & 1)) break;
         if (j >= 2 && !wait(f8::kFreeV + st, ((j - 2) >> 1) & 1)) break;
-        widen_tile<true>(base_ptr + f8::kOffVc, base_ptr + f8::kOffV + st * kTile, ct, sv,
-                         k_len - j * kBN);
+        widen_tile(base_ptr + f8::kOffCodes + sv * f8::kCodeTile,
+                   base_ptr + f8::kOffV + st * kTile, ct, k_len - j * kBN);
         fence_proxy_async_smem();
-        mbar_arrive(bar(f8::kVcFree));
+        mbar_arrive(bar(f8::kCodeFree + sv));
         mbar_arrive(bar(f8::kV16 + st));
       }
     } else {
       // ---------------- tensor-core issue (lane 0) ----------------
-      auto issue_s = [&](int hh, int j) {
+      auto issue_s = [&](int hh) {
         const uint32_t qa = base + f8::kOffQ + hh * kTile;
-        const uint32_t kb = base + f8::kOffK + (j & 1) * kTile;
+        const uint32_t kb = base + f8::kOffK;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t off = (kk >> 2) * kHalf + (kk & 3) * 32;
@@ -1100,9 +1110,9 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
       bool ok = wait(f8::kQ16, 0) && wait(f8::kK16, 0);
       if (ok && lane == 0) {
         tc::fence_after_sync();
-        issue_s(0, 0);
-        issue_s(1, 0);
-        tc::commit(bar(f8::kFreeK));
+        issue_s(0);
+        issue_s(1);
+        tc::commit(bar(f8::kFreeK));                    // K stage free after both S(0)
       }
       __syncwarp();
       for (int j = 0; j < nk && ok; ++j) {
@@ -1122,17 +1132,17 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
             tc::commit(bar(f8::kPV + hh));
           }
           if (ok && j + 1 < nk) {
-            if (hh == 0) ok = wait(f8::kK16 + ((j + 1) & 1), ((j + 1) >> 1) & 1);
+            if (hh == 0) ok = wait(f8::kK16, (j + 1) & 1);
             if (ok && lane == 0) {
               tc::fence_after_sync();
-              issue_s(hh, j + 1);
+              issue_s(hh);
             }
           }
           __syncwarp();
         }
         if (ok && lane == 0) {
           tc::commit(bar(f8::kFreeV + st));
-          if (j + 1 < nk) tc::commit(bar(f8::kFreeK + ((j + 1) & 1)));
+          if (j + 1 < nk) tc::commit(bar(f8::kFreeK));   // both heads' S(j+1) issued
         }
         __syncwarp();
       }
@@ -1160,6 +1170,7 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
       fence_proxy_async_smem();
     }
     mbar_arrive(bar(f8::kQ16));
+    const float v_ref = __uint_as_float(*v_ref_bits);
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const int qi = m * kBM + row;
     const bool row_ok = qi < q_len;
@@ -1170,8 +1181,10 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
     float m_run = row_ok ? -INFINITY : 0.f, l_run = 0.f;
     uint32_t s[4][32];
     bool ok = true;
-    auto exp_store = [&](float mu, float sl) {
-      const uint64_t sl2 = f32x2(sl, sl), nmu2 = f32x2(-mu, -mu);
+    // P' = 2^(S * sl - mu + lv) of the S row in registers, packed f16 over the
+    // first 64 columns of S; returns the row sum of P'.
+    auto exp_store = [&](float mu, float sl, float lv) {
+      const uint64_t sl2 = f32x2(sl, sl), nmu2 = f32x2(lv - mu, lv - mu);
       uint64_t rs2[4] = {0ull, 0ull, 0ull, 0ull};
 #pragma unroll
       for (int hb = 0; hb < 2; ++hb) {
@@ -1198,7 +1211,13 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
       const int key0 = j * kBN;
       const bool full = key0 + kBN - 1 <= kmax;
       const int kpage = key0 / p.block_size;
-      const float sl = p.scale_log2 * fmaxf(kpage < p.max_blocks ? s_ks[kpage] : 0.f, 1e-30f);
+      const float2 kv = kpage < p.max_blocks ? s_kv[kpage] : make_float2(0.f, 0.f);
+      // a zero K scale (a page of zero codes) must keep masked -inf keys at -inf
+      const float sl = p.scale_log2 * fmaxf(kv.x, 1e-30f);
+      // V scale relative to v_ref (<= 1); a zero-scale page has zero codes,
+      // so any factor works there and 1 keeps its P in the row sum exact
+      const float rv = kv.y > 0.f ? __fdividef(kv.y, v_ref) : 1.f;
+      const float lv = __log2f(rv);
 #pragma unroll
       for (int i = 0; i < 4; ++i) tc::ld32(s_addr + 32 * i, s[i]);
       tc::wait_ld();
@@ -1213,7 +1232,7 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
       float alpha = 1.f, rs = 0.f;
       bool redo = fresh;
       if (!fresh) {
-        rs = exp_store(m_run, sl);
+        rs = exp_store(m_run, sl, lv) / rv;
         redo = __any_sync(0xffffffffu, !(rs <= kSumLimit));
       }
       if (redo) {
@@ -1228,7 +1247,7 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
           m_run = mx;
         }
         if (!fresh) tc::wait_st();
-        rs = exp_store(m_run == -INFINITY ? 0.f : m_run, sl);
+        rs = exp_store(m_run == -INFINITY ? 0.f : m_run, sl, lv) / rv;
       }
       l_run = l_run * alpha + rs;
       if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
@@ -1249,7 +1268,8 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
     ok = ok && wait(f8::kPV + hh, (nk - 1) & 1);
     tc::fence_after_sync();
     if (__all_sync(0xffffffffu, ok)) {
-      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      // O is in units of v_ref: out = O * v_ref / l
+      const float inv = l_run > 0.f ? v_ref / l_run : 0.f;
       Tq *orow = static_cast<Tq *>(p.out) + static_cast<int64_t>(q0 + qi) * p.out_st +
                  static_cast<int64_t>(h0 + hh) * p.out_sh;
 #pragma unroll
@@ -1341,7 +1361,7 @@ int launch_fp8(const Params &p, const CUtensorMap &qm, const CUtensorMap &km,
          fa.numRegs == ws::kRegsLaunch;
   });
   if (!ok) return SLOKV_ERR_UNSUPPORTED;
-  const int64_t smem = f8::kSmemFixed + 4 * static_cast<int64_t>(p.max_blocks);
+  const int64_t smem = f8::kSmemFixed + 8 * static_cast<int64_t>(p.max_blocks);
   if (smem > ws::kSmemMax) return SLOKV_ERR_UNSUPPORTED;
   if (p.order != nullptr)
     prefill_schedule_kernel<<<1, kSchedThreads, 0, stream>>>(p.cu_q, p.cu_k, rows, p.m_tiles,

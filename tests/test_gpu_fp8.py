@@ -357,10 +357,12 @@ def _page_copy_prefill(pkg, q, dev, tables, cu_q, cu_k, max_q, max_k, scale):
 
 
 @pytest.mark.parametrize("qdt", [torch.bfloat16, torch.float16])
-def test_fused_fp8_prefill_equals_page_copy_path(pkg, qdt):
-    """The fused-dequant FP8 prefill (slokv_paged_prefill_fp8) against the same
-    arithmetic done as page copy + f16 prefill: identical fp32 results, so the
-    outputs differ at most by the final rounding (f16 then bf16 vs bf16 once)."""
+def test_fused_fp8_prefill_against_page_copy_path(pkg, qdt):
+    """The fused-dequant FP8 prefill (slokv_paged_prefill_fp8: V kept as exact
+    code values, its page scale applied to P) against the same attention done
+    as page copy (V widened to f16(code x scale)) + f16 prefill: both within the
+    FP8 bar of the fp32 oracle on the dequantised pool, the fused one at least
+    as close to it (one rounding fewer per V element)."""
     c = _mixed_fp8_case(3400, [], [(1024, 300), (0, 77), (3000, 2048), (255, 1), (4095, 129)])
     dev = _gpu(_pools(c["NB"], H=c["Hkv"]))
     hk, hv, hs = c["hist"]
@@ -377,18 +379,15 @@ def test_fused_fp8_prefill_equals_page_copy_path(pkg, qdt):
     torch.cuda.synchronize()
     assert pkg.read_device_errors() == 0
     assert fused.dtype == qdt and torch.isfinite(fused.float()).all()
-    if qdt == torch.float16:
-        assert torch.equal(fused, two)
-    else:
-        ref = two.to(qdt).float()
-        d = (fused.float() - ref).abs()
-        # bf16(x) against bf16(f16(x)): at most one bf16 spacing (2^-7 relative)
-        assert (d <= 2 ** -7 * ref.abs() + 1e-30).all(), d.max().item()
-        assert (d == 0).float().mean().item() >= 0.99
     exp = O.varlen(c["q"].to(qdt), O.fp8_dequant(dev[0].cpu(), dev[2].cpu()),
                    O.fp8_dequant(dev[1].cpu(), dev[3].cpu()), c["meta"]["prefill_cu_q"],
                    c["meta"]["prefill_cu_k"], scale, c["meta"]["prefill_tables"])
     assert_fp8_close(fused, exp)
+    assert_fp8_close(two.to(qdt), exp)
+    e_fused = (fused.float().cpu() - exp).abs().mean().item()
+    e_two = (two.to(qdt).float().cpu() - exp).abs().mean().item()
+    print(f"mean |err| vs the fp32 oracle: fused {e_fused:.3e}, page copy {e_two:.3e}")
+    assert e_fused <= 1.05 * e_two + 1e-6
 
 
 def test_fused_fp8_prefill_flags_bad_block_id(pkg):
@@ -407,3 +406,27 @@ def test_fused_fp8_prefill_flags_bad_block_id(pkg):
     torch.cuda.synchronize()
     assert pkg.read_device_errors() & pkg._lib.DEVERR_BLOCK_RANGE
     assert torch.isfinite(out.float()).all()
+
+
+def test_fp8_decode_plain_bar_without_outliers(pkg):
+    """On N(0, 1) K/V without the config-4 outliers the outputs stay O(1), so the
+    FP8 decode meets the plain bf16 attention bar of the fp32 oracle on the
+    dequantised pool: max |err| <= 2e-2, mean |err| <= 2e-3."""
+    c = _fp8_case(3600, 12, 1024, 8192)
+    k = kv_values(3601, tuple(c["k"].shape), outlier_frac=0.0)
+    v = kv_values(3603, tuple(c["v"].shape), outlier_frac=0.0)
+    ref = _pools(c["NB"], H=c["Hkv"])
+    O.fp8_append(k, v, *ref, c["slots"])
+    dev = _gpu(_pools(c["NB"], H=c["Hkv"]))
+    pkg.store_kvcache_fp8(k.cuda(), v.cuda(), *dev, c["slots"].cuda())
+    _assert_pool_equal(dev, ref)
+    scale = 128 ** -0.5
+    out = pkg.flash_attn_with_kvcache_fp8(c["q"].cuda().unsqueeze(1), *dev,
+                                          cache_seqlens=c["lens"].cuda(),
+                                          block_table=c["tables"].cuda(), softmax_scale=scale)
+    torch.cuda.synchronize()
+    expect = O.fp8_decode(c["q"].unsqueeze(1), *ref, c["lens"], c["tables"], scale)
+    err = (out.float().cpu().reshape(expect.shape) - expect).abs()
+    assert err.max().item() <= MAX_TOL and err.mean().item() <= MEAN_TOL, (
+        f"max {err.max().item():.3e} mean {err.mean().item():.3e}")
+    assert pkg.read_device_errors() == 0
