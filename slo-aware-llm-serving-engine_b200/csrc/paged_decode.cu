@@ -491,15 +491,26 @@ __global__ void __launch_bounds__(Ring<kFp8>::kWarpsPerCta * 32, 1)
           w0[nt] = lds128(kb + swz128(nt * 8 + g, c));
           w1[nt] = lds128(kb + swz128(nt * 8 + g, c + 4));
         }
+        // Two accumulator sets (dims 0-63 and 64-127), summed after: eight
+        // dependent MMA chains of four instead of four of eight.
+        float sc2[4][4];
 #pragma unroll
-        for (int ks = 0; ks < 8; ++ks) {
+        for (int nt = 0; nt < 4; ++nt) sc2[nt][0] = sc2[nt][1] = sc2[nt][2] = sc2[nt][3] = 0.f;
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks) {
 #pragma unroll
           for (int nt = 0; nt < 4; ++nt) {
-            uint32_t b0, b1;
-            e4m3x4_to_f16x2x2(word(ks < 4 ? w0[nt] : w1[nt], ks & 3), b0, b1);
+            uint32_t b0, b1, b2, b3;
+            e4m3x4_to_f16x2x2(word(w0[nt], ks), b0, b1);
+            e4m3x4_to_f16x2x2(word(w1[nt], ks), b2, b3);
             MQ::run(sc[nt], qa[ks], b0, b1);
+            MQ::run(sc2[nt], qa[ks + 4], b2, b3);
           }
         }
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+          for (int e2 = 0; e2 < 4; ++e2) sc[nt][e2] += sc2[nt][e2];
       }
 
       // ---- online softmax (log2 domain) ----

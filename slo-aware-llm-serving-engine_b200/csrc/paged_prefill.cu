@@ -899,7 +899,16 @@ enum Bar {
 // of every page of the table row
 constexpr int kOffScale = kTilesBytes + kNum * 8 + 16;
 constexpr int kSmemFixed = 1024 + kOffScale;        // + 8 bytes per page of the table row
-constexpr int kConvThreads = 64;                    // warps 10 and 11
+// Warps 0-7 softmax, 8 MMA issue, 9 TMA, 10 .. 10 + kConvWarps - 1 widen codes.
+// Register split (setmaxnreg): launch kRegsLaunch a thread; the softmax
+// warpgroups rise to kRegsSoftmax, every other warp drops to kRegsIssue.
+constexpr int kConvWarps = 6;
+constexpr int kConvThreads = kConvWarps * 32;
+constexpr int kThreads = (10 + kConvWarps) * 32;
+constexpr int kRegsLaunch = 128, kRegsIssue = 48, kRegsSoftmax = 208;
+static_assert(2 * 128 * kRegsSoftmax + (kThreads - 256) * kRegsIssue <= kThreads * kRegsLaunch,
+              "register split exceeds the launch allocation");
+static_assert(kThreads * kRegsLaunch <= 65536, "launch allocation exceeds the register file");
 }  // namespace f8
 
 // Widen one 128-key tile of E4M3 codes (128-byte rows, 128-byte swizzle) into
@@ -930,7 +939,7 @@ __device__ __forceinline__ void widen_tile(const uint8_t *codes, uint8_t *dst, i
 }
 
 template <typename Tq>
-__global__ void __launch_bounds__(ws::kThreads, 1)
+__global__ void __launch_bounds__(f8::kThreads, 1)
     paged_prefill_fp8_kernel(const __grid_constant__ CUtensorMap qmap,
                              const __grid_constant__ CUtensorMap kmap,
                              const __grid_constant__ CUtensorMap vmap, const Params p) {
@@ -988,7 +997,7 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
   const int npg = min((need + p.block_size - 1) / p.block_size, p.max_blocks);
   if (tid == 0) *v_ref_bits = 0u;
   __syncthreads();
-  for (int pg = tid; pg < npg; pg += ws::kThreads) {
+  for (int pg = tid; pg < npg; pg += f8::kThreads) {
     const int32_t pid = __ldg(p.block_tables + static_cast<int64_t>(r) * p.bt_stride + pg);
     float2 kv = make_float2(0.f, 0.f);
     if (pid >= 0 && pid < p.num_blocks) {
@@ -1035,7 +1044,7 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
   };
 
   if (warp >= 8) {
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(ws::kRegsIssue));
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(f8::kRegsIssue));
     if (warp == 9) {
       // ---------------- TMA producer: q once, then the code tiles ----------------
       if (lane == 0) {
@@ -1148,7 +1157,7 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
       }
     }
   } else {
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(ws::kRegsSoftmax));
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(f8::kRegsSoftmax));
     const int hh = warp >> 2;
     const int row = tid & 127;
     // q -> f16 in place (one row of one head per thread), then release the Q stage
@@ -1353,12 +1362,12 @@ int launch_fp8(const Params &p, const CUtensorMap &qm, const CUtensorMap &km,
   static bool ok = false;
   std::call_once(once, [] {
     cudaFuncAttributes fa;
-    // the register split hands out exactly the launch allocation (see ws::kRegsLaunch)
+    // the register split hands out exactly the launch allocation (see f8::kRegsLaunch)
     ok = cudaFuncSetAttribute(paged_prefill_fp8_kernel<Tq>,
                               cudaFuncAttributeMaxDynamicSharedMemorySize, ws::kSmemMax) ==
              cudaSuccess &&
          cudaFuncGetAttributes(&fa, paged_prefill_fp8_kernel<Tq>) == cudaSuccess &&
-         fa.numRegs == ws::kRegsLaunch;
+         fa.numRegs == f8::kRegsLaunch;
   });
   if (!ok) return SLOKV_ERR_UNSUPPORTED;
   const int64_t smem = f8::kSmemFixed + 8 * static_cast<int64_t>(p.max_blocks);
@@ -1368,7 +1377,7 @@ int launch_fp8(const Params &p, const CUtensorMap &qm, const CUtensorMap &km,
                                                                const_cast<int32_t *>(p.order));
   const int64_t blocks = static_cast<int64_t>(rows) * p.m_tiles * (p.hq / 2);
   if (blocks > 0x7fffffff) return SLOKV_ERR_UNSUPPORTED;
-  paged_prefill_fp8_kernel<Tq><<<static_cast<unsigned>(blocks), ws::kThreads,
+  paged_prefill_fp8_kernel<Tq><<<static_cast<unsigned>(blocks), f8::kThreads,
                                  static_cast<unsigned>(smem), stream>>>(qm, km, vm, p);
   return cudaGetLastError() == cudaSuccess ? SLOKV_OK : SLOKV_ERR_CUDA;
 }
