@@ -915,11 +915,14 @@ static_assert(kThreads * kRegsLaunch <= 65536, "launch allocation exceeds the re
 // the f16 operand layout (two 64-dim halves of 128-byte rows, 128-byte
 // swizzle), rows >= valid written as zeros (stale pool bytes past a row's keys
 // may hold NaN codes).  Thread ct of the kConvThreads converters takes 16-code
-// chunks ct, ct + 64, ...
+// chunks g = ct, ct + kConvThreads, ...: chunk (g >> 3) & 7 of row
+// (g & 7) + 8 (g >> 6), so the 8 lanes of a shared-memory phase touch one
+// chunk of 8 consecutive rows, whose swizzled positions are all distinct for
+// the load and for both stores (no bank conflict).
 __device__ __forceinline__ void widen_tile(const uint8_t *codes, uint8_t *dst, int ct, int valid) {
 #pragma unroll 4
   for (int g = ct; g < kBN * 8; g += f8::kConvThreads) {
-    const int row = g >> 3, c = g & 7;
+    const int row = (g & 7) | ((g >> 6) << 3), c = (g >> 3) & 7;
     uint4 lo = make_uint4(0, 0, 0, 0), hi = lo;
     if (row < valid) {
       const uint4 w = *reinterpret_cast<const uint4 *>(codes + swz128(row, c));
@@ -1226,6 +1229,7 @@ __global__ void __launch_bounds__(f8::kThreads, 1)
       // V scale relative to v_ref (<= 1); a zero-scale page has zero codes,
       // so any factor works there and 1 keeps its P in the row sum exact
       const float rv = kv.y > 0.f ? __fdividef(kv.y, v_ref) : 1.f;
+      const float irv = kv.y > 0.f ? __fdividef(v_ref, kv.y) : 1.f;
       const float lv = __log2f(rv);
 #pragma unroll
       for (int i = 0; i < 4; ++i) tc::ld32(s_addr + 32 * i, s[i]);
@@ -1241,7 +1245,7 @@ __global__ void __launch_bounds__(f8::kThreads, 1)
       float alpha = 1.f, rs = 0.f;
       bool redo = fresh;
       if (!fresh) {
-        rs = exp_store(m_run, sl, lv) / rv;
+        rs = exp_store(m_run, sl, lv) * irv;
         redo = __any_sync(0xffffffffu, !(rs <= kSumLimit));
       }
       if (redo) {
@@ -1256,7 +1260,7 @@ __global__ void __launch_bounds__(f8::kThreads, 1)
           m_run = mx;
         }
         if (!fresh) tc::wait_st();
-        rs = exp_store(m_run == -INFINITY ? 0.f : m_run, sl, lv) / rv;
+        rs = exp_store(m_run == -INFINITY ? 0.f : m_run, sl, lv) * irv;
       }
       l_run = l_run * alpha + rs;
       if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {

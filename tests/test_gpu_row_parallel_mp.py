@@ -1,7 +1,7 @@
 """Fused row-parallel linear + all-reduce with one process per GPU (NCCL group
 for the handshake, CUDA IPC symmetric buffers, P2P stores over NVLink), against
-the reference's F.linear + dist.all_reduce and the fp32 product.  Needs >= 2
-GPUs; skipped otherwise.  The process group has a short timeout and every wait
+the reference's F.linear + dist.all_reduce and the fp32 product, at TP = 2, 4
+and 8 as the box has GPUs (each size skipped otherwise).  The process group has a short timeout and every wait
 in the kernel is bounded, so a rank that fails ends the others with an error."""
 import datetime
 import os
@@ -86,10 +86,12 @@ def _worker(rank, world, port, queue):
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
-                    reason="needs two GPUs")
-def test_row_parallel_two_processes_match_nccl():
-    world = 2
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_row_parallel_processes_match_nccl(world):
+    """One process per GPU for TP = 2, 4 and 8 (each skipped without that many
+    GPUs): the fused call against F.linear + dist.all_reduce."""
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
     queue = ctx.Queue()
     port = _free_port()
