@@ -168,16 +168,17 @@ __global__ void __launch_bounds__(256, 2) kv_append_fp8_kernel(
 // ---- the same append in three launches, for calls with long runs ------------
 //
 // A prefill chunk writes runs of up to a block (256 tokens) per (block, head,
-// K|V); one warp per run walks them serially.  Here every (token, head, K|V)
-// warp works on its own token: (1) its row's amax goes into a per-(block, head,
-// K|V) word with atomicMax on the float bits (non-negative floats order like
-// their bit patterns, so the word ends as the exact run amax); (2) each warp
-// derives s_new = max(s_old, amax / 448) -- the same value for every warp of
-// the run, s_old being 0 for a run that starts at offset 0 -- and encodes its
-// token; the run's first warp re-encodes the block's
-// earlier positions when the scale grows; (3) the run's first warp stores s_new
-// and clears the word.  Codes and scales are the one-launch kernel's, bit for
-// bit.  `amax_ws` is num_blocks * hkv * 2 words, zero between calls.
+// K|V); one warp per run walks them serially.  Here one warp per token works
+// on the token's 2 * hkv (head, K|V) rows: (1) each row's amax goes into a
+// per-(block, head, K|V) word with atomicMax on the float bits (non-negative
+// floats order like their bit patterns, so the word ends as the exact run
+// amax); (2) each row derives s_new = max(s_old, amax / 448) -- the same value
+// for every token of the run, s_old being 0 for a run that starts at offset 0
+// -- and encodes the token; the run's first token re-encodes the block's
+// earlier positions of a row whose scale grows; (3) one thread per run start
+// and row stores s_new and clears the word.  Codes and scales are the
+// one-launch kernel's, bit for bit.  `amax_ws` is num_blocks * hkv * 2 words,
+// zero between calls.
 
 struct RunToken {
   bool valid;       // a slot inside the pool
@@ -200,34 +201,53 @@ __device__ __forceinline__ RunToken run_token(const int32_t *slots, int i, int32
   return t;
 }
 
+// One warp per token, looping over its 2 * hkv (head, K|V) rows four at a
+// time: the token's slot is read once, the four rows' loads are in flight
+// together, and lanes 0-3 issue the four rows' atomics.
 template <typename T>
 __global__ void __launch_bounds__(256) kv_append_fp8_amax_kernel(
     const T *__restrict__ key, int64_t key_stride, const T *__restrict__ value,
     int64_t value_stride, const int32_t *__restrict__ slots, int32_t num_tokens, int32_t hkv,
     int32_t block_size, int32_t num_blocks, uint32_t *__restrict__ amax_ws, uint32_t *err) {
   const int lane = threadIdx.x & 31;
-  const int64_t wid = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-  if (wid >= static_cast<int64_t>(num_tokens) * hkv * 2) return;
-  const int which = static_cast<int>(wid & 1);
-  const int h = static_cast<int>((wid >> 1) % hkv);
-  const int i = static_cast<int>((wid >> 1) / hkv);
+  const int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  if (i >= num_tokens) return;
   const int32_t slot = __ldg(slots + i);
   if (slot < 0 || slot >= static_cast<int64_t>(num_blocks) * block_size) {
-    if (slot != -1 && lane == 0 && h == 0 && which == 0) record_error(err, SLOKV_DEVERR_SLOT_RANGE);
+    if (slot != -1 && lane == 0) record_error(err, SLOKV_DEVERR_SLOT_RANGE);
     return;
   }
-  const T *src = (which ? value + i * value_stride : key + i * key_stride) + h * kHeadDim + lane * 4;
-  const float4 v = load4<T>(src);
-  // seeded with 0 as in the one-launch kernel: NaN elements drop out of the max
-  // (fmaxf keeps the non-NaN operand), so the word never holds NaN bits
-  float a = fmaxf(fmaxf(fmaxf(0.f, fabsf(v.x)), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+  uint32_t *words = amax_ws + static_cast<int64_t>(slot / block_size) * hkv * 2;
+  const int rows = 2 * hkv;                       // row r: head r / 2, K (r even) or V
+  for (int r0 = 0; r0 < rows; r0 += 4) {
+    float a[4];
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
-  if (lane == 0)
-    atomicMax(amax_ws + (static_cast<int64_t>(slot / block_size) * hkv + h) * 2 + which,
-              __float_as_uint(a));
+    for (int u = 0; u < 4; ++u) {
+      const int r = r0 + u;
+      a[u] = 0.f;
+      if (r < rows) {
+        const T *src = ((r & 1) ? value + i * value_stride : key + i * key_stride) +
+                       (r >> 1) * kHeadDim + lane * 4;
+        const float4 v = load4<T>(src);
+        // seeded with 0 as in the one-launch kernel: NaN elements drop out of
+        // the max (fmaxf keeps the non-NaN operand), so no word holds NaN bits
+        a[u] = fmaxf(fmaxf(fmaxf(0.f, fabsf(v.x)), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int u = 0; u < 4; ++u) a[u] = fmaxf(a[u], __shfl_xor_sync(0xffffffffu, a[u], o));
+    const float mine = lane == 0 ? a[0] : lane == 1 ? a[1] : lane == 2 ? a[2] : a[3];
+    if (lane < 4 && r0 + lane < rows) atomicMax(words + r0 + lane, __float_as_uint(mine));
+  }
 }
 
+// One warp per token over its 2 * hkv rows: s_new = max(s_old, amax / 448) of
+// each row's (block, head, K|V) -- the same value for every token of the run,
+// s_old being 0 for a run that starts at offset 0 -- then the token's codes;
+// the run's first token re-encodes the block's earlier positions of a row
+// whose scale grows.
 template <typename T>
 __global__ void __launch_bounds__(256, 2) kv_append_fp8_encode_kernel(
     const T *__restrict__ key, int64_t key_stride, const T *__restrict__ value,
@@ -236,53 +256,57 @@ __global__ void __launch_bounds__(256, 2) kv_append_fp8_encode_kernel(
     const int32_t *__restrict__ slots, int32_t num_tokens, int32_t hkv, int32_t block_size,
     int32_t num_blocks, const uint32_t *__restrict__ amax_ws, uint32_t *err) {
   const int lane = threadIdx.x & 31;
-  const int64_t wid = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-  if (wid >= static_cast<int64_t>(num_tokens) * hkv * 2) return;
-  const int which = static_cast<int>(wid & 1);
-  const int h = static_cast<int>((wid >> 1) % hkv);
-  const int i = static_cast<int>((wid >> 1) / hkv);
-  const RunToken tk = run_token(slots, i, block_size, static_cast<int64_t>(num_blocks) * block_size);
+  const int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  if (i >= num_tokens) return;
+  const RunToken tk = run_token(slots, static_cast<int>(i), block_size,
+                                static_cast<int64_t>(num_blocks) * block_size);
   if (!tk.valid) return;
-  const int64_t si = static_cast<int64_t>(tk.blk) * hkv + h;
   // The run starts at offset 0 (a freshly assigned page, stored scale ignored)
   // iff the token tk.off places earlier holds offset 0 of the same block: runs
   // are adjacent with consecutive offsets and a block has one run per call.
   const bool fresh = i >= tk.off && __ldg(slots + i - tk.off) ==
                                         static_cast<int64_t>(tk.blk) * block_size;
-  const float s_old = fresh ? 0.f : (which ? v_scale : k_scale)[si];
-  const float s_new = fmaxf(s_old, __fdiv_rn(__uint_as_float(amax_ws[si * 2 + which]), 448.0f));
   const int64_t row = static_cast<int64_t>(hkv) * kHeadDim;
   const int d0 = lane * 4;
-  uint8_t *base = (which ? v_codes : k_codes) + static_cast<int64_t>(tk.blk) * block_size * row +
-                  h * kHeadDim + d0;
+  const int rows = 2 * hkv;
   bool bad = false;
-  if (tk.start && s_new > s_old && s_old > 0.f) {   // earlier positions of the block
-    constexpr int kUnroll = 8;
-    auto reencode = [&](uint32_t c) {
-      float4 v;
-      v.x = __fmul_rn(e4m3_decode(c & 0xffu), s_old);
-      v.y = __fmul_rn(e4m3_decode((c >> 8) & 0xffu), s_old);
-      v.z = __fmul_rn(e4m3_decode((c >> 16) & 0xffu), s_old);
-      v.w = __fmul_rn(e4m3_decode(c >> 24), s_old);
-      return encode4(v, s_new, bad);
-    };
-    int p = 0;
-    for (; p + kUnroll <= tk.off; p += kUnroll) {
-      uint32_t c[kUnroll];
+  for (int r0 = 0; r0 < rows; r0 += 4) {
+    float4 v[4];
+    float s_old[4], s_new[4];
 #pragma unroll
-      for (int u = 0; u < kUnroll; ++u) c[u] = *reinterpret_cast<const uint32_t *>(base + (p + u) * row);
-#pragma unroll
-      for (int u = 0; u < kUnroll; ++u)
-        *reinterpret_cast<uint32_t *>(base + (p + u) * row) = reencode(c[u]);
+    for (int u = 0; u < 4; ++u) {
+      const int r = r0 + u;
+      if (r >= rows) continue;
+      const int h = r >> 1;
+      const int64_t si = static_cast<int64_t>(tk.blk) * hkv + h;
+      v[u] = load4<T>(((r & 1) ? value + i * value_stride : key + i * key_stride) +
+                      h * kHeadDim + d0);
+      s_old[u] = fresh ? 0.f : ((r & 1) ? v_scale : k_scale)[si];
+      s_new[u] = fmaxf(s_old[u], __fdiv_rn(__uint_as_float(amax_ws[si * 2 + (r & 1)]), 448.0f));
     }
-    for (; p < tk.off; ++p) {
-      uint32_t *cp = reinterpret_cast<uint32_t *>(base + p * row);
-      *cp = reencode(*cp);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int r = r0 + u;
+      if (r >= rows) continue;
+      uint8_t *base = ((r & 1) ? v_codes : k_codes) +
+                      static_cast<int64_t>(tk.blk) * block_size * row + (r >> 1) * kHeadDim + d0;
+      if (tk.start && s_new[u] > s_old[u] && s_old[u] > 0.f) {   // earlier positions
+        const float so = s_old[u], sn = s_new[u];
+        for (int p = 0; p < tk.off; ++p) {
+          uint32_t *cp = reinterpret_cast<uint32_t *>(base + p * row);
+          const uint32_t c = *cp;
+          float4 w;
+          w.x = __fmul_rn(e4m3_decode(c & 0xffu), so);
+          w.y = __fmul_rn(e4m3_decode((c >> 8) & 0xffu), so);
+          w.z = __fmul_rn(e4m3_decode((c >> 16) & 0xffu), so);
+          w.w = __fmul_rn(e4m3_decode(c >> 24), so);
+          *cp = encode4(w, sn, bad);
+        }
+      }
+      *reinterpret_cast<uint32_t *>(base + tk.off * row) =
+          encode4(v[u], s_new[u] > 0.f ? s_new[u] : 1.0f, bad);
     }
   }
-  const T *src = (which ? value + i * value_stride : key + i * key_stride) + h * kHeadDim + d0;
-  *reinterpret_cast<uint32_t *>(base + tk.off * row) =
-      encode4(load4<T>(src), s_new > 0.f ? s_new : 1.0f, bad);
   if (__any_sync(0xffffffffu, bad) && lane == 0) record_error(err, SLOKV_DEVERR_NONFINITE);
 }
 
@@ -426,7 +450,7 @@ extern "C" int slokv_kv_append_fp8_runs(const void *key, int64_t key_row_stride,
       ((reinterpret_cast<uintptr_t>(k_codes) | reinterpret_cast<uintptr_t>(v_codes)) & 3))
     return SLOKV_ERR_ALIGNMENT;
   const int64_t units = static_cast<int64_t>(num_tokens) * num_kv_heads * 2;
-  const unsigned warp_grid = static_cast<unsigned>((units * 32 + 255) / 256);
+  const unsigned warp_grid = static_cast<unsigned>((static_cast<int64_t>(num_tokens) * 32 + 255) / 256);
   const unsigned unit_grid = static_cast<unsigned>((units + 255) / 256);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   auto *kc = static_cast<uint8_t *>(k_codes);
