@@ -241,23 +241,24 @@ int slokv_fp8_pages_dequant(const void *k_codes, const void *v_codes, int64_t k_
                             void *dst_k, void *dst_v, float *dst_k_scale, uint32_t *dev_error,
                             void *stream);
 
-/* Prefix-cache prefill over an FP8 pool with the dequantisation fused into the
- * tile loads (the prefill half of flash_attn_varlen_func / forward_mixed,
+/* Prefix-cache prefill over an FP8 pool, reading the code pages directly (the
+ * prefill half of flash_attn_varlen_func / forward_mixed,
  * nanovllm/layers/attention.py:69-74, nanovllm/layers/mixed_attention.py:123-133,
  * when the pool is FP8).  Arguments as slokv_paged_prefill with paged K/V, the
  * pool being k_codes / v_codes (uint8 [num_blocks, block_size, Hkv, 128],
  * block strides in bytes, 16-byte multiples) and its fp32 scales k_scale /
  * v_scale [num_blocks, Hkv].  Each 128-key tile of codes is TMA-loaded from its
- * page and widened in shared memory: K to its unscaled code values (exact in
- * f16) with the logits of the page's keys multiplied by its K scale, V to
- * f16(fp32(decode(code)) * V scale); the MMAs run in f16 (a bf16 q is
- * converted to f16 in the kernel) and out is written in q_dtype (bf16 or
- * f16).  The same arithmetic as slokv_fp8_pages_dequant followed by
- * slokv_paged_prefill(f16, k_page_scale), without the page buffer.  Even GQA
- * groups only, block_size % 128 == 0, max_blocks_per_seq <= 460 (one K scale
- * per page in shared memory; pass the pages the longest row reaches), else
- * SLOKV_ERR_UNSUPPORTED.  An id outside the pool loads zero codes (scale 0)
- * and sets SLOKV_DEVERR_BLOCK_RANGE. */
+ * page.  S = Q K^T runs on the K codes (E4M3 x E4M3 MMAs, fp32 accumulate)
+ * against each query row split into two E4M3 rows (a power-of-two row scale,
+ * hi = e4m3(q), lo = e4m3(q - hi): exact for every element at least 2^-10 of
+ * its row's largest), times the page's K scale; V codes are widened in shared
+ * memory to their f16 values and the page's V scale applied to P.  Out is
+ * written in q_dtype (bf16 or f16).  Within the FP8 attention bar of the fp32
+ * result on the dequantised pool.  Even GQA groups only, block_size % 128 == 0,
+ * max_blocks_per_seq <= 4330 (a K and a V scale per page in shared memory;
+ * pass the pages the longest row reaches), else SLOKV_ERR_UNSUPPORTED.  An id
+ * outside the pool loads zero codes (scale 0) and sets
+ * SLOKV_DEVERR_BLOCK_RANGE. */
 int slokv_paged_prefill_fp8(void *out, int64_t out_stride_t, int64_t out_stride_h,
                             const void *q, int64_t q_stride_t, int64_t q_stride_h, int64_t q_rows,
                             const void *k_codes, const void *v_codes, int64_t k_block_stride,

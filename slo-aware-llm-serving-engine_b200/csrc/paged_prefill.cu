@@ -862,44 +862,47 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
 }
 
 
-// ---- FP8-E4M3 pool: the two-head kernel with the dequantisation in the tile load --
+// ---- FP8-E4M3 pool: the two-head kernel reading the code pages directly -----
 //
-// Replaces the page copy of the FP8 prefix-cache path: K and V pages of E4M3
-// codes are TMA-loaded as they lie in the pool (16 KB per 128-key tile) into a
-// 3-slot code ring, and the two otherwise idle warps of the issue warpgroup
-// (10 and 11) widen them in shared memory into the f16 stages the tensor core
-// reads.  Both K and V are widened to their unscaled code values (every E4M3
-// value is exact in f16), so the widening is one conversion per code pair.  The
-// scales enter the softmax instead, per 128-key tile (a tile never spans two
-// 256-token pages):
-//   * K: the tile's logits are S * k_scale (as in the FP8 decode);
-//   * V: P of the tile's keys is multiplied by r = v_scale / v_ref, with v_ref
-//     the largest V scale among the row's pages, by shifting the exponent of
-//     P = 2^(s - m + log2 r) (r <= 1, so P stays <= 2^8 in f16), the row sum
-//     taking P / r, and the output O * v_ref / l.
-// P and the V codes are f16 (11 bits, one rounding on P), the MMAs run in f16
-// (kind::f16): a bf16 q is converted to f16 in shared memory by the softmax
-// warps once per CTA and the output is written in q's dtype.  The pipeline is
-// the two-head kernel's (warps 0-7 softmax, 8 MMA issue, 9 TMA) with one f16 K
-// stage (the K widening of tile j+1 overlaps the softmax of tile j) and two
-// f16 V stages; tiles two ahead are prefetched into L2.
+// Replaces the page copy of the FP8 prefix-cache path.  K and V pages of E4M3
+// codes are TMA-loaded as they lie in the pool (16 KB per 128-key tile, one
+// head) into two-slot K and V code rings; tiles two ahead are prefetched into
+// L2.
+//  * S = Q K^T runs on the codes themselves (tcgen05 kind::f8f6f4, fp32
+//    accumulate): each softmax thread splits its query row, scaled by a power of
+//    two 2^e so its largest element lies in [128, 256), into two E4M3 rows,
+//    hi = e4m3(q 2^e) and lo = e4m3(q 2^e - hi), written over the row's q in
+//    shared memory.  A bf16 (8-bit) or f16 element is then exactly hi + lo
+//    whenever it is at least 2^-10 of the row's largest (below that the split
+//    drops bits under 2^-17 of the row max), so S = (hi K^T + lo K^T) 2^-e: two
+//    MMAs of K = 32 per 32 dims, the tensor time of one f16 MMA, and no K
+//    conversion.
+//  * V is widened to its unscaled code values (exact in f16) by six converter
+//    warps, rows past the keys zeroed (stale pool bytes may hold NaN codes).
+//  * Scales in the softmax, per 128-key tile (a tile never spans two pages):
+//    logits S * k_scale * 2^-e; P multiplied by r = v_scale / v_ref (v_ref the
+//    largest V scale among the row's pages) through the exponent,
+//    P = 2^(s - m + log2 r) (r <= 1, so P stays <= 2^8 in f16), the row sum
+//    taking P / r and the output O * v_ref / l.  PV runs in f16 (kind::f16).
+//  * CTA: 16 warps -- 0-7 softmax (two heads), 8 MMA issue, 9 TMA, 10-15
+//    converters -- with a setmaxnreg split of 208 / 48 on a 128-register launch.
+//  * The output is written in q's dtype.
 namespace f8 {
 constexpr int kCodeTile = kBN * kD;                  // 16 KB of codes per 128-key tile
-constexpr int kSlots = 3;                            // code ring: K(j), V(j), K(j+1), ...
-constexpr int kOffQ = 0;
-constexpr int kOffK = 2 * kTile;                     // one f16 K stage
-constexpr int kOffV = 3 * kTile;                     // two f16 V stages
-constexpr int kOffCodes = 5 * kTile;
-constexpr int kTilesBytes = kOffCodes + kSlots * kCodeTile;   // 208 KB
+constexpr int kOffQ = 0;                             // per head: hi rows | lo rows
+constexpr int kOffKc = 2 * kTile;                    // K codes, two slots
+constexpr int kOffVc = kOffKc + 2 * kCodeTile;       // V codes, two slots
+constexpr int kOffV = kOffVc + 2 * kCodeTile;        // two f16 V stages
+constexpr int kTilesBytes = kOffV + 2 * kTile;       // 192 KB
 enum Bar {
-  kQ = 0, kQ16 = 1, kCode = 2, kCodeFree = 5, kK16 = 8, kV16 = 9, kFreeK = 11, kFreeV = 12,
+  kQ = 0, kQ8 = 1, kKc = 2, kVc = 4, kFreeK = 6, kVcFree = 8, kV16 = 10, kFreeV = 12,
   kS = 14, kP = 16, kPV = 18, kNum = 20
 };
 // after the barriers: TMEM slot, abort flag, v_ref; then (k scale, v scale)
 // of every page of the table row
 constexpr int kOffScale = kTilesBytes + kNum * 8 + 16;
 constexpr int kSmemFixed = 1024 + kOffScale;        // + 8 bytes per page of the table row
-// Warps 0-7 softmax, 8 MMA issue, 9 TMA, 10 .. 10 + kConvWarps - 1 widen codes.
+// Warps 0-7 softmax, 8 MMA issue, 9 TMA, 10 .. 10 + kConvWarps - 1 widen V.
 // Register split (setmaxnreg): launch kRegsLaunch a thread; the softmax
 // warpgroups rise to kRegsSoftmax, every other warp drops to kRegsIssue.
 constexpr int kConvWarps = 6;
@@ -913,12 +916,11 @@ static_assert(kThreads * kRegsLaunch <= 65536, "launch allocation exceeds the re
 
 // Widen one 128-key tile of E4M3 codes (128-byte rows, 128-byte swizzle) into
 // the f16 operand layout (two 64-dim halves of 128-byte rows, 128-byte
-// swizzle), rows >= valid written as zeros (stale pool bytes past a row's keys
-// may hold NaN codes).  Thread ct of the kConvThreads converters takes 16-code
-// chunks g = ct, ct + kConvThreads, ...: chunk (g >> 3) & 7 of row
-// (g & 7) + 8 (g >> 6), so the 8 lanes of a shared-memory phase touch one
-// chunk of 8 consecutive rows, whose swizzled positions are all distinct for
-// the load and for both stores (no bank conflict).
+// swizzle), rows >= valid written as zeros.  Thread ct of the kConvThreads
+// converters takes 16-code chunks g = ct, ct + kConvThreads, ...: chunk
+// (g >> 3) & 7 of row (g & 7) + 8 (g >> 6), so the 8 lanes of a shared-memory
+// phase touch one chunk of 8 consecutive rows, whose swizzled positions are
+// all distinct for the load and for both stores (no bank conflict).
 __device__ __forceinline__ void widen_tile(const uint8_t *codes, uint8_t *dst, int ct, int valid) {
 #pragma unroll 4
   for (int g = ct; g < kBN * 8; g += f8::kConvThreads) {
@@ -942,12 +944,29 @@ __device__ __forceinline__ void widen_tile(const uint8_t *codes, uint8_t *dst, i
 }
 
 template <typename Tq>
+__device__ __forceinline__ float2 to_float2(uint32_t u);
+template <>
+__device__ __forceinline__ float2 to_float2<__nv_bfloat16>(uint32_t u) {
+  return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&u));
+}
+template <>
+__device__ __forceinline__ float2 to_float2<__half>(uint32_t u) {
+  return __half22float2(*reinterpret_cast<const __half2 *>(&u));
+}
+
+// Two E4M3 codes (low byte first) of two fp32 values, round to nearest even,
+// saturated to the finite range.
+__device__ __forceinline__ uint32_t f32x2_to_e4m3x2(float a, float b) {
+  return static_cast<uint32_t>(__nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3));
+}
+
+template <typename Tq>
 __global__ void __launch_bounds__(f8::kThreads, 1)
     paged_prefill_fp8_kernel(const __grid_constant__ CUtensorMap qmap,
                              const __grid_constant__ CUtensorMap kmap,
                              const __grid_constant__ CUtensorMap vmap, const Params p) {
-  constexpr uint32_t kIdescS = tc::idesc_f16(false, false, 128, 128);
-  constexpr uint32_t kIdescPV = tc::idesc_f16(false, true, 128, 128);
+  constexpr uint32_t kIdescS = tc::idesc_f16(false, false, 128, 128);   // E4M3 x E4M3 (format 0)
+  constexpr uint32_t kIdescPV = tc::idesc_f16(false, true, 128, 128);   // f16, V MN-major
 
   const int tid = threadIdx.x, lane = tid & 31;
   const int warp = __shfl_sync(0xffffffffu, tid >> 5, 0);
@@ -1017,9 +1036,8 @@ __global__ void __launch_bounds__(f8::kThreads, 1)
     prefetch_tensormap(&vmap);
     for (int i = 0; i < f8::kNum; ++i) {
       uint32_t count = 1;
-      if (i == f8::kQ16) count = 256;
-      if ((i >= f8::kCodeFree && i < f8::kCodeFree + f8::kSlots) || i == f8::kK16 ||
-          i == f8::kV16 || i == f8::kV16 + 1)
+      if (i == f8::kQ8) count = 256;
+      if (i == f8::kVcFree || i == f8::kVcFree + 1 || i == f8::kV16 || i == f8::kV16 + 1)
         count = f8::kConvThreads;
       if (i == f8::kP || i == f8::kP + 1) count = 128;
       mbar_init(bar(i), count);
@@ -1058,7 +1076,6 @@ __global__ void __launch_bounds__(f8::kThreads, 1)
           tma_load_4d(dst, &qmap, bar(f8::kQ), 0, h0 + hh, q0 + m * kBM, 0, policy);
           tma_load_4d(dst + kHalf, &qmap, bar(f8::kQ), 64, h0 + hh, q0 + m * kBM, 0, policy);
         }
-        // Code items n = 2j (K of tile j) and 2j + 1 (V of tile j) go to slot n % 3.
         auto prefetch = [&](int jj) {
           if (jj >= nk) return;
           const KvCoord c = kv_coord(p, r, k0, jj);
@@ -1066,65 +1083,57 @@ __global__ void __launch_bounds__(f8::kThreads, 1)
           tma_prefetch_4d(&vmap, 0, hk, c.c2, c.c3);
         };
         prefetch(1);
-        bool stop = false;
-        for (int j = 0; j < nk && !stop; ++j) {
+        for (int j = 0; j < nk; ++j) {
+          const int st = j & 1;
           const KvCoord c = kv_coord(p, r, k0, j);
           if (!c.ok) record_error(p.err, SLOKV_DEVERR_BLOCK_RANGE);
           prefetch(j + 2);
-          for (int v = 0; v < 2; ++v) {
-            const int n = 2 * j + v, slot = n % f8::kSlots;
-            if (n >= f8::kSlots &&
-                !wait(f8::kCodeFree + slot, ((n - f8::kSlots) / f8::kSlots) & 1)) {
-              stop = true;
-              break;
-            }
-            mbar_arrive_expect_tx(bar(f8::kCode + slot), f8::kCodeTile);
-            tma_load_4d(base + f8::kOffCodes + slot * f8::kCodeTile, v ? &vmap : &kmap,
-                        bar(f8::kCode + slot), 0, hk, c.c2, c.c3, policy);
-          }
+          // K slot st frees once both heads' S(j-2) are done, V slot st once
+          // the converters have widened tile j-2
+          if (j >= 2 && !wait(f8::kFreeK + st, ((j - 2) >> 1) & 1)) break;
+          mbar_arrive_expect_tx(bar(f8::kKc + st), f8::kCodeTile);
+          tma_load_4d(base + f8::kOffKc + st * f8::kCodeTile, &kmap, bar(f8::kKc + st), 0, hk,
+                      c.c2, c.c3, policy);
+          if (j >= 2 && !wait(f8::kVcFree + st, ((j - 2) >> 1) & 1)) break;
+          mbar_arrive_expect_tx(bar(f8::kVc + st), f8::kCodeTile);
+          tma_load_4d(base + f8::kOffVc + st * f8::kCodeTile, &vmap, bar(f8::kVc + st), 0, hk,
+                      c.c2, c.c3, policy);
         }
       }
     } else if (warp >= 10) {
-      // ---------------- converters: codes -> f16 code values ----------------
+      // ---------------- converters: V codes -> f16 code values ----------------
       const int ct = tid - 10 * 32;
       for (int j = 0; j < nk; ++j) {
         const int st = j & 1;
-        const int nkk = 2 * j, sk = nkk % f8::kSlots, sv = (nkk + 1) % f8::kSlots;
-        // K: one f16 stage, free once both heads' S(j-1) are done
-        if (!wait(f8::kCode + sk, (nkk / f8::kSlots) & 1)) break;
-        if (j >= 1 && !wait(f8::kFreeK, (j - 1) & 1)) break;
-        widen_tile(base_ptr + f8::kOffCodes + sk * f8::kCodeTile, base_ptr + f8::kOffK, ct, kBN);
-        fence_proxy_async_smem();
-        mbar_arrive(bar(f8::kCodeFree + sk));
-        mbar_arrive(bar(f8::kK16));
-        // V: two f16 stages, stage st free once both heads' PV(j-2) are done
-        if (!wait(f8::kCode + sv, ((nkk + 1) / f8::kSlots) & 1)) break;
+        if (!wait(f8::kVc + st, (j >> 1) & 1)) break;
         if (j >= 2 && !wait(f8::kFreeV + st, ((j - 2) >> 1) & 1)) break;
-        widen_tile(base_ptr + f8::kOffCodes + sv * f8::kCodeTile,
-                   base_ptr + f8::kOffV + st * kTile, ct, k_len - j * kBN);
+        widen_tile(base_ptr + f8::kOffVc + st * f8::kCodeTile, base_ptr + f8::kOffV + st * kTile,
+                   ct, k_len - j * kBN);
         fence_proxy_async_smem();
-        mbar_arrive(bar(f8::kCodeFree + sv));
+        mbar_arrive(bar(f8::kVcFree + st));
         mbar_arrive(bar(f8::kV16 + st));
       }
     } else {
       // ---------------- tensor-core issue (lane 0) ----------------
-      auto issue_s = [&](int hh) {
+      // S_hh(j) = Q_hi K^T + Q_lo K^T over the code tile in K slot j & 1
+      auto issue_s = [&](int hh, int j) {
         const uint32_t qa = base + f8::kOffQ + hh * kTile;
-        const uint32_t kb = base + f8::kOffK;
+        const uint32_t kb = base + f8::kOffKc + (j & 1) * f8::kCodeTile;
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t off = (kk >> 2) * kHalf + (kk & 3) * 32;
-          tc::mma_f16_ss(tmem + ws::kColS + hh * 128, tc::smem_desc_sw128(qa + off, 16, 1024),
-                         tc::smem_desc_sw128(kb + off, 16, 1024), kIdescS, kk > 0);
-        }
+        for (int t = 0; t < 2; ++t)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            tc::mma_f8_ss(tmem + ws::kColS + hh * 128,
+                          tc::smem_desc_sw128(qa + t * kHalf + kk * 32, 16, 1024),
+                          tc::smem_desc_sw128(kb + kk * 32, 16, 1024), kIdescS, t | kk);
         tc::commit(bar(f8::kS + hh));
       };
-      bool ok = wait(f8::kQ16, 0) && wait(f8::kK16, 0);
+      bool ok = wait(f8::kQ8, 0) && wait(f8::kKc, 0);
       if (ok && lane == 0) {
         tc::fence_after_sync();
-        issue_s(0);
-        issue_s(1);
-        tc::commit(bar(f8::kFreeK));                    // K stage free after both S(0)
+        issue_s(0, 0);
+        issue_s(1, 0);
+        tc::commit(bar(f8::kFreeK));                    // K slot 0 free after both S(0)
       }
       __syncwarp();
       for (int j = 0; j < nk && ok; ++j) {
@@ -1144,17 +1153,17 @@ __global__ void __launch_bounds__(f8::kThreads, 1)
             tc::commit(bar(f8::kPV + hh));
           }
           if (ok && j + 1 < nk) {
-            if (hh == 0) ok = wait(f8::kK16, (j + 1) & 1);
+            if (hh == 0) ok = wait(f8::kKc + ((j + 1) & 1), ((j + 1) >> 1) & 1);
             if (ok && lane == 0) {
               tc::fence_after_sync();
-              issue_s(hh);
+              issue_s(hh, j + 1);
             }
           }
           __syncwarp();
         }
         if (ok && lane == 0) {
           tc::commit(bar(f8::kFreeV + st));
-          if (j + 1 < nk) tc::commit(bar(f8::kFreeK));   // both heads' S(j+1) issued
+          if (j + 1 < nk) tc::commit(bar(f8::kFreeK + ((j + 1) & 1)));   // both heads' S(j+1)
         }
         __syncwarp();
       }
@@ -1163,26 +1172,60 @@ __global__ void __launch_bounds__(f8::kThreads, 1)
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(f8::kRegsSoftmax));
     const int hh = warp >> 2;
     const int row = tid & 127;
-    // q -> f16 in place (one row of one head per thread), then release the Q stage
-    if (wait(f8::kQ, 0) && !std::is_same<Tq, __half>::value) {
+    // Split this thread's query row (head hh, row `row`) into E4M3 hi / lo rows
+    // scaled by 2^qe, written over the row's q (hi into the first 64-dim half's
+    // 128 bytes of the row, lo into the second's).
+    float qe = 0.f;
+    if (wait(f8::kQ, 0)) {
       uint8_t *qrow = base_ptr + f8::kOffQ + hh * kTile;
-#pragma unroll 4
+      uint32_t w[64];
+#pragma unroll
       for (int c = 0; c < 16; ++c) {
-        uint4 *ptr = reinterpret_cast<uint4 *>(qrow + (c >> 3) * kHalf + swz128(row, c & 7));
-        uint4 w = *ptr;
-        uint32_t v[4] = {w.x, w.y, w.z, w.w};
+        const uint4 v = *reinterpret_cast<const uint4 *>(qrow + (c >> 3) * kHalf + swz128(row, c & 7));
+        w[4 * c] = v.x;
+        w[4 * c + 1] = v.y;
+        w[4 * c + 2] = v.z;
+        w[4 * c + 3] = v.w;
+      }
+      float amax = 0.f;
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {
+        const float2 f = to_float2<Tq>(w[i]);
+        amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
+      }
+      // 2^qe puts the row's largest element in [128, 256) (exponent clamped so
+      // a row of denormals cannot overflow the scale)
+      const int e = amax > 0.f
+                        ? max(static_cast<int>((__float_as_uint(amax) >> 23) & 0xffu) - 127, -100)
+                        : 7;
+      qe = static_cast<float>(7 - e);
+      const float sc = exp2f(qe);
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {        // 16-dim chunks c (hi) -> row chunk c, half 0 / 1
+        uint32_t hi[4], lo[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          const __half2 h2 = __float22half2_rn(
-              __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&v[i])));
-          v[i] = *reinterpret_cast<const uint32_t *>(&h2);
+          const float2 a = to_float2<Tq>(w[8 * c + 2 * i]);
+          const float2 b = to_float2<Tq>(w[8 * c + 2 * i + 1]);
+          const float x0 = a.x * sc, x1 = a.y * sc, x2 = b.x * sc, x3 = b.y * sc;
+          const uint32_t h01 = f32x2_to_e4m3x2(x0, x1), h23 = f32x2_to_e4m3x2(x2, x3);
+          const uint32_t d01u = e4m3x2_to_f16x2(h01), d23u = e4m3x2_to_f16x2(h23);
+          const float2 d01 = __half22float2(*reinterpret_cast<const __half2 *>(&d01u));
+          const float2 d23 = __half22float2(*reinterpret_cast<const __half2 *>(&d23u));
+          const uint32_t l01 = f32x2_to_e4m3x2(x0 - d01.x, x1 - d01.y);
+          const uint32_t l23 = f32x2_to_e4m3x2(x2 - d23.x, x3 - d23.y);
+          hi[i] = h01 | (h23 << 16);
+          lo[i] = l01 | (l23 << 16);
         }
-        *ptr = make_uint4(v[0], v[1], v[2], v[3]);
+        *reinterpret_cast<uint4 *>(qrow + swz128(row, c)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        *reinterpret_cast<uint4 *>(qrow + kHalf + swz128(row, c)) =
+            make_uint4(lo[0], lo[1], lo[2], lo[3]);
       }
       fence_proxy_async_smem();
     }
-    mbar_arrive(bar(f8::kQ16));
+    mbar_arrive(bar(f8::kQ8));
     const float v_ref = __uint_as_float(*v_ref_bits);
+    const float q_unscale = exp2f(-qe);
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const int qi = m * kBM + row;
     const bool row_ok = qi < q_len;
@@ -1225,7 +1268,7 @@ __global__ void __launch_bounds__(f8::kThreads, 1)
       const int kpage = key0 / p.block_size;
       const float2 kv = kpage < p.max_blocks ? s_kv[kpage] : make_float2(0.f, 0.f);
       // a zero K scale (a page of zero codes) must keep masked -inf keys at -inf
-      const float sl = p.scale_log2 * fmaxf(kv.x, 1e-30f);
+      const float sl = p.scale_log2 * q_unscale * fmaxf(kv.x, 1e-30f);
       // V scale relative to v_ref (<= 1); a zero-scale page has zero codes,
       // so any factor works there and 1 keeps its P in the row sum exact
       const float rv = kv.y > 0.f ? __fdividef(kv.y, v_ref) : 1.f;

@@ -452,7 +452,7 @@ def flash_attn_varlen_func_fp8(q, k_codes, v_codes, k_scale, v_scale, cu_seqlens
     f16(decode(code) * V scale) -- so the tensor cores run f16 MMAs on them; a
     bf16 q is converted to f16 inside the kernel and the output is written in
     q's dtype.  Nothing is copied or allocated per call beyond `out`.  Needs
-    an even number of query heads per KV head and max_seqlen_k <= 460 pages.
+    an even number of query heads per KV head and max_seqlen_k <= 4330 pages.
     """
     if block_table is None:
         raise SlokvError("FP8 varlen attention reads the pool: block_table is required")
