@@ -1,8 +1,16 @@
 """Fused row-parallel linear + all-reduce with one process per GPU (NCCL group
 for the handshake, CUDA IPC symmetric buffers, P2P stores over NVLink), against
 the reference's F.linear + dist.all_reduce and the fp32 product, at TP = 2, 4
-and 8 as the box has GPUs (each size skipped otherwise).  The process group has a short timeout and every wait
-in the kernel is bounded, so a rank that fails ends the others with an error."""
+and 8 as the box has GPUs (each size skipped otherwise).  The process group has
+a short timeout and every wait in the kernel is bounded, so a rank that fails
+ends the others with an error.
+
+The fused kernel sums the ranks' bf16 partials in fp32 and rounds once; NCCL's
+bf16 all-reduce rounds after every addition, so at TP = 8 its own error grows
+past a fixed bf16 tolerance.  The comparison with the reference's collective is
+therefore on error against the fp32 product: the fused result must be at least
+as close to it as F.linear + dist.all_reduce (mean error within 2 %, largest
+error within one bf16 spacing of the largest output)."""
 import datetime
 import os
 import socket
@@ -20,6 +28,14 @@ def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         return s.getsockname()[1]
+
+
+def _errors(y, ref, exact):
+    """(mean, max) |error| against the fp32 product of the fused result and of
+    the reference's bf16 collective, and the largest |product|."""
+    e, r = (y.float() - exact).abs(), (ref.float() - exact).abs()
+    return (e.mean().item(), e.max().item(), r.mean().item(), r.max().item(),
+            exact.abs().max().item())
 
 
 def _worker(rank, world, port, queue):
@@ -59,6 +75,7 @@ def _worker(rank, world, port, queue):
             dist.all_gather(ys, y)
             result[f"same_{it}"] = all(torch.equal(ys[0], t) for t in ys)
             result[f"vs_nccl_{it}"] = (y.float() - ref.float()).abs().max().item()
+            result[f"err_{it}"] = _errors(y, ref, exact)
         # captured in a graph, replayed
         x = torch.randn(256, 1024, device="cuda").bfloat16()
         w = (torch.randn(N, 1024, device="cuda") * 0.02).bfloat16()
@@ -73,7 +90,10 @@ def _worker(rank, world, port, queue):
         torch.cuda.synchronize()
         ref = F.linear(x, w)
         dist.all_reduce(ref)
+        exact = x.float() @ w.float().t()
+        dist.all_reduce(exact)
         result["graph_vs_nccl"] = (out.float() - ref.float()).abs().max().item()
+        result["err_graph"] = _errors(out, ref, exact)
         del graph
         result["worst_excess"] = worst
         result["errors"] = pkg.read_device_errors()
@@ -106,7 +126,11 @@ def test_row_parallel_processes_match_nccl(world):
         assert r["errors"] == 0, r
         assert r["worst_excess"] <= 0, r
         assert all(r[f"same_{i}"] for i in range(3)), r
-        assert all(r[f"vs_nccl_{i}"] <= 0.0625 for i in range(3)), r
-        assert r["graph_vs_nccl"] <= 0.0625, r
+        for key in ("err_0", "err_1", "err_2", "err_graph"):
+            mean, top, ref_mean, ref_top, scale = r[key]
+            print(f"TP {world} rank {r['rank']} {key}: fused mean / max |error| "
+                  f"{mean:.3e} / {top:.3e}, F.linear + all_reduce {ref_mean:.3e} / {ref_top:.3e}")
+            assert mean <= 1.02 * ref_mean, (key, r)
+            assert top <= ref_top + 2 ** -8 * scale, (key, r)
     for p in procs:
         assert p.exitcode == 0
