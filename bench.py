@@ -758,22 +758,25 @@ def run_mixed(args):
         "value": round(T / (ms * 1e-3), 1), "unit": "tok/s", "n_gpus": 1, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None,
-        "dtype": "fp8_e4m3 KV (f16 MMA on codes), bf16 q/out" if fp8 else "bf16",
+        "dtype": ("fp8_e4m3 KV (prefill: S as E4M3 MMAs on the K codes, PV in f16 on V "
+                  "widened in shared memory; decode: f16 MMAs on codes widened in registers), "
+                  "bf16 q/out") if fp8 else "bf16",
         "data": "synthetic (seed 1)",
         "config": {"workload": "BASELINE config 3: 64 decode rows (context U[256,4096]) + 3 "
                                "prefill chunks of 2048 over cached prefixes 0/1024/3072, 36 layers "
                                "of forward_mixed (store + paged decode + paged varlen)"
                                + (" over an FP8-E4M3 pool (forward_mixed_fp8)" if fp8 else ""),
                    "tokens_per_step": T, "layers": L, "pool_blocks": NB},
-        "roofline": {"kernel": "paged_prefill (tcgen05, one layer"
-                               + (", incl. the f16 page copy)" if fp8 else ")"),
+        "roofline": {"kernel": ("paged_prefill_fp8 (tcgen05, one layer, reading the FP8 "
+                                "code pages)") if fp8 else "paged_prefill (tcgen05, one layer)",
                      "bound": "tensor",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind_str(kind),
                      "algorithmic_flops": flops, "launch_ms": round(pre_ms, 4),
                      "traffic": traffic},
-        # per layer: append, decode + merge, prefill work order + prefill (+ FP8 page copy)
-        "gpu_launches": args.steps * L * (6 if fp8 else 5),
+        # per layer: append (FP8: amax, encode, scale commit), decode + merge, prefill
+        # work order + prefill
+        "gpu_launches": args.steps * L * (7 if fp8 else 5),
         "clocks": clocks.summary(),
         "device_errors": pkg.read_device_errors(),
     }

@@ -142,11 +142,16 @@ def _fp8_case(seed, B, lo, hi, Hq=32, Hkv=8, D=128, bs=256):
                 slots=torch.tensor(slots, dtype=torch.int32), k=k, v=v, q=q, NB=NB, Hkv=Hkv, D=D, bs=bs)
 
 
-@pytest.mark.parametrize("B,lo,hi,seed", [(6, 1024, 8192, 3000),   # config 4 distribution
-                                          (20, 1, 700, 3001),       # tails, short rows
-                                          (3, 9000, 12000, 3002)])  # long rows: many splits
-def test_fp8_decode_matches_oracle(pkg, B, lo, hi, seed):
-    c = _fp8_case(seed, B, lo, hi)
+@pytest.mark.parametrize("B,lo,hi,seed,Hq,Hkv", [
+    (6, 1024, 8192, 3000, 32, 8),    # config 4 distribution (G = 4: E4M3 QK on the codes)
+    (20, 1, 700, 3001, 32, 8),       # tails, short rows
+    (3, 9000, 12000, 3002, 32, 8),   # long rows: many splits
+    (5, 1, 3000, 3003, 16, 2),       # G = 8: the largest group of the E4M3 QK path
+    (4, 1, 3000, 3004, 32, 2),       # G = 16: K codes widened to f16 for QK
+    (9, 1, 2000, 3005, 8, 8),        # G = 1
+])
+def test_fp8_decode_matches_oracle(pkg, B, lo, hi, seed, Hq, Hkv):
+    c = _fp8_case(seed, B, lo, hi, Hq=Hq, Hkv=Hkv)
     ref = _pools(c["NB"], H=c["Hkv"])
     O.fp8_append(c["k"], c["v"], *ref, c["slots"])
     dev = _gpu(_pools(c["NB"], H=c["Hkv"]))
