@@ -399,6 +399,9 @@ int slokv_kv_block_copy(const void *src, int64_t src_plane_stride_bytes,
  * its partial x_r W_r^T on the tensor cores and the ranks exchange 128 x 128
  * output tiles through each other's symmetric buffer over NVLink peer memory
  * (owner-reduce, then broadcast of the reduced tile), all inside one launch.
+ * GEMMs of at least 2^34 multiply-adds (tokens x n_features x k_features) run
+ * on CTA pairs (tcgen05.mma.cta_group::2, 256 x 256 tiles); smaller ones on one
+ * CTA per 128 x 128 tile (slokv_row_parallel_plan reports the choice).
  * Result: y = round(bias + sum_r round(x_r W_r^T)) on every rank (the per-rank
  * rounding is the reference's F.linear output; the sum is fp32 in rank order,
  * rounded once), identical on every rank.
@@ -426,6 +429,15 @@ int slokv_row_parallel_linear(const void *const *x, int64_t x_row_stride, const 
                               int32_t k_features, void *const *rank_buffers, int32_t world,
                               int32_t rank_base, int32_t local_ranks, int32_t max_tokens,
                               uint32_t *state, int32_t dtype, uint32_t *dev_error, void *stream);
+
+/* The grid slokv_row_parallel_linear would launch for this geometry on the
+ * current device (no launch): plan[0] = kernel (1: one CTA per 128 x 128 tile,
+ * 2: CTA pairs on 256 x 256 tiles with tcgen05.mma.cta_group::2), plan[1] =
+ * CTAs per rank, plan[2] = CTAs of a rank with GEMM work, plan[3] = CTAs per
+ * rank launched, plan[4] = co-resident two-CTA clusters on the device (0 when
+ * the single-CTA kernel is chosen without querying it). */
+int slokv_row_parallel_plan(int32_t tokens, int32_t n_features, int32_t k_features,
+                            int32_t world, int32_t local_ranks, int32_t *plan);
 
 /* Symmetric-buffer plumbing: a zeroed device allocation owned by the library,
  * and CUDA IPC export / import / close of it between the ranks' processes

@@ -110,6 +110,7 @@ SIGNATURES = {
         _c_f32, _c_i32, _c_vp, _c_vp]),   # as slokv_paged_decode, without the workspace
     "slokv_paged_decode_noalloc_scratch_bytes": (_c_sz, []),
     "slokv_row_parallel_buffer_bytes": (_c_sz, [_c_i32, _c_i32, _c_i32]),
+    "slokv_row_parallel_plan": (ctypes.c_int, [_c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_vp]),
     "slokv_row_parallel_linear": (ctypes.c_int, [
         _c_vp, _c_i64, _c_vp, _c_i64,             # x[], row stride, w[], row stride
         _c_vp, _c_vp, _c_i64,                     # bias[] (or None), y[], row stride

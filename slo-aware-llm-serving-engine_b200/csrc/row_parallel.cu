@@ -82,12 +82,26 @@ constexpr int kEpiThreads = 128;
 constexpr int kMaxRanks = 8;
 constexpr int kMaxCtas = 160;                      // >= SMs per GPU (fix-up slots)
 constexpr int kMinChunks = 4;                      // K chunks per CTA at least
-constexpr uint32_t kFixBytes = kBM * kBN * 4;      // fp32 fix-up slot of one CTA
+constexpr int64_t kPairMinMacs = int64_t(1) << 34;  // GEMM size from which CTA pairs run
+constexpr uint32_t kFixBytes = kBM * 2 * kBN * 4;  // fp32 fix-up slot of one CTA (pair width)
 constexpr uint32_t kTmemCols = 256;                // two 128-column accumulators
 constexpr uint32_t kOffStaging = kStages * kStageBytes;
 constexpr uint32_t kOffBars = kOffStaging + kTileBytes;
 constexpr int kNumBars = 2 * kStages + 4;          // full, empty, acc_full[2], acc_empty[2]
 constexpr uint32_t kSmemBytes = kOffBars + kNumBars * 8 + 16 + 1024;
+
+// CTA-pair variant (tcgen05.mma.cta_group::2): a pair of CTAs on two SMs
+// computes a 256 x 256 output tile, CTA r of the pair holding rows 128 r ..
+// 128 r + 127 of it in its own TMEM (256 fp32 columns per accumulator, two
+// accumulators = all 512 columns).  Each CTA streams its own 128 rows of X and
+// its own 128 of the tile's 256 W rows per 64-deep K chunk (32 KB per stage, as
+// above), so operand bytes per output element are half the single-CTA tile's.
+constexpr int kPBN = 2 * kBN;                      // output columns of a pair tile
+constexpr uint32_t kPTmemCols = 512;
+constexpr uint32_t kPOffBars = kOffStaging + 2 * kTileBytes;   // two staged 128 x 128 halves
+constexpr int kPNumBars = 2 * kStages + 5;         // full, empty, acc_full[2], acc_empty[2], drain
+constexpr uint32_t kPSmemBytes = kPOffBars + kPNumBars * 8 + 16 + 1024;
+static_assert(kPSmemBytes <= 227 * 1024, "pair kernel shared memory");
 
 struct Maps {
   CUtensorMap x[kMaxRanks];  // per local rank: X [tokens, K]
@@ -201,6 +215,141 @@ __device__ __forceinline__ bool wait_flag_gpu(const uint32_t *f, uint32_t epoch)
   }
 }
 
+// ---- CTA-pair primitives ------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Shared::cluster address of the object at shared::cta address `addr` in CTA
+// `rank` of this cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+// Every thread of both CTAs arrives, then waits (release / acquire at cluster scope).
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile(
+      "barrier.cluster.arrive.release.aligned;\n\t"
+      "barrier.cluster.wait.acquire.aligned;" ::
+          : "memory");
+}
+// Arrive on an mbarrier of either CTA of the cluster (shared::cluster address).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar)
+               : "memory");
+}
+// 2-D tile load into THIS CTA's shared memory whose completion is signalled on
+// an mbarrier that may live in the other CTA of the pair (`cluster_bar`, a
+// shared::cluster address): both CTAs' loads complete on the leader's barrier.
+// A plain load of local memory (no cross-CTA delivery of the data).
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap *map,
+                                                 uint32_t cluster_bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(cluster_bar)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+// D (both CTAs' TMEM, 256 rows) (+)= A (128 rows from each CTA) * B (N / 2
+// rows from each CTA); issued by one thread of the leader CTA.
+__device__ __forceinline__ void mma_f16_ss_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                                uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrive once on the mbarrier at shared::cta offset `bar` of every CTA in
+// `cta_mask` when the pair MMAs issued so far have completed.
+__device__ __forceinline__ void commit_pair(uint32_t bar, uint16_t cta_mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;" ::"r"(bar),
+      "h"(cta_mask)
+      : "memory");
+}
+
+// ---- fix-up streaming ---------------------------------------------------------
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// The predecessors' fp32 fix-up sums of a finishing segment, streamed through
+// the CTA's stage ring (idle by then: a segment with predecessors is always
+// the CTA's last, and its accumulator-full signal means every MMA has read its
+// operands).  Block b = q * npred + p is the 16 KB run [8 float4 groups][128
+// rows] of column block q in predecessor p's slot (contiguous in the slot
+// layout); it lands in ring slot b % kFixRing.  Each epilogue thread issues 8
+// of its 16-byte copies, one cp.async group per block (empty past the end), so
+// kFixRing blocks are in flight while earlier ones are added.
+constexpr int kFixRing = 8;                          // 8 x 16 KB = the 128 KB stage ring
+constexpr uint32_t kFixBlock = 8 * kBM * 16;         // 16 KB
+static_assert(kFixRing * kFixBlock <= kStages * kStageBytes, "fix-up ring fits the stages");
+struct FixStream {
+  uint32_t ring;          // shared address of the stage ring
+  const uint8_t *fix;     // this rank's fix-up region
+  int first, npred;       // predecessors first .. first + npred - 1
+  int step, offset;       // slot of predecessor c: c * step + offset
+  int total;              // blocks: column blocks x npred
+  __device__ __forceinline__ void issue(int b, int tid) const {
+    if (b < total) {
+      const int q = b / npred, pr = b - q * npred;
+      const uint8_t *src = fix + static_cast<int64_t>((first + pr) * step + offset) * kFixBytes +
+                           static_cast<int64_t>(q) * kFixBlock;
+      const uint32_t dst = ring + (b % kFixRing) * kFixBlock;
+#pragma unroll
+      for (int i = 0; i < static_cast<int>(kFixBlock / 16) / kEpiThreads; ++i)
+        cp_async16(dst + (tid + i * kEpiThreads) * 16, src + (tid + i * kEpiThreads) * 16);
+    }
+    cp_async_commit();
+  }
+  // v[32] (column block q of row `row`) += every predecessor's sum, in
+  // predecessor order; all epilogue threads call it for the same q.
+  __device__ __forceinline__ void add(float (&v)[32], int q, int row, int tid,
+                                      const uint8_t *smem) const {
+    for (int pr = 0; pr < npred; ++pr) {
+      const int b = q * npred + pr;
+      cp_async_wait<kFixRing - 1>();
+      asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
+      const float4 *blk =
+          reinterpret_cast<const float4 *>(smem + (b % kFixRing) * kFixBlock) + row;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float4 f = blk[j * kBM];
+        v[4 * j] += f.x;
+        v[4 * j + 1] += f.y;
+        v[4 * j + 2] += f.z;
+        v[4 * j + 3] += f.w;
+      }
+      asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
+      issue(b + kFixRing, tid);
+    }
+  }
+};
+
 // One CTA's stream-K range [beg, end) of chunk units (unit = tile * kc + k
 // chunk), cut into per-tile segments.  Segment j of the natural order covers
 // tile t0 + j; when the first one continues a tile begun by earlier CTAs (it
@@ -275,254 +424,28 @@ __device__ __forceinline__ void store_y_chunk(const Params &p, void *y, int m, i
   *reinterpret_cast<uint4 *>(dst) = v;
 }
 
+// Phases 2 and 3 of one call, run by every thread of a CTA after its phase-1
+// work: reduce the quarter tiles this rank owns (waiting for every source
+// rank's partial), push them to the peers, then copy the quarters the peers
+// own into Y.  Shared by the single-CTA and the CTA-pair kernels; `stage` is
+// 32 KB of this CTA's shared memory.
 template <typename T, int W>
-__global__ void __launch_bounds__(kThreads, 1)
-    row_parallel_kernel(const __grid_constant__ Params p, const __grid_constant__ Maps maps) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                              ~uintptr_t(1023));
-  const uint32_t base = smem_u32(smem);
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kOffBars);
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + kOffBars + kNumBars * 8);
-  volatile uint32_t *abort_flag = tmem_slot + 1;
-  auto bar = [&](int i) { return smem_u32(bars + i); };
-  const int kFull = 0, kEmpty = kStages, kAccFull = 2 * kStages, kAccEmpty = 2 * kStages + 2;
-
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int lr = blockIdx.x / p.ctas_per_rank;  // local (virtual) rank of this CTA
-  const int cta = blockIdx.x - lr * p.ctas_per_rank;
-  const int rank = p.rank_base + lr;
+__device__ __forceinline__ void exchange_phases(const Params &p, uint8_t *stage, int lr, int cta,
+                                                int rank, uint32_t epoch,
+                                                volatile uint32_t *abort_flag) {
+  const int tid = threadIdx.x;
   constexpr int world = W;
-  // two ranks: one shot (each rank pushes its partial to both and reduces every
-  // tile itself, same NVLink volume as two shots and one flag round less)
   constexpr bool kOneShot = W == 2;
-  const uint32_t epoch = *reinterpret_cast<volatile uint32_t *>(p.state) + 1u;
-  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
-  constexpr uint32_t kIdesc = tc::idesc_f16(kBf16, false, kBM, kBN);
-
-  if (tid == 0) {
-    for (int i = 0; i < kStages; ++i) {
-      mbar_init(bar(kFull + i), 1);
-      mbar_init(bar(kEmpty + i), 1);
-    }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(bar(kAccFull + i), 1);
-      mbar_init(bar(kAccEmpty + i), 4);  // one arrival per epilogue warp
-    }
-    *abort_flag = 0;
-    fence_barrier_init();
-  }
-  if (warp == 0) {
-    tc::tmem_alloc(smem_u32(tmem_slot), kTmemCols);
-    tc::tmem_relinquish();
-  }
-  tc::fence_before_sync();
-  __syncthreads();
-  tc::fence_after_sync();
-  const uint32_t tmem = *tmem_slot;
   auto fail = [&]() {
     record_error(p.err, SLOKV_DEVERR_TIMEOUT);
     *abort_flag = 1;
   };
-
-  // ---------------- phase 1: stream-K GEMM -> owner partial slots ----------------
-  const Sched sched = make_sched(cta < p.gemm_ctas ? cta : p.gemm_ctas, p.gemm_ctas,
-                                 static_cast<int64_t>(p.tiles) * p.k_chunks, p.k_chunks);
-  if (warp == 4) {
-    if (lane == 0) {  // TMA producer
-      prefetch_tensormap(&maps.x[lr]);
-      prefetch_tensormap(&maps.w[lr]);
-      int s = 0;
-      uint32_t ph = 0;
-      for (int i = 0; i < sched.n && !*abort_flag; ++i) {
-        const Seg sg = sched.get(i);
-        const int m = sg.tile / p.n_tiles, nt = sg.tile - m * p.n_tiles;
-        for (int kc = sg.kc0; kc < sg.kc1; ++kc) {
-          if (!mbar_wait(bar(kEmpty + s), ph ^ 1)) { fail(); break; }
-          const uint32_t dst = base + s * kStageBytes;
-          mbar_arrive_expect_tx(bar(kFull + s), kStageBytes);
-          tma_load_2d(dst, &maps.x[lr], bar(kFull + s), kc * kBK, m * kBM);
-          tma_load_2d(dst + kSlice, &maps.w[lr], bar(kFull + s), kc * kBK, nt * kBN);
-          if (++s == kStages) { s = 0; ph ^= 1; }
-        }
-      }
-    }
-    __syncwarp();
-  } else if (warp == 5) {
-    if (lane == 0) {  // MMA issuer
-      int s = 0;
-      uint32_t ph = 0;
-      for (int it = 0; it < sched.n && !*abort_flag; ++it) {
-        const Seg sg = sched.get(it);
-        const int acc = it & 1;
-        if (!mbar_wait(bar(kAccEmpty + acc), ((it >> 1) & 1) ^ 1)) { fail(); break; }
-        tc::fence_after_sync();
-        const uint32_t d = tmem + acc * kBN;
-        bool ok = true;
-        for (int kc = sg.kc0; kc < sg.kc1; ++kc) {
-          if (!mbar_wait(bar(kFull + s), ph)) { fail(); ok = false; break; }
-          tc::fence_after_sync();
-          const uint32_t a = base + s * kStageBytes, b = a + kSlice;
-#pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk)
-            tc::mma_f16_ss(d, tc::smem_desc_sw128(a + kk * 32, 16, 1024),
-                           tc::smem_desc_sw128(b + kk * 32, 16, 1024), kIdesc,
-                           (kc - sg.kc0) | kk);
-          tc::commit(bar(kEmpty + s));
-          if (++s == kStages) { s = 0; ph ^= 1; }
-        }
-        if (!ok) break;
-        tc::commit(bar(kAccFull + acc));
-      }
-    }
-    __syncwarp();
-  } else {  // epilogue warps 0-3: row 32 * warp + lane of the tile
-    const int row = warp * 32 + lane;
-    uint8_t *stage = smem + kOffStaging;
-    uint8_t *fix_base = p.buf[rank] + p.off_fix;
-    uint32_t *fix_flags = reinterpret_cast<uint32_t *>(p.buf[rank] + p.off_fixflag);
-    int pushed = 0;
-    for (int it = 0; it < sched.n; ++it) {
-      const Seg sg = sched.get(it);
-      const int acc = it & 1;
-      const bool contrib = sg.kc1 < p.k_chunks;          // the tile goes on in the next CTA
-      const bool finish = !contrib && sg.kc0 > 0;         // predecessors hold its first chunks
-      // all 128 threads take the same branch (epi_any), so none is left at bar 1
-      if (epi_any(*abort_flag != 0)) break;
-      if (epi_any(!mbar_wait(bar(kAccFull + acc), (it >> 1) & 1))) { fail(); break; }
-      // predecessors: CTAs first_pred .. cta - 1 (ascending), first_pred being the
-      // CTA whose range holds the tile's first chunk (unit_begin(0) = 0 ends the scan)
-      int first_pred = cta;
-      if (finish) {
-        const int64_t tile_beg = static_cast<int64_t>(sg.tile) * p.k_chunks;
-        const int64_t units = static_cast<int64_t>(p.tiles) * p.k_chunks;
-        first_pred = cta - 1;
-        while (unit_begin(first_pred, p.gemm_ctas, units) > tile_beg) --first_pred;
-        bool bad = false;
-        if (tid == 0)
-          for (int c = first_pred; c < cta; ++c)
-            if (!wait_flag_gpu(fix_flags + c, epoch)) { bad = true; break; }
-        if (epi_any(bad)) { fail(); break; }
-      }
-      tc::fence_after_sync();
-      float *my_fix = reinterpret_cast<float *>(fix_base + static_cast<int64_t>(cta) * kFixBytes) +
-                      row * kBN;
-#pragma unroll 1
-      for (int q = 0; q < 4; ++q) {  // 32 columns at a time
-        uint32_t r[32];
-        tc::ld32(tmem + (static_cast<uint32_t>(warp * 32) << 16) + acc * kBN + q * 32, r);
-        tc::wait_ld();
-        if (contrib) {
-#pragma unroll
-          for (int c = 0; c < 8; ++c)
-            reinterpret_cast<float4 *>(my_fix + q * 32)[c] =
-                make_float4(__uint_as_float(r[4 * c]), __uint_as_float(r[4 * c + 1]),
-                            __uint_as_float(r[4 * c + 2]), __uint_as_float(r[4 * c + 3]));
-          continue;
-        }
-        float v[32];
-#pragma unroll
-        for (int c = 0; c < 32; ++c) v[c] = __uint_as_float(r[c]);
-        if (finish) {
-          for (int c = first_pred; c < cta; ++c) {
-            const float4 *src = reinterpret_cast<const float4 *>(
-                reinterpret_cast<const float *>(fix_base + static_cast<int64_t>(c) * kFixBytes) +
-                row * kBN + q * 32);
-            float4 f[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) f[j] = __ldcg(src + j);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              v[4 * j] += f[j].x;
-              v[4 * j + 1] += f[j].y;
-              v[4 * j + 2] += f[j].z;
-              v[4 * j + 3] += f[j].w;
-            }
-          }
-        }
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {  // four 16-byte chunks of 8 columns
-          const int chunk = q * 4 + c;
-          uint4 o;
-          o.x = pack2<T>(v[8 * c + 0], v[8 * c + 1]);
-          o.y = pack2<T>(v[8 * c + 2], v[8 * c + 3]);
-          o.z = pack2<T>(v[8 * c + 4], v[8 * c + 5]);
-          o.w = pack2<T>(v[8 * c + 6], v[8 * c + 7]);
-          *reinterpret_cast<uint4 *>(stage + row * 256 + ((chunk ^ (row & 7)) << 4)) = o;
-        }
-      }
-      tc::fence_before_sync();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(kAccEmpty + acc));  // accumulator free for segment it + 2
-      asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
-      if (contrib) {  // publish the fp32 segment sum to the finishing CTA (same GPU)
-        if (tid == 0) {
-          __threadfence();
-          st_release_gpu(fix_flags + cta, epoch);
-        }
-        continue;
-      }
-      const int m = sg.tile / p.n_tiles, nt = sg.tile - m * p.n_tiles;
-      if (world == 1) {
-        for (int c = tid; c < kChunks; c += kEpiThreads) {
-          const int rr = c >> 4;
-          const uint4 v = *reinterpret_cast<const uint4 *>(stage + rr * 256 +
-                                                            (((c & 15) ^ (rr & 7)) << 4));
-          store_y_chunk(p, p.y[lr], m, nt, c, v);
-        }
-      } else if (tid == 0) {
-        // the staged tile (kept in its swizzled layout, which the owner reads
-        // back) goes to the owner's partial slot [rank][tile / world] in one copy
-        // (one shot: to slot [rank][tile] of every rank)
-        fence_proxy_async_smem();
-        if (kOneShot) {
-#pragma unroll
-          for (int d = 0; d < W; ++d)
-            bulk_store(p.buf[d] + p.off_partial +
-                           (static_cast<int64_t>(rank) * p.owned_max + sg.tile) * kTileBytes,
-                       smem_u32(stage), kTileBytes);
-        } else {
-          const int owner = sg.tile % world, slot = sg.tile / world;
-          bulk_store(p.buf[owner] + p.off_partial +
-                         (static_cast<int64_t>(rank) * p.owned_max + slot) * kTileBytes,
-                     smem_u32(stage), kTileBytes);
-        }
-        bulk_commit_wait_read();
-      }
-      ++pushed;
-      asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
-    }
-    if (world > 1 && tid == 0 && pushed > 0) {  // publish this CTA's partial tiles
-      bulk_publish_fence();
-      int k = 0;
-      for (int it = 0; it < sched.n && k < pushed; ++it) {
-        const Seg sg = sched.get(it);
-        if (sg.kc1 < p.k_chunks) continue;
-        ++k;
-        if (kOneShot) {
-#pragma unroll
-          for (int d = 0; d < W; ++d)
-            st_relaxed_sys(reinterpret_cast<uint32_t *>(p.buf[d] + p.off_pflag) +
-                               static_cast<int64_t>(rank) * p.owned_max + sg.tile,
-                           epoch);
-        } else {
-          const int owner = sg.tile % world, slot = sg.tile / world;
-          st_relaxed_sys(reinterpret_cast<uint32_t *>(p.buf[owner] + p.off_pflag) +
-                             static_cast<int64_t>(rank) * p.owned_max + slot,
-                         epoch);
-        }
-      }
-    }
-  }
-  __syncthreads();
-
   // ---------------- phase 2: reduce the quarters this rank owns ----------------
   // (abort_flag is stable here: every writer has passed the barrier above, and
   // below it only changes before a __syncthreads_or that all threads read)
   if (world > 1 && !*abort_flag) {
     const T *bias = static_cast<const T *>(p.bias[lr]);
     uint8_t *own = p.buf[rank];
-    uint8_t *stage = smem + kOffStaging;
     const uint32_t *pflags = reinterpret_cast<const uint32_t *>(own + p.off_pflag);
     int done = 0;
     for (int u = cta;; u += p.ctas_per_rank) {
@@ -659,13 +582,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   }
+}
 
-  __syncthreads();
-  if (warp == 0) {
-    tc::fence_after_sync();
-    tc::tmem_dealloc(tmem, kTmemCols);
-  }
-  if (tid == 0) {  // the last CTA of the call advances the epoch
+// The last CTA of the call advances the epoch (nothing is reset between calls).
+__device__ __forceinline__ void advance_epoch(const Params &p, uint32_t epoch) {
+  if (threadIdx.x == 0) {
     __threadfence();
     if (atomicAdd(p.state + 1, 1u) == gridDim.x - 1) {
       atomicExch(p.state + 1, 0u);
@@ -673,6 +594,532 @@ __global__ void __launch_bounds__(kThreads, 1)
       atomicExch(p.state, epoch);
     }
   }
+}
+
+template <typename T, int W>
+__global__ void __launch_bounds__(kThreads, 1)
+    row_parallel_kernel(const __grid_constant__ Params p, const __grid_constant__ Maps maps) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                              ~uintptr_t(1023));
+  const uint32_t base = smem_u32(smem);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kOffBars);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + kOffBars + kNumBars * 8);
+  volatile uint32_t *abort_flag = tmem_slot + 1;
+  auto bar = [&](int i) { return smem_u32(bars + i); };
+  const int kFull = 0, kEmpty = kStages, kAccFull = 2 * kStages, kAccEmpty = 2 * kStages + 2;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int lr = blockIdx.x / p.ctas_per_rank;  // local (virtual) rank of this CTA
+  const int cta = blockIdx.x - lr * p.ctas_per_rank;
+  const int rank = p.rank_base + lr;
+  constexpr int world = W;
+  // two ranks: one shot (each rank pushes its partial to both and reduces every
+  // tile itself, same NVLink volume as two shots and one flag round less)
+  constexpr bool kOneShot = W == 2;
+  const uint32_t epoch = *reinterpret_cast<volatile uint32_t *>(p.state) + 1u;
+  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+  constexpr uint32_t kIdesc = tc::idesc_f16(kBf16, false, kBM, kBN);
+
+  if (tid == 0) {
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(bar(kFull + i), 1);
+      mbar_init(bar(kEmpty + i), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar(kAccFull + i), 1);
+      mbar_init(bar(kAccEmpty + i), 4);  // one arrival per epilogue warp
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tc::tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+    tc::tmem_relinquish();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+  auto fail = [&]() {
+    record_error(p.err, SLOKV_DEVERR_TIMEOUT);
+    *abort_flag = 1;
+  };
+
+  // ---------------- phase 1: stream-K GEMM -> owner partial slots ----------------
+  const Sched sched = make_sched(cta < p.gemm_ctas ? cta : p.gemm_ctas, p.gemm_ctas,
+                                 static_cast<int64_t>(p.tiles) * p.k_chunks, p.k_chunks);
+  if (warp == 4) {
+    if (lane == 0) {  // TMA producer
+      prefetch_tensormap(&maps.x[lr]);
+      prefetch_tensormap(&maps.w[lr]);
+      int s = 0;
+      uint32_t ph = 0;
+      for (int i = 0; i < sched.n && !*abort_flag; ++i) {
+        const Seg sg = sched.get(i);
+        const int m = sg.tile / p.n_tiles, nt = sg.tile - m * p.n_tiles;
+        for (int kc = sg.kc0; kc < sg.kc1; ++kc) {
+          if (!mbar_wait(bar(kEmpty + s), ph ^ 1)) { fail(); break; }
+          const uint32_t dst = base + s * kStageBytes;
+          mbar_arrive_expect_tx(bar(kFull + s), kStageBytes);
+          tma_load_2d(dst, &maps.x[lr], bar(kFull + s), kc * kBK, m * kBM);
+          tma_load_2d(dst + kSlice, &maps.w[lr], bar(kFull + s), kc * kBK, nt * kBN);
+          if (++s == kStages) { s = 0; ph ^= 1; }
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 5) {
+    if (lane == 0) {  // MMA issuer
+      int s = 0;
+      uint32_t ph = 0;
+      for (int it = 0; it < sched.n && !*abort_flag; ++it) {
+        const Seg sg = sched.get(it);
+        const int acc = it & 1;
+        if (!mbar_wait(bar(kAccEmpty + acc), ((it >> 1) & 1) ^ 1)) { fail(); break; }
+        tc::fence_after_sync();
+        const uint32_t d = tmem + acc * kBN;
+        bool ok = true;
+        for (int kc = sg.kc0; kc < sg.kc1; ++kc) {
+          if (!mbar_wait(bar(kFull + s), ph)) { fail(); ok = false; break; }
+          tc::fence_after_sync();
+          const uint32_t a = base + s * kStageBytes, b = a + kSlice;
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            tc::mma_f16_ss(d, tc::smem_desc_sw128(a + kk * 32, 16, 1024),
+                           tc::smem_desc_sw128(b + kk * 32, 16, 1024), kIdesc,
+                           (kc - sg.kc0) | kk);
+          tc::commit(bar(kEmpty + s));
+          if (++s == kStages) { s = 0; ph ^= 1; }
+        }
+        if (!ok) break;
+        tc::commit(bar(kAccFull + acc));
+      }
+    }
+    __syncwarp();
+  } else {  // epilogue warps 0-3: row 32 * warp + lane of the tile
+    const int row = warp * 32 + lane;
+    uint8_t *stage = smem + kOffStaging;
+    uint8_t *fix_base = p.buf[rank] + p.off_fix;
+    uint32_t *fix_flags = reinterpret_cast<uint32_t *>(p.buf[rank] + p.off_fixflag);
+    int pushed = 0;
+    for (int it = 0; it < sched.n; ++it) {
+      const Seg sg = sched.get(it);
+      const int acc = it & 1;
+      const bool contrib = sg.kc1 < p.k_chunks;          // the tile goes on in the next CTA
+      const bool finish = !contrib && sg.kc0 > 0;         // predecessors hold its first chunks
+      // all 128 threads take the same branch (epi_any), so none is left at bar 1
+      if (epi_any(*abort_flag != 0)) break;
+      if (epi_any(!mbar_wait(bar(kAccFull + acc), (it >> 1) & 1))) { fail(); break; }
+      // predecessors: CTAs first_pred .. cta - 1 (ascending), first_pred being the
+      // CTA whose range holds the tile's first chunk (unit_begin(0) = 0 ends the scan)
+      int first_pred = cta;
+      if (finish) {
+        const int64_t tile_beg = static_cast<int64_t>(sg.tile) * p.k_chunks;
+        const int64_t units = static_cast<int64_t>(p.tiles) * p.k_chunks;
+        first_pred = cta - 1;
+        while (unit_begin(first_pred, p.gemm_ctas, units) > tile_beg) --first_pred;
+        bool bad = false;
+        if (tid == 0)
+          for (int c = first_pred; c < cta; ++c)
+            if (!wait_flag_gpu(fix_flags + c, epoch)) { bad = true; break; }
+        if (epi_any(bad)) { fail(); break; }
+      }
+      tc::fence_after_sync();
+      // fix-up slot layout: float4 group g = 8 q + c (columns 4 g .. 4 g + 3) of
+      // row `row` at float4 index g * 128 + row, so a warp's 32 rows of one
+      // group are 512 contiguous bytes (coalesced stores and loads)
+      float4 *my_fix =
+          reinterpret_cast<float4 *>(fix_base + static_cast<int64_t>(cta) * kFixBytes) + row;
+      FixStream fs{base, fix_base, first_pred, cta - first_pred, 1, 0, 4 * (cta - first_pred)};
+      if (finish)
+        for (int b = 0; b < kFixRing; ++b) fs.issue(b, tid);
+#pragma unroll 1
+      for (int q = 0; q < 4; ++q) {  // 32 columns at a time
+        uint32_t r[32];
+        tc::ld32(tmem + (static_cast<uint32_t>(warp * 32) << 16) + acc * kBN + q * 32, r);
+        tc::wait_ld();
+        if (contrib) {
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            my_fix[(q * 8 + c) * kBM] =
+                make_float4(__uint_as_float(r[4 * c]), __uint_as_float(r[4 * c + 1]),
+                            __uint_as_float(r[4 * c + 2]), __uint_as_float(r[4 * c + 3]));
+          continue;
+        }
+        float v[32];
+#pragma unroll
+        for (int c = 0; c < 32; ++c) v[c] = __uint_as_float(r[c]);
+        if (finish) fs.add(v, q, row, tid, smem);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {  // four 16-byte chunks of 8 columns
+          const int chunk = q * 4 + c;
+          uint4 o;
+          o.x = pack2<T>(v[8 * c + 0], v[8 * c + 1]);
+          o.y = pack2<T>(v[8 * c + 2], v[8 * c + 3]);
+          o.z = pack2<T>(v[8 * c + 4], v[8 * c + 5]);
+          o.w = pack2<T>(v[8 * c + 6], v[8 * c + 7]);
+          *reinterpret_cast<uint4 *>(stage + row * 256 + ((chunk ^ (row & 7)) << 4)) = o;
+        }
+      }
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(kAccEmpty + acc));  // accumulator free for segment it + 2
+      asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
+      if (contrib) {  // publish the fp32 segment sum to the finishing CTA (same GPU)
+        if (tid == 0) {
+          __threadfence();
+          st_release_gpu(fix_flags + cta, epoch);
+        }
+        continue;
+      }
+      const int m = sg.tile / p.n_tiles, nt = sg.tile - m * p.n_tiles;
+      if (world == 1) {
+        for (int c = tid; c < kChunks; c += kEpiThreads) {
+          const int rr = c >> 4;
+          const uint4 v = *reinterpret_cast<const uint4 *>(stage + rr * 256 +
+                                                            (((c & 15) ^ (rr & 7)) << 4));
+          store_y_chunk(p, p.y[lr], m, nt, c, v);
+        }
+      } else if (tid == 0) {
+        // the staged tile (kept in its swizzled layout, which the owner reads
+        // back) goes to the owner's partial slot [rank][tile / world] in one copy
+        // (one shot: to slot [rank][tile] of every rank)
+        fence_proxy_async_smem();
+        if (kOneShot) {
+#pragma unroll
+          for (int d = 0; d < W; ++d)
+            bulk_store(p.buf[d] + p.off_partial +
+                           (static_cast<int64_t>(rank) * p.owned_max + sg.tile) * kTileBytes,
+                       smem_u32(stage), kTileBytes);
+        } else {
+          const int owner = sg.tile % world, slot = sg.tile / world;
+          bulk_store(p.buf[owner] + p.off_partial +
+                         (static_cast<int64_t>(rank) * p.owned_max + slot) * kTileBytes,
+                     smem_u32(stage), kTileBytes);
+        }
+        bulk_commit_wait_read();
+      }
+      ++pushed;
+      asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
+    }
+    if (world > 1 && tid == 0 && pushed > 0) {  // publish this CTA's partial tiles
+      bulk_publish_fence();
+      int k = 0;
+      for (int it = 0; it < sched.n && k < pushed; ++it) {
+        const Seg sg = sched.get(it);
+        if (sg.kc1 < p.k_chunks) continue;
+        ++k;
+        if (kOneShot) {
+#pragma unroll
+          for (int d = 0; d < W; ++d)
+            st_relaxed_sys(reinterpret_cast<uint32_t *>(p.buf[d] + p.off_pflag) +
+                               static_cast<int64_t>(rank) * p.owned_max + sg.tile,
+                           epoch);
+        } else {
+          const int owner = sg.tile % world, slot = sg.tile / world;
+          st_relaxed_sys(reinterpret_cast<uint32_t *>(p.buf[owner] + p.off_pflag) +
+                             static_cast<int64_t>(rank) * p.owned_max + slot,
+                         epoch);
+        }
+      }
+    }
+  }
+  __syncthreads();
+
+  exchange_phases<T, W>(p, smem + kOffStaging, lr, cta, rank, epoch, abort_flag);
+  __syncthreads();
+  if (warp == 0) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem, kTmemCols);
+  }
+  advance_epoch(p, epoch);
+}
+
+// CTA-pair form of phase 1 (clusters of two CTAs on two SMs, cta_group::2).
+// The stream-K schedule is over pair tiles (256 x 256 outputs) and pairs; both
+// CTAs of a pair walk the same segments.  Per stage each CTA's TMA warp loads
+// its 128 X rows and its 128 W rows into its own shared memory, both loads
+// completing on the LEADER's full barrier (the leader expects both CTAs'
+// bytes); the leader's MMA thread issues the M = 256, N = 256 MMAs, whose
+// commits arrive on the empty / accumulator-full barriers of both CTAs.  Each
+// CTA's epilogue reads its 128 rows x 256 columns from its own TMEM and
+// arrives on the leader's accumulator-empty barrier (4 + 4 warps).  Outputs
+// leave as two 128 x 128 tiles per CTA, so the exchange of phases 2 / 3 is the
+// single-CTA kernel's.  A CTA whose 128 rows all lie past `tokens` (odd row
+// tile counts) still runs the pipeline and skips only the stores.
+template <typename T, int W>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    row_parallel_pair_kernel(const __grid_constant__ Params p, const __grid_constant__ Maps maps) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                              ~uintptr_t(1023));
+  const uint32_t base = smem_u32(smem);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kPOffBars);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + kPOffBars + kPNumBars * 8);
+  volatile uint32_t *abort_flag = tmem_slot + 1;
+  auto bar = [&](int i) { return smem_u32(bars + i); };
+  const int kFull = 0, kEmpty = kStages, kAccFull = 2 * kStages, kAccEmpty = 2 * kStages + 2,
+            kDrain = 2 * kStages + 4;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int lr = blockIdx.x / p.ctas_per_rank;  // ctas_per_rank is even: a pair never straddles
+  const int cta = blockIdx.x - lr * p.ctas_per_rank;
+  const int rank = p.rank_base + lr;
+  const uint32_t cr = cluster_ctarank();        // 0: leader (issues the MMAs), 1: peer
+  const int pair = cta >> 1;
+  constexpr int world = W;
+  constexpr bool kOneShot = W == 2;
+  const uint32_t epoch = *reinterpret_cast<volatile uint32_t *>(p.state) + 1u;
+  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+  constexpr uint32_t kIdesc = tc::idesc_f16(kBf16, false, 2 * kBM, kPBN);
+
+  if (tid == 0) {
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(bar(kFull + i), 1);    // the leader's expect-tx (both CTAs' bytes)
+      mbar_init(bar(kEmpty + i), 1);   // one commit of the leader
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar(kAccFull + i), 1);
+      mbar_init(bar(kAccEmpty + i), 8);  // four epilogue warps in each CTA (leader's is used)
+    }
+    mbar_init(bar(kDrain), 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) {  // the same warp in both CTAs allocates the pair's columns
+    tmem_alloc_pair(smem_u32(tmem_slot), kPTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  cluster_sync();  // both CTAs' barriers and TMEM exist before any cross-CTA arrive or MMA
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+  auto fail = [&]() {
+    record_error(p.err, SLOKV_DEVERR_TIMEOUT);
+    *abort_flag = 1;
+  };
+
+  // ---------------- phase 1: stream-K GEMM over pair tiles ----------------
+  const int pm_tiles = (p.m_tiles + 1) >> 1, pn_tiles = (p.n_tiles + 1) >> 1;
+  const int gemm_pairs = p.gemm_ctas >> 1;
+  const int64_t units = static_cast<int64_t>(pm_tiles) * pn_tiles * p.k_chunks;
+  const Sched sched =
+      make_sched(pair < gemm_pairs ? pair : gemm_pairs, gemm_pairs, units, p.k_chunks);
+  if (warp == 4) {
+    if (lane == 0) {  // TMA producer (both CTAs)
+      prefetch_tensormap(&maps.x[lr]);
+      prefetch_tensormap(&maps.w[lr]);
+      int s = 0;
+      uint32_t ph = 0;
+      for (int i = 0; i < sched.n && !*abort_flag; ++i) {
+        const Seg sg = sched.get(i);
+        const int pm = sg.tile / pn_tiles, pn = sg.tile - pm * pn_tiles;
+        const int xrow = (2 * pm + static_cast<int>(cr)) * kBM;
+        const int wrow = (2 * pn + static_cast<int>(cr)) * kBN;
+        for (int kc = sg.kc0; kc < sg.kc1; ++kc) {
+          if (!mbar_wait(bar(kEmpty + s), ph ^ 1)) { fail(); break; }
+          const uint32_t dst = base + s * kStageBytes;
+          const uint32_t full = mapa_shared(bar(kFull + s), 0);
+          if (cr == 0) mbar_arrive_expect_tx(bar(kFull + s), 2 * kStageBytes);
+          tma_load_2d_pair(dst, &maps.x[lr], full, kc * kBK, xrow);
+          tma_load_2d_pair(dst + kSlice, &maps.w[lr], full, kc * kBK, wrow);
+          if (++s == kStages) { s = 0; ph ^= 1; }
+        }
+      }
+      // tail: wait until the MMAs have released every stage this CTA filled, so
+      // no commit of the leader is still on its way to this CTA's barriers
+      for (int i = 0; i < kStages && !*abort_flag; ++i) {
+        if (!mbar_wait(bar(kEmpty + s), ph ^ 1)) { fail(); break; }
+        if (++s == kStages) { s = 0; ph ^= 1; }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 5) {
+    if (lane == 0 && cr == 0) {  // MMA issuer (leader only)
+      int s = 0;
+      uint32_t ph = 0;
+      for (int it = 0; it < sched.n && !*abort_flag; ++it) {
+        const Seg sg = sched.get(it);
+        const int acc = it & 1;
+        if (!mbar_wait(bar(kAccEmpty + acc), ((it >> 1) & 1) ^ 1)) { fail(); break; }
+        tc::fence_after_sync();
+        const uint32_t d = tmem + acc * kPBN;
+        bool ok = true;
+        for (int kc = sg.kc0; kc < sg.kc1; ++kc) {
+          if (!mbar_wait(bar(kFull + s), ph)) { fail(); ok = false; break; }
+          tc::fence_after_sync();
+          const uint32_t a = base + s * kStageBytes, b = a + kSlice;
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            mma_f16_ss_pair(d, tc::smem_desc_sw128(a + kk * 32, 16, 1024),
+                            tc::smem_desc_sw128(b + kk * 32, 16, 1024), kIdesc,
+                            (kc - sg.kc0) | kk);
+          commit_pair(bar(kEmpty + s), 0x3);
+          if (++s == kStages) { s = 0; ph ^= 1; }
+        }
+        if (!ok) break;
+        commit_pair(bar(kAccFull + acc), 0x3);
+      }
+      // every MMA issued above has completed before the pair releases TMEM
+      commit_pair(bar(kDrain), 0x1);
+      if (!mbar_wait(bar(kDrain), 0)) fail();
+    }
+    __syncwarp();
+  } else {  // epilogue warps 0-3 (both CTAs): row 32 * warp + lane of this CTA's 128 rows
+    const int row = warp * 32 + lane;
+    uint8_t *stage = smem + kOffStaging;
+    uint8_t *fix_base = p.buf[rank] + p.off_fix;
+    uint32_t *fix_flags = reinterpret_cast<uint32_t *>(p.buf[rank] + p.off_fixflag);
+    const uint32_t acc_empty_leader[2] = {mapa_shared(bar(kAccEmpty), 0),
+                                          mapa_shared(bar(kAccEmpty + 1), 0)};
+    int pushed = 0;
+    for (int it = 0; it < sched.n; ++it) {
+      const Seg sg = sched.get(it);
+      const int acc = it & 1;
+      const bool contrib = sg.kc1 < p.k_chunks;
+      const bool finish = !contrib && sg.kc0 > 0;
+      if (epi_any(*abort_flag != 0)) break;
+      if (epi_any(!mbar_wait(bar(kAccFull + acc), (it >> 1) & 1))) { fail(); break; }
+      // predecessor pairs first_pred .. pair - 1; this CTA adds the fix-up
+      // slots of the same-position CTA (2 c + cr) of each
+      int first_pred = pair;
+      if (finish) {
+        const int64_t tile_beg = static_cast<int64_t>(sg.tile) * p.k_chunks;
+        first_pred = pair - 1;
+        while (unit_begin(first_pred, gemm_pairs, units) > tile_beg) --first_pred;
+        bool bad = false;
+        if (tid == 0)
+          for (int c = first_pred; c < pair; ++c)
+            if (!wait_flag_gpu(fix_flags + 2 * c + cr, epoch)) { bad = true; break; }
+        if (epi_any(bad)) { fail(); break; }
+      }
+      tc::fence_after_sync();
+      // fix-up slot layout as in the single-CTA kernel (float4 group g = 8 q + c
+      // of row `row` at index g * 128 + row), 64 groups for 256 columns
+      float4 *my_fix =
+          reinterpret_cast<float4 *>(fix_base + static_cast<int64_t>(cta) * kFixBytes) + row;
+      FixStream fs{base,           fix_base, first_pred, pair - first_pred, 2, static_cast<int>(cr),
+                   8 * (pair - first_pred)};
+      if (finish)
+        for (int b = 0; b < kFixRing; ++b) fs.issue(b, tid);
+#pragma unroll 1
+      for (int q = 0; q < 8; ++q) {  // 32 columns at a time; q / 4 = output half
+        uint32_t r[32];
+        tc::ld32(tmem + (static_cast<uint32_t>(warp * 32) << 16) + acc * kPBN + q * 32, r);
+        tc::wait_ld();
+        if (contrib) {
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            my_fix[(q * 8 + c) * kBM] =
+                make_float4(__uint_as_float(r[4 * c]), __uint_as_float(r[4 * c + 1]),
+                            __uint_as_float(r[4 * c + 2]), __uint_as_float(r[4 * c + 3]));
+          continue;
+        }
+        float v[32];
+#pragma unroll
+        for (int c = 0; c < 32; ++c) v[c] = __uint_as_float(r[c]);
+        if (finish) fs.add(v, q, row, tid, smem);
+        uint8_t *half = stage + (q >> 2) * kTileBytes;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {  // four 16-byte chunks of 8 columns
+          const int chunk = (q & 3) * 4 + c;
+          uint4 o;
+          o.x = pack2<T>(v[8 * c + 0], v[8 * c + 1]);
+          o.y = pack2<T>(v[8 * c + 2], v[8 * c + 3]);
+          o.z = pack2<T>(v[8 * c + 4], v[8 * c + 5]);
+          o.w = pack2<T>(v[8 * c + 6], v[8 * c + 7]);
+          *reinterpret_cast<uint4 *>(half + row * 256 + ((chunk ^ (row & 7)) << 4)) = o;
+        }
+      }
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(acc_empty_leader[acc]);  // accumulator free
+      asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
+      if (contrib) {  // publish the fp32 segment sum to the finishing pair (same GPU)
+        if (tid == 0) {
+          __threadfence();
+          st_release_gpu(fix_flags + cta, epoch);
+        }
+        continue;
+      }
+      const int pm = sg.tile / pn_tiles, pn = sg.tile - pm * pn_tiles;
+      const int m = 2 * pm + static_cast<int>(cr);
+      if (m < p.m_tiles) {
+        if (world == 1) {
+          for (int c = tid; c < 2 * kChunks; c += kEpiThreads) {
+            const int h = c / kChunks, cc = c - h * kChunks, rr = cc >> 4;
+            const int nt = 2 * pn + h;
+            if (nt >= p.n_tiles) continue;
+            const uint4 v = *reinterpret_cast<const uint4 *>(
+                stage + h * kTileBytes + rr * 256 + (((cc & 15) ^ (rr & 7)) << 4));
+            store_y_chunk(p, p.y[lr], m, nt, cc, v);
+          }
+        } else if (tid == 0) {
+          fence_proxy_async_smem();
+          for (int h = 0; h < 2; ++h) {
+            const int nt = 2 * pn + h;
+            if (nt >= p.n_tiles) continue;
+            const int tile = m * p.n_tiles + nt;
+            const uint32_t src = smem_u32(stage + h * kTileBytes);
+            if (kOneShot) {
+#pragma unroll
+              for (int d = 0; d < W; ++d)
+                bulk_store(p.buf[d] + p.off_partial +
+                               (static_cast<int64_t>(rank) * p.owned_max + tile) * kTileBytes,
+                           src, kTileBytes);
+            } else {
+              const int owner = tile % world, slot = tile / world;
+              bulk_store(p.buf[owner] + p.off_partial +
+                             (static_cast<int64_t>(rank) * p.owned_max + slot) * kTileBytes,
+                         src, kTileBytes);
+            }
+          }
+          bulk_commit_wait_read();
+        }
+        ++pushed;
+      }
+      asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
+    }
+    if (world > 1 && tid == 0 && pushed > 0) {  // publish this CTA's partial tiles
+      bulk_publish_fence();
+      for (int it = 0; it < sched.n; ++it) {
+        const Seg sg = sched.get(it);
+        if (sg.kc1 < p.k_chunks) continue;
+        const int pm = sg.tile / pn_tiles, pn = sg.tile - pm * pn_tiles;
+        const int m = 2 * pm + static_cast<int>(cr);
+        if (m >= p.m_tiles) continue;
+        for (int h = 0; h < 2; ++h) {
+          const int nt = 2 * pn + h;
+          if (nt >= p.n_tiles) continue;
+          const int tile = m * p.n_tiles + nt;
+          if (kOneShot) {
+#pragma unroll
+            for (int d = 0; d < W; ++d)
+              st_relaxed_sys(reinterpret_cast<uint32_t *>(p.buf[d] + p.off_pflag) +
+                                 static_cast<int64_t>(rank) * p.owned_max + tile,
+                             epoch);
+          } else {
+            const int owner = tile % world, slot = tile / world;
+            st_relaxed_sys(reinterpret_cast<uint32_t *>(p.buf[owner] + p.off_pflag) +
+                               static_cast<int64_t>(rank) * p.owned_max + slot,
+                           epoch);
+          }
+        }
+      }
+    }
+  }
+  __syncthreads();
+
+  exchange_phases<T, W>(p, smem + kOffStaging, lr, cta, rank, epoch, abort_flag);
+  __syncthreads();
+  cluster_sync();  // neither CTA leaves while the other may still arrive on its barriers
+  if (warp == 0) {
+    tc::fence_after_sync();
+    tmem_dealloc_pair(tmem, kPTmemCols);
+  }
+  advance_epoch(p, epoch);
 }
 
 // ---- host side -------------------------------------------------------------
@@ -767,13 +1214,145 @@ int launch(const Params &p, const Maps &maps, int local_ranks, cudaStream_t stre
              : SLOKV_ERR_CUDA;
 }
 
+// Co-resident clusters of two CTAs of the pair kernel on this device (clusters
+// must fit a GPC, so this can be below SMs / 2); 0 if the query fails.
+int pair_capacity() {
+  static int cap = -1;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cap = 0;
+    if (cudaFuncSetAttribute(row_parallel_pair_kernel<__nv_bfloat16, 1>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kPSmemBytes) != cudaSuccess)
+      return;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kPSmemBytes;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, row_parallel_pair_kernel<__nv_bfloat16, 1>, &cfg) ==
+        cudaSuccess)
+      cap = n;
+    else
+      cudaGetLastError();
+  });
+  return cap;
+}
+
+// The pair kernel is launched cooperatively where the runtime accepts a
+// cooperative launch of a cluster kernel; otherwise as a plain launch whose
+// grid never exceeds the co-resident cluster capacity (pair_capacity), so every
+// CTA is resident and every wait of the exchange can end.
+template <typename T, int W>
+int launch_pair(const Params &p, const Maps &maps, int local_ranks, cudaStream_t stream) {
+  static std::once_flag once;
+  static bool ok = false;
+  static int coop = -1;  // -1 unknown, 0 refused, 1 accepted
+  std::call_once(once, [] {
+    ok = cudaFuncSetAttribute(row_parallel_pair_kernel<T, W>,
+                              cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              kPSmemBytes) == cudaSuccess;
+  });
+  if (!ok) return SLOKV_ERR_CUDA;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(local_ranks * p.ctas_per_rank));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kPSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  cudaStreamIsCapturing(stream, &cap);
+  if (coop != 0 && !(coop < 0 && cap != cudaStreamCaptureStatusNone)) {
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, row_parallel_pair_kernel<T, W>, p, maps);
+    if (e == cudaSuccess) {
+      coop = 1;
+      return SLOKV_OK;
+    }
+    if (coop == 1) return SLOKV_ERR_CUDA;
+    cudaGetLastError();  // a refused launch attribute leaves no sticky error
+    coop = 0;
+  }
+  cfg.attrs = nullptr;
+  cfg.numAttrs = 0;
+  return cudaLaunchKernelEx(&cfg, row_parallel_pair_kernel<T, W>, p, maps) == cudaSuccess
+             ? SLOKV_OK
+             : SLOKV_ERR_CUDA;
+}
+
+// Grid of one call: which kernel, CTAs per rank, CTAs with GEMM work.
+struct Plan {
+  bool pair;
+  int per_rank, gemm_ctas, ctas_per_rank, pair_capacity;
+};
+Plan plan_grid(int tokens, int n_features, int k_features, int world, int local_ranks) {
+  const int m_tiles = (tokens + kBM - 1) / kBM, n_tiles = n_features / kBN,
+            k_chunks = k_features / kBK;
+  // CTA pairs (256 x 256 tiles, half the operand bytes per output, stream-K
+  // over every pair) for GEMMs of at least kPairMinMacs multiply-adds; one CTA
+  // per 128 x 128 tile below that.  Measured on B200 (N = 2560): the pairs'
+  // main loop runs 2.3x the single-CTA tile rate, but each pair CTA drains a
+  // 128 x 256 accumulator, so for decode-sized calls (T <= 512 rows per rank,
+  // and T = 1024 with K = 4096) the single-CTA kernel finishes first; from
+  // T = 1024 with K = 9728, or T = 2048 with K = 4096, the pairs win
+  // (1.08 - 1.35x).
+  Plan pl = {};
+  int pair_cap = 0;
+  const bool pair = m_tiles >= 2 && n_tiles >= 2 &&
+                    static_cast<int64_t>(tokens) * n_features * k_features >= kPairMinMacs &&
+                    (pair_cap = pair_capacity()) > 0;
+  pl.pair = pair;
+  pl.pair_capacity = pair_cap;
+  int per_rank = (pair && 2 * pair_cap < sm_count() ? 2 * pair_cap : sm_count()) / local_ranks;
+  if (per_rank > kMaxCtas) per_rank = kMaxCtas;
+  if (pair) per_rank &= ~1;
+  if (per_rank < (pair ? 2 : 1)) return pl;   // per_rank 0: unsupported
+  pl.per_rank = per_rank;
+  if (pair) {
+    // stream-K over all pairs: a pair's range is at least one pair tile's K
+    // loop once there are as many pair tiles as pairs, so a tile has at most
+    // one predecessor; with fewer, every pair still gets >= kMinChunks chunks
+    const int pair_tiles = ((m_tiles + 1) / 2) * ((n_tiles + 1) / 2);
+    const int64_t by_work =
+        (static_cast<int64_t>(pair_tiles) * k_chunks + kMinChunks - 1) / kMinChunks;
+    const int max_pairs = per_rank / 2;
+    pl.gemm_ctas = 2 * static_cast<int>(by_work < max_pairs ? by_work : max_pairs);
+  } else {
+    // GEMM: one CTA per tile while that keeps at least half the SMs busy (the
+    // GEMM is bound by L2 operand traffic, which splitting does not reduce, and
+    // each split adds an fp32 fix-up); stream-K splits of the K loops over all
+    // SMs for long K or few tiles, every CTA getting at least kMinChunks K
+    // chunks.
+    const int tiles = m_tiles * n_tiles;
+    const int64_t units = static_cast<int64_t>(tiles) * k_chunks;
+    if (k_chunks >= 128 || 2 * tiles < per_rank) {
+      const int64_t by_work = (units + kMinChunks - 1) / kMinChunks;
+      pl.gemm_ctas = static_cast<int>(by_work < per_rank ? by_work : per_rank);
+    } else {
+      pl.gemm_ctas = tiles < per_rank ? tiles : per_rank;
+    }
+  }
+  // With an exchange every SM gets a CTA: the ones without GEMM work join the
+  // reduce.
+  pl.ctas_per_rank = world > 1 ? per_rank : pl.gemm_ctas;
+  return pl;
+}
+
 template <typename T>
-int launch_world(const Params &p, const Maps &maps, int local_ranks, cudaStream_t stream) {
+int launch_world(const Params &p, const Maps &maps, int local_ranks, bool pair,
+                 cudaStream_t stream) {
   switch (p.world) {
-    case 1: return launch<T, 1>(p, maps, local_ranks, stream);
-    case 2: return launch<T, 2>(p, maps, local_ranks, stream);
-    case 4: return launch<T, 4>(p, maps, local_ranks, stream);
-    case 8: return launch<T, 8>(p, maps, local_ranks, stream);
+    case 1: return pair ? launch_pair<T, 1>(p, maps, local_ranks, stream)
+                        : launch<T, 1>(p, maps, local_ranks, stream);
+    case 2: return pair ? launch_pair<T, 2>(p, maps, local_ranks, stream)
+                        : launch<T, 2>(p, maps, local_ranks, stream);
+    case 4: return pair ? launch_pair<T, 4>(p, maps, local_ranks, stream)
+                        : launch<T, 4>(p, maps, local_ranks, stream);
+    case 8: return pair ? launch_pair<T, 8>(p, maps, local_ranks, stream)
+                        : launch<T, 8>(p, maps, local_ranks, stream);
     default: return SLOKV_ERR_UNSUPPORTED;
   }
 }
@@ -788,6 +1367,23 @@ extern "C" size_t slokv_row_parallel_buffer_bytes(int32_t max_tokens, int32_t n_
       world > kMaxRanks)
     return 0;
   return static_cast<size_t>(layout(max_tokens, n_features, world).total);
+}
+
+extern "C" int slokv_row_parallel_plan(int32_t tokens, int32_t n_features, int32_t k_features,
+                                       int32_t world, int32_t local_ranks, int32_t *plan) {
+  using namespace slokv;
+  using namespace slokv::rp;
+  if (!plan || tokens <= 0 || n_features <= 0 || k_features <= 0 || world < 1 ||
+      world > kMaxRanks || local_ranks < 1 || local_ranks > world)
+    return SLOKV_ERR_INVALID_ARG;
+  if (n_features % kBN != 0 || k_features % kBK != 0) return SLOKV_ERR_UNSUPPORTED;
+  const Plan pl = plan_grid(tokens, n_features, k_features, world, local_ranks);
+  plan[0] = pl.pair ? 2 : 1;
+  plan[1] = pl.per_rank;
+  plan[2] = pl.gemm_ctas;
+  plan[3] = pl.ctas_per_rank;
+  plan[4] = pl.pair_capacity;
+  return pl.per_rank < 1 ? SLOKV_ERR_UNSUPPORTED : SLOKV_OK;
 }
 
 extern "C" int slokv_row_parallel_linear(
@@ -851,26 +1447,14 @@ extern "C" int slokv_row_parallel_linear(
   p.y_stride = y_row_stride;
   p.state = state;
   p.err = dev_error;
-  int per_rank = sm_count() / local_ranks;
-  if (per_rank > kMaxCtas) per_rank = kMaxCtas;
-  if (per_rank < 1) return SLOKV_ERR_UNSUPPORTED;
-  // GEMM: one CTA per tile while that keeps at least half the SMs busy (the
-  // GEMM is bound by L2 operand traffic, which splitting does not reduce, and
-  // each split adds an fp32 fix-up); stream-K splits of the K loops over all SMs
-  // for long K or few tiles, every CTA getting at least kMinChunks K chunks.
-  // With an exchange every SM gets a CTA: the ones without GEMM work join the
-  // reduce.
-  const int64_t units = static_cast<int64_t>(p.tiles) * p.k_chunks;
-  if (p.k_chunks >= 128 || 2 * p.tiles < per_rank) {
-    const int64_t by_work = (units + kMinChunks - 1) / kMinChunks;
-    p.gemm_ctas = static_cast<int>(by_work < per_rank ? by_work : per_rank);
-  } else {
-    p.gemm_ctas = p.tiles < per_rank ? p.tiles : per_rank;
-  }
-  p.ctas_per_rank = world > 1 ? per_rank : p.gemm_ctas;
+  const Plan plan = plan_grid(tokens, n_features, k_features, world, local_ranks);
+  if (plan.per_rank < 1) return SLOKV_ERR_UNSUPPORTED;
+  p.gemm_ctas = plan.gemm_ctas;
+  p.ctas_per_rank = plan.ctas_per_rank;
+  const bool pair = plan.pair;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  return dtype == SLOKV_DTYPE_BF16 ? launch_world<__nv_bfloat16>(p, maps, local_ranks, st)
-                                   : launch_world<__half>(p, maps, local_ranks, st);
+  return dtype == SLOKV_DTYPE_BF16 ? launch_world<__nv_bfloat16>(p, maps, local_ranks, pair, st)
+                                   : launch_world<__half>(p, maps, local_ranks, pair, st);
 }
 
 // ---- symmetric buffers shared between the ranks' processes (CUDA IPC) --------

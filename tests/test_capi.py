@@ -103,10 +103,11 @@ def test_row_parallel_argument_checks(pkg):
 
 def test_row_parallel_buffer_layout(pkg):
     lib = pkg._lib.lib()
-    # stream-K fix-up slots (160 CTAs x 128 x 128 fp32) + flags, then for world > 1
-    # partial slots [world][ceil(tiles / world)] (two ranks: [2][tiles]) + result
-    # slots [tiles] of 32 KB tiles + their flags
-    fix = 160 * 128 * 128 * 4 + 160 * 4
+    # stream-K fix-up slots (160 CTAs x 128 rows x 256 fp32 columns, the width of
+    # a CTA-pair tile) + flags, then for world > 1 partial slots
+    # [world][ceil(tiles / world)] (two ranks: [2][tiles]) + result slots [tiles]
+    # of 32 KB tiles + their flags
+    fix = 160 * 128 * 256 * 4 + 160 * 4
     for T, n, world in ((1, 2560, 2), (512, 2560, 4), (8192, 2560, 8), (130, 1024, 1)):
         tiles = -(-T // 128) * (n // 128)
         got = lib.slokv_row_parallel_buffer_bytes(T, n, world)

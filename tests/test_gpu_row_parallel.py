@@ -30,14 +30,20 @@ def _case(seed, world, T, K, bias=False, dtype=torch.bfloat16):
 
 
 def _check(ys, xs, ws, b):
-    parts = [x.float() @ w.float().t() for x, w in zip(xs, ws)]
-    exact = sum(parts) + (b.float() if b is not None else 0)
-    # half an ulp of bf16 (2^-9 relative) per partial and for the final rounding, doubled
-    bound = 2 ** -8 * (sum(p.abs() for p in parts) + exact.abs()) + 1e-6
+    parts = [x.double() @ w.double().t() for x, w in zip(xs, ws)]
+    exact = sum(parts) + (b.double() if b is not None else 0)
+    # half an ulp of bf16 (2^-9 relative) per partial and for the final rounding,
+    # doubled, plus the fp32 accumulation of each rank's K products (4 sqrt(K)
+    # unit roundoffs of the sum of |products|: it dominates only where the
+    # products cancel to near zero)
+    absum = sum(x.double().abs() @ w.double().abs().t() for x, w in zip(xs, ws))
+    K = xs[0].shape[1]
+    bound = (2 ** -8 * (sum(p.abs() for p in parts) + exact.abs())
+             + 4 * K ** 0.5 * 2 ** -24 * absum + 1e-6)
     for r, y in enumerate(ys):
         assert torch.isfinite(y.float()).all()
         assert torch.equal(y, ys[0]), f"rank {r} differs from rank 0"
-    err = (ys[0].float() - exact).abs()
+    err = (ys[0].double() - exact).abs()
     assert (err <= bound).all(), f"max excess {(err - bound).max().item():.3e}"
     # the reference's arithmetic: cuBLAS bf16 partials, summed (fp32 here, rounded once)
     ref = sum(F.linear(x, w).float() for x, w in zip(xs, ws))
@@ -131,3 +137,51 @@ def test_row_parallel_linear_module_single_rank(pkg):
     torch.nn.init.normal_(m.weight, std=0.02)
     x = torch.randn(5, 1024, device="cuda").bfloat16()
     assert torch.equal(m(x), F.linear(x, m.weight))
+
+
+def _plan(pkg, T, n, K, world, local):
+    import ctypes
+    plan = (ctypes.c_int32 * 5)()
+    assert pkg._lib.lib().slokv_row_parallel_plan(T, n, K, world, local, plan) == 0
+    return list(plan)
+
+
+@pytest.mark.parametrize("world,T,n,K,seed", [
+    (1, 1000, 2560, 8192, 40),    # 8 row tiles, ragged; 40 pair tiles over 74 pairs (split K)
+    (1, 2048, 2560, 4096, 41),    # 80 pair tiles: stream-K over every pair
+    (1, 300, 2560, 22528, 42),    # 3 row tiles: the second CTA of the last pair is padding
+    (2, 1024, 640, 27648, 43),    # 5 column tiles: the last pair half is padding; one shot
+    (4, 1024, 2560, 8192, 44),    # four emulated ranks of 18 pairs each, two-shot exchange
+])
+def test_row_parallel_pair_tiles(pkg, world, T, n, K, seed):
+    """The 256 x 256 CTA-pair tiles (tcgen05.mma.cta_group::2), chosen for
+    GEMMs of at least 2^34 multiply-adds, at shapes whose pair tiles are partly
+    padding in rows or columns and whose K loops are split over pairs."""
+    assert _plan(pkg, T, n, K, world, world)[0] == 2, "the pair kernel is not chosen"
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    xs = [torch.randn(T, K, device="cuda", generator=g).bfloat16() for _ in range(world)]
+    ws = [(torch.randn(n, K, device="cuda", generator=g) * 0.02).bfloat16()
+          for _ in range(world)]
+    comm = pkg.RowParallelAllReduce.emulated(world, max_tokens=2048, n_features=n, device="cuda")
+    try:
+        ys = comm.emulate(xs, ws)
+        torch.cuda.synchronize()
+        assert pkg.read_device_errors() == 0
+        _check(ys, xs, ws, None)
+    finally:
+        comm.close()
+
+
+def test_row_parallel_plan_query(pkg):
+    """slokv_row_parallel_plan: decode-sized calls take the single-CTA kernel,
+    large GEMMs the pairs; grids never exceed one CTA per SM or 160 per rank."""
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    for T, K, world, local, kernel in ((512, 4096, 1, 1, 1), (512, 2048, 2, 1, 1),
+                                       (2048, 4096, 1, 1, 2), (1024, 9728, 1, 1, 2),
+                                       (1024, 8192, 4, 4, 2), (64, 4096, 8, 8, 1)):
+        plan = _plan(pkg, T, 2560, K, world, local)
+        assert plan[0] == kernel, (T, K, plan)
+        assert 1 <= plan[2] <= plan[3] <= plan[1] <= min(160, sms // local)
+        if kernel == 2:
+            assert plan[1] % 2 == 0 and plan[2] % 2 == 0 and plan[3] % 2 == 0
+            assert plan[1] * local <= 2 * plan[4]          # every pair co-resident

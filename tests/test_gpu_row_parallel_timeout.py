@@ -18,14 +18,18 @@ pytestmark = pytest.mark.gpu
 N = 2560
 
 
-@pytest.mark.parametrize("world", [2, 4])
-def test_missing_rank_times_out_with_error_status(pkg, world):
+@pytest.mark.parametrize("world,T,K", [
+    (2, 256, 512),      # single-CTA tiles
+    (4, 256, 512),
+    (2, 1024, 16384),   # CTA pairs (cta_group::2): the exchange waits of the pair kernel
+])
+def test_missing_rank_times_out_with_error_status(pkg, world, T, K):
     assert pkg.read_device_errors() == 0
-    comm = pkg.RowParallelAllReduce.emulated(world, max_tokens=256, n_features=N, device="cuda")
+    comm = pkg.RowParallelAllReduce.emulated(world, max_tokens=T, n_features=N, device="cuda")
     g = torch.Generator(device="cuda").manual_seed(31 + world)
-    x = torch.randn(256, 512, device="cuda", generator=g).bfloat16()
-    w = (torch.randn(N, 512, device="cuda", generator=g) * 0.02).bfloat16()
-    out = torch.zeros(256, N, dtype=torch.bfloat16, device="cuda")
+    x = torch.randn(T, K, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(N, K, device="cuda", generator=g) * 0.02).bfloat16()
+    out = torch.zeros(T, N, dtype=torch.bfloat16, device="cuda")
     torch.cuda.synchronize()
     t0 = time.monotonic()
     comm._launch([x], [w], None, [out], 0)           # rank 0 of `world`, peers never start
@@ -36,10 +40,11 @@ def test_missing_rank_times_out_with_error_status(pkg, world):
     assert errs & pkg._lib.DEVERR_TIMEOUT, f"error word {errs:#x}"
     assert 1.5 <= elapsed <= 20.0, f"returned after {elapsed:.1f} s"
     # the context still works: the same GEMM with no exchange
-    solo = pkg.RowParallelAllReduce.emulated(1, max_tokens=256, n_features=N, device="cuda")
+    solo = pkg.RowParallelAllReduce.emulated(1, max_tokens=T, n_features=N, device="cuda")
     y = solo.emulate([x], [w])[0]
     torch.cuda.synchronize()
     exact = x.float() @ w.float().t()
-    assert ((y.float() - exact).abs() <= 2 ** -8 * exact.abs() * 2 + 1e-6).all()
+    absum = x.float().abs() @ w.float().abs().t()
+    assert ((y.float() - exact).abs() <= 2 ** -8 * (absum + exact.abs()) + 1e-6).all()
     assert pkg.read_device_errors() == 0
     solo.close()

@@ -79,3 +79,72 @@ def test_stream_k_schedule_invariants(tiles, k):
                 ci = next(i for i, s in enumerate(segs) if s[2] < k)
                 fi = [i for i, s in enumerate(segs) if s[2] == k and s[1] > 0]
                 assert not fi or ci < fi[0]                   # publishes before it waits
+
+
+# ---- the CTA-pair kernel (256 x 256 pair tiles, cta_group::2) ----------------
+
+BM = BN = 128
+FIX_FLOATS = BM * 2 * BN          # one CTA's fp32 fix-up slot (128 rows x 256 columns)
+MAX_CTAS = 160
+MIN_CHUNKS = 4
+PAIR_MIN_MACS = 1 << 34
+
+
+def pair_grid(m_tiles, n_tiles, k, per_rank):
+    """The host's choice for the pair kernel (plan_grid in row_parallel.cu):
+    gemm_pairs for `per_rank` CTAs (already even): stream-K over every pair,
+    at least MIN_CHUNKS K chunks each."""
+    pair_tiles = ((m_tiles + 1) // 2) * ((n_tiles + 1) // 2)
+    return min(-(-(pair_tiles * k) // MIN_CHUNKS), per_rank // 2)
+
+
+def test_pair_kernel_size_rule():
+    """Pairs from 2^34 multiply-adds per call (T x N x K) with two row and two
+    column tiles."""
+    def pair(T, N, K):
+        return -(-T // BM) >= 2 and N // BN >= 2 and T * N * K >= PAIR_MIN_MACS
+    assert not pair(512, 2560, 4096) and not pair(512, 2560, 9728)    # decode batches
+    assert not pair(1024, 2560, 4096) and pair(1024, 2560, 9728)
+    assert pair(2048, 2560, 4096) and not pair(2048, 2560, 1024)
+    assert not pair(128, 2560, 1 << 20)                                # one row tile
+
+
+@pytest.mark.parametrize("tokens", [129, 256, 300, 512, 1024])
+@pytest.mark.parametrize("n_tiles", [2, 3, 20])
+@pytest.mark.parametrize("k", [8, 32, 64, 152, 352])
+def test_pair_schedule_produces_every_output_tile_once(tokens, n_tiles, k):
+    """Every 128 x 128 output tile (m < m_tiles, nt < n_tiles) is written by
+    exactly one (pair, CTA position, half) of a finishing segment; padding
+    halves (m or nt past the end) are never pushed; fix-up reads and writes of
+    CTA position r stay inside slot 2 c + r of the contributing pair c."""
+    m_tiles = -(-tokens // BM)
+    pm_tiles, pn_tiles = (m_tiles + 1) // 2, (n_tiles + 1) // 2
+    for sms, local_ranks in ((148, 1), (148, 4), (140, 8)):
+        per_rank = min(sms // local_ranks, MAX_CTAS) & ~1
+        G = pair_grid(m_tiles, n_tiles, k, per_rank)
+        assert 2 * G <= per_rank and G >= 1
+        U = pm_tiles * pn_tiles * k
+        written = {}
+        for pair in range(per_rank // 2):
+            for t, a, b in sched(pair, G, U, k):
+                if b < k:
+                    continue                            # contributing segment: fix-up only
+                preds = predecessors(pair, t, G, U, k) if a > 0 else []
+                for r in (0, 1):
+                    for c in preds:
+                        slot = 2 * c + r
+                        assert 0 <= slot < per_rank
+                    pm, pn = divmod(t, pn_tiles)
+                    m = 2 * pm + r
+                    if m >= m_tiles:
+                        continue
+                    for h in (0, 1):
+                        nt = 2 * pn + h
+                        if nt >= n_tiles:
+                            continue
+                        assert (m, nt) not in written
+                        written[(m, nt)] = (pair, r, h)
+        assert set(written) == {(m, nt) for m in range(m_tiles) for nt in range(n_tiles)}
+    # the largest fix-up float a thread touches: float4 group 8 q + c = 63 of row
+    # 127 (groups of 128 rows, 4 floats each)
+    assert ((7 * 8 + 7) * BM + 127) * 4 + 3 < FIX_FLOATS
