@@ -152,6 +152,7 @@ def _plan(pkg, T, n, K, world, local):
     (1, 300, 2560, 22528, 42),    # 3 row tiles: the second CTA of the last pair is padding
     (2, 1024, 640, 27648, 43),    # 5 column tiles: the last pair half is padding; one shot
     (4, 1024, 2560, 8192, 44),    # four emulated ranks of 18 pairs each, two-shot exchange
+    (8, 1024, 2560, 8192, 45),    # eight emulated ranks of 9 pairs each
 ])
 def test_row_parallel_pair_tiles(pkg, world, T, n, K, seed):
     """The 256 x 256 CTA-pair tiles (tcgen05.mma.cta_group::2), chosen for
