@@ -44,6 +44,11 @@
 // symmetric buffer); only stores cross NVLink.  Every TMA load is a plain
 // single-CTA load of local memory.
 //
+// Large GEMMs (>= 2^34 multiply-adds per call) run phase 1 on CTA pairs
+// instead (row_parallel_pair_kernel: clusters of two CTAs, 256 x 256 tiles,
+// tcgen05.mma.cta_group::2), which halves the operand bytes per output; the
+// tiles they produce are 128 x 128 halves, so phases 2 and 3 are shared.
+//
 // The world size is a template parameter (1, 2, 4 or 8: the TP sizes of the
 // 8-KV-head model), so the per-source loops unroll into independent loads.
 //
