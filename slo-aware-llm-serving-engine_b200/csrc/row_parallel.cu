@@ -1326,14 +1326,15 @@ Plan plan_grid(int tokens, int n_features, int k_features, int world, int local_
     const int max_pairs = per_rank / 2;
     pl.gemm_ctas = 2 * static_cast<int>(by_work < max_pairs ? by_work : max_pairs);
   } else {
-    // GEMM: one CTA per tile while that keeps at least half the SMs busy (the
-    // GEMM is bound by L2 operand traffic, which splitting does not reduce, and
-    // each split adds an fp32 fix-up); stream-K splits of the K loops over all
-    // SMs for long K or few tiles, every CTA getting at least kMinChunks K
-    // chunks.
+    // GEMM: one CTA per tile while that keeps at least half the SMs busy (each
+    // split adds an fp32 fix-up); stream-K splits of the K loops over all SMs
+    // for K of 64 chunks or more (T = 512 rows: o_proj at TP 1 22.8 -> 21.0 us,
+    // down_proj at TP 2 25.7 -> 21.8 us; shorter K loops lose, e.g. o_proj at
+    // TP 4 11.0 vs 14.8 us) or few tiles, every CTA getting at least
+    // kMinChunks K chunks.
     const int tiles = m_tiles * n_tiles;
     const int64_t units = static_cast<int64_t>(tiles) * k_chunks;
-    if (k_chunks >= 128 || 2 * tiles < per_rank) {
+    if (k_chunks >= 64 || 2 * tiles < per_rank) {
       const int64_t by_work = (units + kMinChunks - 1) / kMinChunks;
       pl.gemm_ctas = static_cast<int>(by_work < per_rank ? by_work : per_rank);
     } else {
